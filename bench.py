@@ -1,0 +1,526 @@
+"""Benchmark of the RMSNorm + SwiGLU (+ RoPE) hot path on B200; prints one JSON line.
+
+Default workload: a Llama-3-8B-shaped norm/activation stack, bf16,
+32 layers x (2 RMSNorm h4096 + SwiGLU i14336), forward then backward, 16384 tokens per GPU
+(4 x 4096), data-parallel over N GPUs with one packed all-reduce of the 64 RMSNorm weight
+gradients (fp32, NCCL) per step. Every layer has its own inputs (x for both norms, gate,
+up, and the upstream gradients), all larger than L2, so no L2 flush is needed.
+
+Numbers reported (rank 0 prints, other ranks stay silent):
+* ``value``: tokens/s of the whole job = N x 16384 / (max over ranks of the CUDA-event
+  time of one step), inputs resident in HBM, kernels called through the C ABI.
+* ``e2e``: the same metric through the public API (``picotron_b200.kernels``, torch ops
+  with autograd), with each step's inputs copied from pinned host memory and the reduced
+  weight gradients read back to the host inside the timed region.
+* ``roofline``: the dominant kernel (SwiGLU backward) -- algorithmic bytes per launch /
+  its mean CUDA-event duration inside the timed region, against MEASURED_PEAKS.json.
+* ``cpu_baseline``: the reference's PyTorch CPU path (the oracle's "eager" form) on a
+  bounded sample of the same workload, rank 0 at N=1 only.
+
+``--impl reference`` times only the reference's CPU path (rank 0; other ranks exit 0).
+
+Run: ``python bench.py [--gpus N --steps K --warmup W]``; for N>1 under torchrun.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "RMSNorm+SwiGLU fwd+bwd tokens/s & HBM GB/s (bf16, h4096/i14336) at 1–8 B200"
+HIDDEN, INTER = 4096, 14336
+EPS = 1e-5
+BF16 = 2
+
+
+# --------------------------------------------------------------------------- helpers --
+
+
+def measured_peaks() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def dram_traffic_per_launch(kernel: str, tokens: int) -> float | None:
+    """Per-launch DRAM bytes of ``kernel`` from the committed ncu summary, scaled to
+    ``tokens`` rows (the traffic of these kernels grows in proportion to the rows)."""
+
+    path = ROOT / "profiles" / "traffic.json"
+    try:
+        entry = json.loads(path.read_text())[kernel]
+        return float(entry["dram_bytes_per_launch"]) * tokens / float(entry["tokens"])
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuids: list[str]) -> None:
+        self.uuids = {u.lower().replace("gpu-", "") for u in uuids}
+        self.proc = None
+        self.out_path = None
+
+    def __enter__(self):
+        try:
+            self.out_path = f"/tmp/pt_clocks_{os.getpid()}.csv"
+            self.fh = open(self.out_path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        if self.proc is None or self.out_path is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, sm_max, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in Path(self.out_path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            uuid = parts[0].lower().replace("gpu-", "")
+            if self.uuids and uuid not in self.uuids:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                sm_max.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        try:
+            os.unlink(self.out_path)
+        except OSError:
+            pass
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(sm_max),
+                "power_w_max": max(power) if power else None, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def init_distributed(gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != gpus:
+        raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}; launch N>1 under torchrun")
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int, device) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- CPU reference path --
+
+
+def cpu_reference_layer(tokens: int, seed: int = 0):
+    """One layer of the stack on the reference's PyTorch CPU path (the oracle's eager
+    form: the reference's own forward and backward arithmetic), bf16 like the GPU run."""
+
+    from oracle import picotron_oracle as po
+
+    g = torch.Generator().manual_seed(seed)
+    xs = [torch.randn(tokens, HIDDEN, generator=g).bfloat16() for _ in range(2)]
+    dys = [torch.randn(tokens, HIDDEN, generator=g).bfloat16() for _ in range(2)]
+    ws = [(1 + 0.02 * torch.randn(HIDDEN, generator=g)) for _ in range(2)]
+    gate = (torch.randn(tokens, INTER, generator=g) * 2).bfloat16()
+    up = (torch.randn(tokens, INTER, generator=g) * 2).bfloat16()
+    dout = torch.randn(tokens, INTER, generator=g).bfloat16()
+
+    def run():
+        for x, w in zip(xs, ws):
+            po.rms_norm_forward(x, w, EPS, "eager")
+        po.swiglu_forward(gate, up, "eager")
+        po.swiglu_backward(gate, up, dout, "eager")
+        for x, w, dy in zip(xs, ws, dys):
+            po.rms_norm_backward(x, w, dy, EPS, "eager")
+
+    return run
+
+
+def cpu_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
+def time_cpu_reference(tokens: int, steps: int, warmup: int, layers: int) -> dict:
+    cores = cpu_cores()
+    torch.set_num_threads(cores)
+    run = cpu_reference_layer(tokens)
+    for _ in range(warmup):
+        run()
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    per_layer = statistics.median(times)
+    value = tokens / (per_layer * layers)
+    return {
+        "value": value,
+        "unit": "tokens/s",
+        "cores": cores,
+        "kind": "port",
+        "sample": (f"1 of {layers} layers (2 RMSNorm + SwiGLU fwd+bwd, bf16) at {tokens} tokens, "
+                   f"median of {steps} after {warmup} warm-up; tokens/s = tokens / (median "
+                   f"layer time x {layers})"),
+        "seconds_per_layer": per_layer,
+    }
+
+
+# ----------------------------------------------------------------------- GPU stack --
+
+
+class Stack:
+    """Device-resident inputs of the config-5 stack and its step through the C ABI."""
+
+    def __init__(self, layers: int, tokens: int, device: torch.device, seed: int) -> None:
+        from picotron_b200 import _capi
+        from picotron_b200.dist import DWeightBucket
+
+        self.capi = _capi
+        self.lib = _capi.library()
+        self.layers, self.tokens, self.device = layers, tokens, device
+        gen = torch.Generator(device=device).manual_seed(seed)
+        bf = torch.bfloat16
+        self.x = torch.randn((layers, 2, tokens, HIDDEN), generator=gen, device=device, dtype=bf)
+        self.dy = torch.randn((layers, 2, tokens, HIDDEN), generator=gen, device=device, dtype=bf)
+        self.gate = torch.randn((layers, tokens, INTER), generator=gen, device=device, dtype=bf)
+        self.gate.mul_(2)
+        self.up = torch.randn((layers, tokens, INTER), generator=gen, device=device, dtype=bf)
+        self.up.mul_(2)
+        self.dout = torch.randn((layers, tokens, INTER), generator=gen, device=device, dtype=bf)
+        self.w = 1 + 0.02 * torch.randn((layers, 2, HIDDEN), generator=gen, device=device)
+        # outputs are write-only here; their consumers (GEMMs) are outside this path
+        self.y = torch.empty((tokens, HIDDEN), device=device, dtype=bf)
+        self.dx = torch.empty((tokens, HIDDEN), device=device, dtype=bf)
+        self.act = torch.empty((tokens, INTER), device=device, dtype=bf)
+        self.dg = torch.empty((tokens, INTER), device=device, dtype=bf)
+        self.du = torch.empty((tokens, INTER), device=device, dtype=bf)
+        self.bucket = DWeightBucket([HIDDEN] * (2 * layers), device)
+        self.num_partials = _capi.rmsnorm_bwd_num_partials(tokens, HIDDEN, _capi.PT_BFLOAT16,
+                                                           _capi.PT_FLOAT32)
+        self.partials = torch.empty((self.num_partials, HIDDEN), device=device,
+                                    dtype=torch.float32)
+        self.launches_per_step = layers * 8
+
+    # algorithmic bytes (each input read once, each output written once)
+    def bytes_per_step(self) -> int:
+        t = self.tokens
+        rms = 2 * t * HIDDEN * BF16 + 3 * t * HIDDEN * BF16          # fwd + bwd
+        swi = 3 * t * INTER * BF16 + 5 * t * INTER * BF16
+        return self.layers * (2 * rms + swi)
+
+    def _check(self, status: int, name: str) -> None:
+        if status != 0:
+            raise RuntimeError(f"{name}: {self.capi.last_error()}")
+
+    def step(self, stream: int, world: int, swiglu_bwd_events: list | None = None) -> None:
+        lib, L, T = self.lib, self.layers, self.tokens
+        f32, b16 = self.capi.PT_FLOAT32, self.capi.PT_BFLOAT16
+        y, act = self.y.data_ptr(), self.act.data_ptr()
+        for l in range(L):
+            for k in range(2):
+                self._check(lib.pt_rmsnorm_fwd(self.x[l, k].data_ptr(), HIDDEN,
+                                               self.w[l, k].data_ptr(), y, HIDDEN, None, T,
+                                               HIDDEN, b16, f32, EPS, stream), "rms fwd")
+            self._check(lib.pt_swiglu_fwd(self.gate[l].data_ptr(), self.up[l].data_ptr(), act,
+                                          T * INTER, b16, stream), "swiglu fwd")
+        part, P = self.partials.data_ptr(), self.num_partials
+        for l in reversed(range(L)):
+            if swiglu_bwd_events is not None:
+                start, end = swiglu_bwd_events[l]
+                start.record()
+            self._check(lib.pt_swiglu_bwd(self.dout[l].data_ptr(), self.gate[l].data_ptr(),
+                                          self.up[l].data_ptr(), self.dg.data_ptr(),
+                                          self.du.data_ptr(), T * INTER, b16, stream),
+                        "swiglu bwd")
+            if swiglu_bwd_events is not None:
+                end.record()
+            for k in (1, 0):
+                self._check(lib.pt_rmsnorm_bwd(self.dy[l, k].data_ptr(), HIDDEN,
+                                               self.x[l, k].data_ptr(), HIDDEN,
+                                               self.w[l, k].data_ptr(), None, self.dx.data_ptr(),
+                                               HIDDEN, part, P, T, HIDDEN, b16, f32, EPS, stream),
+                            "rms bwd")
+                self._check(lib.pt_rmsnorm_dw_reduce(part, P, HIDDEN,
+                                                     self.bucket.slot(2 * l + k).data_ptr(), f32,
+                                                     stream), "dw reduce")
+        self.bucket.all_reduce()
+
+
+def e2e_run(stack: Stack, steps: int, warmup: int, world: int) -> dict:
+    """The stack through the public API with host inputs (see the module docstring)."""
+
+    from picotron_b200.kernels import triton_rms_norm, triton_swiglu
+
+    dev = stack.device
+    T = stack.tokens
+    pin = dict(
+        x=torch.empty((2, T, HIDDEN), dtype=torch.bfloat16).pin_memory(),
+        dy=torch.empty((2, T, HIDDEN), dtype=torch.bfloat16).pin_memory(),
+        gate=torch.empty((T, INTER), dtype=torch.bfloat16).pin_memory(),
+        up=torch.empty((T, INTER), dtype=torch.bfloat16).pin_memory(),
+        dout=torch.empty((T, INTER), dtype=torch.bfloat16).pin_memory(),
+    )
+    # Host copies of layer 0's inputs; every layer's device buffers are refilled from them.
+    pin["x"].copy_(stack.x[0])
+    pin["dy"].copy_(stack.dy[0])
+    pin["gate"].copy_(stack.gate[0])
+    pin["up"].copy_(stack.up[0])
+    pin["dout"].copy_(stack.dout[0])
+    weights = [torch.nn.Parameter(stack.w[l, k].clone()) for l in range(stack.layers)
+               for k in range(2)]
+    result_host = torch.empty(stack.bucket.buffer.numel(), dtype=torch.float32).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in pin.values()) * stack.layers
+    d2h = result_host.numel() * 4
+
+    def one_step():
+        for w in weights:
+            w.grad = None
+        for l in range(stack.layers):
+            stack.x[l].copy_(pin["x"], non_blocking=True)
+            stack.dy[l].copy_(pin["dy"], non_blocking=True)
+            stack.gate[l].copy_(pin["gate"], non_blocking=True)
+            stack.up[l].copy_(pin["up"], non_blocking=True)
+            stack.dout[l].copy_(pin["dout"], non_blocking=True)
+            xa = stack.x[l, 0].detach().requires_grad_(True)
+            xm = stack.x[l, 1].detach().requires_grad_(True)
+            g = stack.gate[l].detach().requires_grad_(True)
+            u = stack.up[l].detach().requires_grad_(True)
+            ya = triton_rms_norm(xa, weights[2 * l], EPS)
+            ym = triton_rms_norm(xm, weights[2 * l + 1], EPS)
+            out = triton_swiglu(g, u)
+            torch.autograd.backward([out, ym, ya],
+                                    [stack.dout[l], stack.dy[l, 1], stack.dy[l, 0]])
+        torch.cat([w.grad for w in weights], out=stack.bucket.buffer)
+        stack.bucket.all_reduce()
+        result_host.copy_(stack.bucket.buffer)  # synchronous read of the step's result
+
+    for _ in range(warmup):
+        one_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        one_step()
+    end.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world, dev) / steps
+    return {"value": world * T / (ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": ms, "steps": steps,
+            "path": "picotron_b200.kernels.triton_rms_norm / triton_swiglu (torch ops + autograd)"}
+
+
+# ------------------------------------------------------------------------------ main --
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--tokens", type=int, default=16384, help="tokens per GPU")
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-tokens", type=int, default=2048)
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("note: warm-up raised to the minimum of 3 steps", file=sys.stderr)
+        args.warmup = 3
+
+    config = {
+        "workload": "llama3-8b norm/act stack (BASELINE config 5)",
+        "layers": args.layers,
+        "tokens_per_gpu": args.tokens,
+        "hidden": HIDDEN,
+        "intermediate": INTER,
+        "global_batch": 4 * args.gpus * args.tokens // 16384,
+        "seq_len": 4096,
+        "parallelism": f"dp{args.gpus}",
+        "eps": EPS,
+        "weight_dtype": "float32",
+        "l2": "no flush: every layer has its own inputs, each larger than the 126 MB L2",
+    }
+
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return
+        ref = time_cpu_reference(args.cpu_tokens, args.steps, args.warmup, args.layers)
+        line = {
+            "metric": METRIC, "impl": "reference", "value": ref["value"], "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ref["seconds_per_layer"] * args.layers * 1e3 * 16384 / args.cpu_tokens,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) inputs of the BASELINE shapes)",
+            "config": config,
+            "cpu_baseline": {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": ref["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+        return
+
+    world, rank, local = init_distributed(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    import picotron_b200  # noqa: F401  (loads the library; fails loudly if it is missing)
+    from picotron_b200 import _capi
+
+    status, major, minor, sms = _capi.probe(local)
+    if status != 0:
+        raise SystemExit(f"device rejected: {_capi.last_error()}")
+
+    stack = Stack(args.layers, args.tokens, device, seed=1234 + rank)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        stack.step(stream, world)
+    torch.cuda.synchronize()
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.layers * args.steps)]
+    uuids = []
+    for i in range(torch.cuda.device_count()):
+        try:
+            uuids.append(str(torch.cuda.get_device_properties(i).uuid))
+        except Exception:
+            pass
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(uuids if rank == 0 else []) as clocks:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for s in range(args.steps):
+            stack.step(stream, world, ev[s * args.layers:(s + 1) * args.layers])
+        end.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    elapsed = start.elapsed_time(end)
+    ms = max_over_ranks(elapsed, world, device) / args.steps
+    swiglu_ms = statistics.fmean(a.elapsed_time(b) for a, b in ev)
+    swiglu_ms = max_over_ranks(swiglu_ms, world, device)
+
+    peak, peak_kind = measured_peaks()
+    bytes_step = stack.bytes_per_step()
+    swiglu_bytes = 5 * args.tokens * INTER * BF16
+    achieved = swiglu_bytes / (swiglu_ms / 1e3) / 1e9
+    traffic = dram_traffic_per_launch("swiglu_bwd", args.tokens)
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = e2e_run(stack, max(1, args.e2e_steps), 1, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        ref = time_cpu_reference(args.cpu_tokens, 3, 1, args.layers)
+        cpu = {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": world * args.tokens / (ms / 1e3),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) inputs of the BASELINE shapes, on device)",
+            "config": config,
+            "hbm_gbs_per_gpu": bytes_step / (ms / 1e3) / 1e9,
+            "hbm_frac_per_gpu": bytes_step / (ms / 1e3) / 1e9 / peak,
+            "roofline": {
+                "kernel": "swiglu_bwd_vec (SwiGLU backward)",
+                "bound": "hbm",
+                "achieved": achieved,
+                "peak": peak,
+                "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
+                "unit": "GB/s",
+                "frac": achieved / peak,
+                "traffic": traffic,
+                "algorithmic_bytes_per_launch": swiglu_bytes,
+                "mean_launch_us": swiglu_ms * 1e3,
+            },
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": stack.launches_per_step * args.steps,
+            "clocks": clocks.summary() if rank == 0 else None,
+        }
+        print(json.dumps(line), flush=True)
+
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,174 @@
+/*
+ * picotron_b200.h -- C ABI of the B200 (sm_100a) RMSNorm / SwiGLU / RoPE hot path.
+ *
+ * This is the drop-in boundary for picotron's `model.triton_kernels.{rmsnorm,swiglu,rope}`
+ * kernels. Every entry point takes plain device pointers, element counts, strides (in
+ * elements, not bytes), dtype codes and a CUDA stream passed as `void*` (a cudaStream_t;
+ * NULL means the legacy default stream). No entry point allocates device memory except
+ * where a comment says so; outputs are written into caller-owned buffers, inputs are
+ * read-only. Calls are re-entrant: the library keeps no mutable state shared between
+ * calls other than a per-device, write-once cache of device properties and the
+ * thread-local error string returned by pt_last_error().
+ *
+ * Every function returns a pt_status. On failure nothing has been launched and
+ * pt_last_error() describes the cause on the calling thread. All pointers must be
+ * device (or managed) memory of the CUDA device that is current on the calling thread;
+ * the library checks this before it launches anything.
+ *
+ * Reference interfaces replaced (paths inside the picotron project):
+ *   src/picotron/nn/triton_kernels/rmsnorm.py  -- triton_rms_norm, _RMSNormAutogradFunction
+ *   src/picotron/nn/triton_kernels/swiglu.py   -- triton_swiglu, _SwiGLUAutogradFunction
+ *   src/picotron/nn/triton_kernels/rope.py     -- triton_apply_rotary_embedding
+ *   src/picotron/nn/rope.py                    -- apply_rotary_embedding (eager fwd + autograd bwd)
+ *   src/picotron/utils/hardware.py             -- detect_triton_support (capability probe)
+ */
+#ifndef PICOTRON_B200_H
+#define PICOTRON_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Exported symbols; the library is built with hidden default visibility. */
+#if defined(__GNUC__)
+#define PT_API __attribute__((visibility("default")))
+#else
+#define PT_API
+#endif
+
+#define PT_ABI_VERSION 1
+
+/* Status codes returned by every entry point. */
+enum pt_status {
+    PT_OK = 0,
+    PT_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, bad enum value */
+    PT_ERR_UNSUPPORTED_DTYPE = 2, /* dtype code or dtype combination not built */
+    PT_ERR_SHAPE = 3,             /* sizes or strides that the op cannot accept */
+    PT_ERR_DEVICE = 4,            /* no device, wrong device, pointer not on the current device */
+    PT_ERR_CUDA = 5               /* a CUDA runtime call or a kernel launch failed */
+};
+
+/* Element types. Values are stable across ABI versions. */
+enum pt_dtype {
+    PT_FLOAT32 = 0,
+    PT_FLOAT16 = 1,
+    PT_BFLOAT16 = 2
+};
+
+/* RoPE pair layouts. INTERLEAVED rotates (x[2i], x[2i+1]) and is the layout of the
+ * reference (src/picotron/nn/rope.py:42-51, triton_kernels/rope.py:40-49).
+ * ROTATE_HALF rotates (x[i], x[i + D/2]) (the Llama/HF convention). */
+enum pt_rope_layout {
+    PT_ROPE_INTERLEAVED = 0,
+    PT_ROPE_ROTATE_HALF = 1
+};
+
+/* ABI version the library was built with (PT_ABI_VERSION). No reference counterpart. */
+PT_API int pt_abi_version(void);
+
+/* Thread-local, NUL-terminated description of the last failure on this thread.
+ * Replaces the message of the Triton*Unavailable exceptions
+ * (rmsnorm.py:19, swiglu.py:20, triton_kernels/rope.py:19). */
+PT_API const char* pt_last_error(void);
+
+/* Capability probe. Fills the compute capability and SM count of `device` and returns
+ * PT_OK only when the device can run this library's sm_100a code (compute capability
+ * 10.0). Replaces detect_triton_support (src/picotron/utils/hardware.py:93-108), whose
+ * check was "triton installed and capability >= 7.0". Any output pointer may be NULL. */
+PT_API int pt_probe(int device, int* cc_major, int* cc_minor, int* sm_count);
+
+/* ---------------------------------------------------------------- RMSNorm -------- */
+
+/* y[r, :] = x[r, :] * rsqrt(mean(x[r, :]^2) + eps) * weight, fp32 accumulation, y in the
+ * x dtype. rstd (optional, may be NULL) receives rsqrt(mean(x^2) + eps) per row in fp32.
+ * Row strides are in elements; the last dimension must be contiguous.
+ * Supported (x_dtype, w_dtype): (f32,f32) (f16,f16) (f16,f32) (bf16,bf16) (bf16,f32).
+ * Replaces _rmsnorm_kernel + _run_triton_forward + _inverse_rms
+ * (src/picotron/nn/triton_kernels/rmsnorm.py:25-84, 49-53). */
+PT_API int pt_rmsnorm_fwd(const void* x, int64_t x_row_stride,
+                   const void* weight,
+                   void* y, int64_t y_row_stride,
+                   float* rstd,
+                   int64_t rows, int64_t hidden,
+                   int x_dtype, int w_dtype, float eps,
+                   void* stream);
+
+/* Number of dweight partial rows that pt_rmsnorm_bwd should be given for this problem on
+ * the current device: one per resident CTA of the backward kernel. Any positive value
+ * is valid; the result of the backward depends only on (inputs, num_partials). */
+PT_API int pt_rmsnorm_bwd_num_partials(int64_t rows, int64_t hidden, int x_dtype, int w_dtype,
+                                int* num_partials);
+
+/* Backward of pt_rmsnorm_fwd. With r = rsqrt(mean(x^2) + eps) (read from `rstd` when it
+ * is not NULL, else recomputed from x) and g = dy * weight:
+ *   dx = r * (g - x * r^2 * mean(g * x))              (written in the x dtype)
+ *   dw_partials[p, :] = sum over the rows that CTA p owns of dy * x * r   (fp32)
+ * dw_partials is caller-owned scratch of num_partials * hidden floats; every element is
+ * written. Reduce it with pt_rmsnorm_dw_reduce. Deterministic for fixed num_partials.
+ * dy has the x dtype. Replaces _RMSNormAutogradFunction.backward
+ * (src/picotron/nn/triton_kernels/rmsnorm.py:109-134). */
+PT_API int pt_rmsnorm_bwd(const void* dy, int64_t dy_row_stride,
+                   const void* x, int64_t x_row_stride,
+                   const void* weight,
+                   const float* rstd,
+                   void* dx, int64_t dx_row_stride,
+                   float* dw_partials, int num_partials,
+                   int64_t rows, int64_t hidden,
+                   int x_dtype, int w_dtype, float eps,
+                   void* stream);
+
+/* dw[c] = sum over p < num_partials of dw_partials[p, c], fp32, in a summation order that
+ * depends only on num_partials (so the result is bit-reproducible), stored in dw_dtype
+ * (the weight dtype). Second, deterministic stage of the dweight reduction; replaces
+ * `.reshape(-1, H).sum(dim=0)` at rmsnorm.py:125-127. */
+PT_API int pt_rmsnorm_dw_reduce(const float* dw_partials, int num_partials, int64_t hidden,
+                         void* dw, int dw_dtype, void* stream);
+
+/* ----------------------------------------------------------------- SwiGLU -------- */
+
+/* out = gate * sigmoid(gate) * up over n contiguous elements, fp32 math, one rounding.
+ * All three tensors share `dtype`. Replaces _swiglu_kernel + _run_triton_forward
+ * (src/picotron/nn/triton_kernels/swiglu.py:26-53). */
+PT_API int pt_swiglu_fwd(const void* gate, const void* up, void* out, int64_t n, int dtype,
+                  void* stream);
+
+/* s = sigmoid(gate); dgate = dout * up * s * (1 + gate * (1 - s)); dup = dout * gate * s.
+ * fp32 math with sigmoid recomputed from gate, one rounding per output. Replaces
+ * _SwiGLUAutogradFunction.backward (src/picotron/nn/triton_kernels/swiglu.py:71-81). */
+PT_API int pt_swiglu_bwd(const void* dout, const void* gate, const void* up,
+                  void* dgate, void* dup, int64_t n, int dtype, void* stream);
+
+/* ------------------------------------------------------------------- RoPE -------- */
+
+/* Rotary embedding of a 4-D tensor with logical shape sizes = [B, H, S, D] (the
+ * reference's (batch, heads, sequence, head_dim) view) and arbitrary strides in elements
+ * for x and out (stride of D must be 1). The angle of pair i at sequence index s comes
+ * from the tables cosine/sine of logical shape [S, D/2] with row stride table_row_stride
+ * (elements) and contiguous columns, in table_dtype. INTERLEAVED:
+ *   out[2i]   = x[2i] * c - x[2i+1] * s,   out[2i+1] = x[2i] * s + x[2i+1] * c
+ * fp32 math, one rounding. Replaces apply_rotary_embedding (src/picotron/nn/rope.py:35-51)
+ * and triton_apply_rotary_embedding (src/picotron/nn/triton_kernels/rope.py:52-91). */
+PT_API int pt_rope_fwd(const void* x, const int64_t x_strides[4],
+                void* out, const int64_t out_strides[4],
+                const int64_t sizes[4],
+                const void* cosine, const void* sine, int64_t table_row_stride,
+                int layout, int dtype, int table_dtype, void* stream);
+
+/* Backward of pt_rope_fwd: the rotation by -angle (the transpose of the forward
+ * rotation), i.e. for INTERLEAVED
+ *   dx[2i] = dy[2i] * c + dy[2i+1] * s,   dx[2i+1] = -dy[2i] * s + dy[2i+1] * c.
+ * Replaces the autograd backward of apply_rotary_embedding (src/picotron/nn/rope.py:35-51),
+ * which the reference's Triton kernel does not provide (triton_kernels/rope.py:60-61). */
+PT_API int pt_rope_bwd(const void* dy, const int64_t dy_strides[4],
+                void* dx, const int64_t dx_strides[4],
+                const int64_t sizes[4],
+                const void* cosine, const void* sine, int64_t table_row_stride,
+                int layout, int dtype, int table_dtype, void* stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* PICOTRON_B200_H */

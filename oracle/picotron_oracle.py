@@ -1,0 +1,177 @@
+"""CPU restatement of picotron's RMSNorm / SwiGLU / RoPE arithmetic (test oracle).
+
+TEST INFRASTRUCTURE ONLY -- see ``oracle/__init__.py``. Every function cites the
+reference file and lines whose arithmetic it restates. ``mode="eager"`` reproduces the
+reference's PyTorch CPU computation op for op (same dtypes, same operation order);
+``mode="exact"`` evaluates the same formula in float64 and returns float64.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+from torch.nn import functional as F
+
+MODES = ("eager", "exact")
+
+
+def _check_mode(mode: str) -> None:
+    if mode not in MODES:
+        raise ValueError(f"mode must be one of {MODES}, got {mode!r}")
+
+
+# --------------------------------------------------------------------------- RMSNorm --
+
+
+def rms_norm_forward(x: Tensor, weight: Tensor, eps: float, mode: str = "eager"):
+    """Returns (y, inverse_rms).
+
+    eager: ``_inverse_rms`` + ``_pytorch_forward`` (picotron
+    src/picotron/nn/triton_kernels/rmsnorm.py:49-60): r = rsqrt(mean(x.float()^2) + eps),
+    y = (x.float() * r * w.float()).to(x.dtype). The fused Triton forward (:25-46) computes
+    the same fp32 expression and stores in the x dtype.
+    exact: the same formula in float64, unrounded.
+    """
+
+    _check_mode(mode)
+    if mode == "exact":
+        xd, wd = x.double(), weight.double()
+        inv = torch.rsqrt(xd.square().mean(dim=-1, keepdim=True) + eps)
+        return xd * inv * wd, inv
+    values = x.float()
+    inv = torch.rsqrt(values.square().mean(dim=-1, keepdim=True) + eps)
+    return (values * inv * weight.float()).to(dtype=x.dtype), inv
+
+
+def rms_norm_backward(x: Tensor, weight: Tensor, dy: Tensor, eps: float, mode: str = "eager"):
+    """Returns (dx, dweight).
+
+    eager: ``_RMSNormAutogradFunction.backward`` (rmsnorm.py:109-134):
+      g = dy * w; dot_mean = mean(g * x); dx = r * (g - x * r^2 * dot_mean);
+      dw = sum_rows(dy * x * r); all fp32, dx cast to x dtype, dw to w dtype.
+    exact: the same in float64, unrounded.
+    """
+
+    _check_mode(mode)
+    if mode == "exact":
+        xd, wd, gd = x.double(), weight.double(), dy.double()
+        inv = torch.rsqrt(xd.square().mean(dim=-1, keepdim=True) + eps)
+        g = gd * wd
+        dot_mean = (g * xd).mean(dim=-1, keepdim=True)
+        dx = inv * (g - xd * inv.square() * dot_mean)
+        dw = (gd * xd * inv).reshape(-1, weight.numel()).sum(dim=0)
+        return dx, dw
+    inverse_rms = torch.rsqrt(x.float().square().mean(dim=-1, keepdim=True) + eps)
+    x32, w32, g32 = x.float(), weight.float(), dy.float()
+    weighted_grad = g32 * w32
+    dot_mean = (weighted_grad * x32).mean(dim=-1, keepdim=True)
+    dx = inverse_rms * (weighted_grad - x32 * inverse_rms.square() * dot_mean)
+    dw = (g32 * x32 * inverse_rms).reshape(-1, weight.numel()).sum(dim=0)
+    return dx.to(dtype=x.dtype), dw.to(dtype=weight.dtype)
+
+
+# ---------------------------------------------------------------------------- SwiGLU --
+
+
+def swiglu_forward(gate: Tensor, up: Tensor, mode: str = "eager") -> Tensor:
+    """eager: ``F.silu(gate) * up`` in the input dtype (picotron
+    src/picotron/nn/triton_kernels/swiglu.py:63-64 and nn/feedforward.py:42), i.e. SiLU
+    rounded to the input dtype, then the product rounded again. (The Triton forward,
+    swiglu.py:26-41, instead rounds once from fp32: g * (1/(1+exp(-g))) * u.)
+    exact: g * sigmoid(g) * u in float64, unrounded."""
+
+    _check_mode(mode)
+    if mode == "exact":
+        g, u = gate.double(), up.double()
+        return g * torch.sigmoid(g) * u
+    return F.silu(gate) * up
+
+
+def swiglu_backward(gate: Tensor, up: Tensor, dout: Tensor, mode: str = "eager"):
+    """Returns (dgate, dup).
+
+    eager: ``_SwiGLUAutogradFunction.backward`` (swiglu.py:71-81) op for op in the input
+    dtype: s = sigmoid(g); silu = g * s; dsilu = s * (1 + g * (1 - s));
+    dgate = dout * up * dsilu; dup = dout * silu.
+    exact: the same in float64, unrounded."""
+
+    _check_mode(mode)
+    if mode == "exact":
+        gate, up, dout = gate.double(), up.double(), dout.double()
+    sigmoid_gate = torch.sigmoid(gate)
+    silu_gate = gate * sigmoid_gate
+    silu_derivative = sigmoid_gate * (1 + gate * (1 - sigmoid_gate))
+    return dout * up * silu_derivative, dout * silu_gate
+
+
+# ------------------------------------------------------------------------------ RoPE --
+
+
+def rotary_cos_sin(sequence_length: int, head_dim: int, theta: float, dtype: torch.dtype):
+    """``rotary_cos_sin`` (picotron src/picotron/nn/rope.py:13-32) on CPU:
+    inv = 1 / theta^(arange(0, D, 2) / D) in fp32; angles = outer(arange(S), inv);
+    returns (cos(angles), sin(angles)) cast to ``dtype``."""
+
+    if head_dim % 2 != 0:
+        raise ValueError("RoPE requires an even attention head dimension.")
+    inverse_frequencies = 1.0 / (
+        theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim)
+    )
+    positions = torch.arange(sequence_length, dtype=torch.float32)
+    angles = torch.outer(positions, inverse_frequencies)
+    return angles.cos().to(dtype=dtype), angles.sin().to(dtype=dtype)
+
+
+def _rope_eager(states: Tensor, cosine: Tensor, sine: Tensor) -> Tensor:
+    # apply_rotary_embedding, picotron src/picotron/nn/rope.py:35-51.
+    cosine = cosine.unsqueeze(0).unsqueeze(0)
+    sine = sine.unsqueeze(0).unsqueeze(0)
+    even_states = states[..., 0::2]
+    odd_states = states[..., 1::2]
+    rotated = torch.stack(
+        (even_states * cosine - odd_states * sine, even_states * sine + odd_states * cosine),
+        dim=-1,
+    )
+    return rotated.flatten(start_dim=-2)
+
+
+def rope_forward(states: Tensor, cosine: Tensor, sine: Tensor, mode: str = "eager",
+                 layout: str = "interleaved") -> Tensor:
+    """Interleaved layout (the reference's): out[2i] = e*c - o*s, out[2i+1] = e*s + o*c,
+    with (e, o) = (x[2i], x[2i+1]) and c, s = tables[seq, i] (nn/rope.py:42-51).
+    eager evaluates in the states/table dtype op for op; exact in float64.
+
+    layout="rotate_half" has no counterpart in the reference: it is the Llama/HF
+    convention out[i] = x[i]*c[i] - x[i+D/2]*s[i], out[i+D/2] = x[i+D/2]*c[i] + x[i]*s[i],
+    restated here for the labelled rotate-half variant of the kernels."""
+
+    _check_mode(mode)
+    if mode == "exact":
+        states, cosine, sine = states.double(), cosine.double(), sine.double()
+    if layout == "interleaved":
+        return _rope_eager(states, cosine, sine)
+    if layout != "rotate_half":
+        raise ValueError(f"unknown layout {layout!r}")
+    half = states.size(-1) // 2
+    c, s = cosine[None, None], sine[None, None]
+    x1, x2 = states[..., :half], states[..., half:]
+    return torch.cat((x1 * c - x2 * s, x2 * c + x1 * s), dim=-1)
+
+
+def rope_backward(dout: Tensor, cosine: Tensor, sine: Tensor, mode: str = "eager",
+                  layout: str = "interleaved") -> Tensor:
+    """Gradient of ``rope_forward`` with respect to the states.
+
+    eager: what the reference's training path computes, i.e. torch autograd through the
+    eager ``apply_rotary_embedding`` graph (nn/rope.py:35-51) in the states dtype.
+    exact: the transposed rotation in float64: d_e = dy_e*c + dy_o*s,
+    d_o = -dy_e*s + dy_o*c (interleaved), unrounded."""
+
+    _check_mode(mode)
+    if mode == "eager":
+        x = torch.zeros(dout.shape, dtype=dout.dtype, requires_grad=True)
+        with torch.enable_grad():
+            out = rope_forward(x, cosine, sine, "eager", layout)
+            (grad,) = torch.autograd.grad(out, x, dout)
+        return grad
+    return rope_forward(dout, cosine, -sine, "exact", layout)

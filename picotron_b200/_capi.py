@@ -1,0 +1,221 @@
+"""ctypes binding of ``libpicotron_b200.so`` (declared in ``include/picotron_b200.h``).
+
+This module is the only place Python touches the C ABI. Each wrapper takes raw device
+addresses (ints), sizes, dtype codes and a stream handle (int), calls the C entry point
+and raises :class:`PtError` (or the subclass the caller asks for) on a non-zero status
+with the library's thread-local message. There is no fallback: if the shared library is
+missing or does not load, :func:`library` raises :class:`LibraryUnavailable`.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIBRARY_PATH = Path(__file__).resolve().with_name("libpicotron_b200.so")
+
+# enum pt_status
+PT_OK = 0
+PT_ERR_INVALID_ARGUMENT = 1
+PT_ERR_UNSUPPORTED_DTYPE = 2
+PT_ERR_SHAPE = 3
+PT_ERR_DEVICE = 4
+PT_ERR_CUDA = 5
+
+STATUS_NAMES = {
+    PT_OK: "PT_OK",
+    PT_ERR_INVALID_ARGUMENT: "PT_ERR_INVALID_ARGUMENT",
+    PT_ERR_UNSUPPORTED_DTYPE: "PT_ERR_UNSUPPORTED_DTYPE",
+    PT_ERR_SHAPE: "PT_ERR_SHAPE",
+    PT_ERR_DEVICE: "PT_ERR_DEVICE",
+    PT_ERR_CUDA: "PT_ERR_CUDA",
+}
+
+# enum pt_dtype
+PT_FLOAT32 = 0
+PT_FLOAT16 = 1
+PT_BFLOAT16 = 2
+
+# enum pt_rope_layout
+PT_ROPE_INTERLEAVED = 0
+PT_ROPE_ROTATE_HALF = 1
+
+ABI_VERSION = 1
+
+_c_i64 = ctypes.c_int64
+_c_int = ctypes.c_int
+_c_float = ctypes.c_float
+_c_ptr = ctypes.c_void_p
+_c_i64_4 = ctypes.c_int64 * 4
+
+# name -> (restype, argtypes). Mirrors include/picotron_b200.h one to one; the CPU test
+# suite checks that every function declared there is exported and listed here.
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "pt_abi_version": (_c_int, []),
+    "pt_last_error": (ctypes.c_char_p, []),
+    "pt_probe": (_c_int, [_c_int, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int),
+                          ctypes.POINTER(_c_int)]),
+    "pt_rmsnorm_fwd": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64, _c_ptr, _c_i64, _c_i64,
+                                _c_int, _c_int, _c_float, _c_ptr]),
+    "pt_rmsnorm_bwd_num_partials": (_c_int, [_c_i64, _c_i64, _c_int, _c_int,
+                                             ctypes.POINTER(_c_int)]),
+    "pt_rmsnorm_bwd": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_i64,
+                                _c_ptr, _c_int, _c_i64, _c_i64, _c_int, _c_int, _c_float,
+                                _c_ptr]),
+    "pt_rmsnorm_dw_reduce": (_c_int, [_c_ptr, _c_int, _c_i64, _c_ptr, _c_int, _c_ptr]),
+    "pt_swiglu_fwd": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_i64, _c_int, _c_ptr]),
+    "pt_swiglu_bwd": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_int, _c_ptr]),
+    "pt_rope_fwd": (_c_int, [_c_ptr, _c_i64_4, _c_ptr, _c_i64_4, _c_i64_4, _c_ptr, _c_ptr,
+                             _c_i64, _c_int, _c_int, _c_int, _c_ptr]),
+    "pt_rope_bwd": (_c_int, [_c_ptr, _c_i64_4, _c_ptr, _c_i64_4, _c_i64_4, _c_ptr, _c_ptr,
+                             _c_i64, _c_int, _c_int, _c_int, _c_ptr]),
+}
+
+
+class LibraryUnavailable(RuntimeError):
+    """The compiled library is missing or cannot be loaded."""
+
+
+class PtError(RuntimeError):
+    """A C-ABI call returned a non-zero pt_status."""
+
+    def __init__(self, function: str, status: int, message: str) -> None:
+        self.function = function
+        self.status = status
+        self.message = message
+        name = STATUS_NAMES.get(status, str(status))
+        super().__init__(f"{function} failed with {name}: {message}")
+
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def library() -> ctypes.CDLL:
+    """Load (once) and return the C-ABI library; raise if it is not built or loadable."""
+
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIBRARY_PATH.is_file():
+            raise LibraryUnavailable(
+                f"{LIBRARY_PATH.name} is not built; run `python -m picotron_b200.build`"
+            )
+        try:
+            lib = ctypes.CDLL(str(LIBRARY_PATH))
+        except OSError as error:
+            raise LibraryUnavailable(f"cannot load {LIBRARY_PATH}: {error}") from error
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        version = lib.pt_abi_version()
+        if version != ABI_VERSION:
+            raise LibraryUnavailable(
+                f"{LIBRARY_PATH.name} has ABI version {version}; expected {ABI_VERSION}"
+            )
+        _lib = lib
+        return lib
+
+
+def is_available() -> bool:
+    """True when the library loads (says nothing about a GPU being present)."""
+
+    try:
+        library()
+    except LibraryUnavailable:
+        return False
+    return True
+
+
+def last_error() -> str:
+    return library().pt_last_error().decode("utf-8", "replace")
+
+
+def _check(function: str, status: int, error_type: type[Exception] | None) -> None:
+    if status == PT_OK:
+        return
+    message = last_error()
+    error = PtError(function, status, message)
+    if error_type is not None and error_type is not PtError:
+        raise error_type(str(error)) from error
+    raise error
+
+
+def _i64x4(values) -> ctypes.Array:
+    return _c_i64_4(*[int(v) for v in values])
+
+
+# ------------------------------------------------------------------------- wrappers --
+
+
+def probe(device: int) -> tuple[int, int, int, int]:
+    """Return (status, cc_major, cc_minor, sm_count) for ``device`` without raising."""
+
+    major, minor, sms = _c_int(0), _c_int(0), _c_int(0)
+    status = library().pt_probe(int(device), ctypes.byref(major), ctypes.byref(minor),
+                                ctypes.byref(sms))
+    return status, major.value, minor.value, sms.value
+
+
+def rmsnorm_fwd(x: int, x_row_stride: int, weight: int, y: int, y_row_stride: int,
+                rstd: int | None, rows: int, hidden: int, x_dtype: int, w_dtype: int,
+                eps: float, stream: int, error_type: type[Exception] | None = None) -> None:
+    status = library().pt_rmsnorm_fwd(x, x_row_stride, weight, y, y_row_stride, rstd, rows,
+                                      hidden, x_dtype, w_dtype, eps, stream)
+    _check("pt_rmsnorm_fwd", status, error_type)
+
+
+def rmsnorm_bwd_num_partials(rows: int, hidden: int, x_dtype: int, w_dtype: int,
+                             error_type: type[Exception] | None = None) -> int:
+    out = _c_int(0)
+    status = library().pt_rmsnorm_bwd_num_partials(rows, hidden, x_dtype, w_dtype,
+                                                   ctypes.byref(out))
+    _check("pt_rmsnorm_bwd_num_partials", status, error_type)
+    return out.value
+
+
+def rmsnorm_bwd(dy: int, dy_row_stride: int, x: int, x_row_stride: int, weight: int,
+                rstd: int | None, dx: int, dx_row_stride: int, dw_partials: int,
+                num_partials: int, rows: int, hidden: int, x_dtype: int, w_dtype: int,
+                eps: float, stream: int, error_type: type[Exception] | None = None) -> None:
+    status = library().pt_rmsnorm_bwd(dy, dy_row_stride, x, x_row_stride, weight, rstd, dx,
+                                      dx_row_stride, dw_partials, num_partials, rows, hidden,
+                                      x_dtype, w_dtype, eps, stream)
+    _check("pt_rmsnorm_bwd", status, error_type)
+
+
+def rmsnorm_dw_reduce(dw_partials: int, num_partials: int, hidden: int, dw: int,
+                      dw_dtype: int, stream: int,
+                      error_type: type[Exception] | None = None) -> None:
+    status = library().pt_rmsnorm_dw_reduce(dw_partials, num_partials, hidden, dw, dw_dtype,
+                                            stream)
+    _check("pt_rmsnorm_dw_reduce", status, error_type)
+
+
+def swiglu_fwd(gate: int, up: int, out: int, n: int, dtype: int, stream: int,
+               error_type: type[Exception] | None = None) -> None:
+    status = library().pt_swiglu_fwd(gate, up, out, n, dtype, stream)
+    _check("pt_swiglu_fwd", status, error_type)
+
+
+def swiglu_bwd(dout: int, gate: int, up: int, dgate: int, dup: int, n: int, dtype: int,
+               stream: int, error_type: type[Exception] | None = None) -> None:
+    status = library().pt_swiglu_bwd(dout, gate, up, dgate, dup, n, dtype, stream)
+    _check("pt_swiglu_bwd", status, error_type)
+
+
+def rope(direction: str, x: int, x_strides, out: int, out_strides, sizes, cosine: int,
+         sine: int, table_row_stride: int, layout: int, dtype: int, table_dtype: int,
+         stream: int, error_type: type[Exception] | None = None) -> None:
+    """``direction`` is "fwd" (rotate by +angle) or "bwd" (rotate by -angle)."""
+
+    name = {"fwd": "pt_rope_fwd", "bwd": "pt_rope_bwd"}[direction]
+    fn = getattr(library(), name)
+    status = fn(x, _i64x4(x_strides), out, _i64x4(out_strides), _i64x4(sizes), cosine, sine,
+                table_row_stride, layout, dtype, table_dtype, stream)
+    _check(name, status, error_type)

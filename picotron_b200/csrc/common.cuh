@@ -1,0 +1,189 @@
+// Shared device and host helpers for the picotron B200 kernels (sm_100a only).
+//
+// Device side: element-type traits, 16-byte vector loads/stores with explicit cache
+// hints, bf16/fp16 <-> fp32 conversion of packed vectors, warp reductions.
+// Host side: status/error plumbing for the C ABI (pt_last_error is thread-local),
+// pointer validation, and a write-once per-device cache of the SM count.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/picotron_b200.h"
+
+namespace pt {
+
+// ------------------------------------------------------------------ element types --
+
+template <typename T> struct ElemTraits;
+template <> struct ElemTraits<float> {
+  static constexpr int kDtype = PT_FLOAT32;
+};
+template <> struct ElemTraits<__half> {
+  static constexpr int kDtype = PT_FLOAT16;
+};
+template <> struct ElemTraits<__nv_bfloat16> {
+  static constexpr int kDtype = PT_BFLOAT16;
+};
+
+__device__ __forceinline__ float to_float(float v) { return v; }
+__device__ __forceinline__ float to_float(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T> __device__ __forceinline__ T from_float(float v);
+template <> __device__ __forceinline__ float from_float<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_float<__half>(float v) {
+  return __float2half_rn(v);
+}
+template <> __device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// Number of T elements in one 16-byte vector.
+template <typename T> struct Vec16 {
+  static constexpr int N = 16 / sizeof(T);
+};
+
+// ------------------------------------------------------------- 16-byte memory ops --
+// Loads of inputs that are never written by the same kernel use the non-coherent path
+// without L1 allocation: every byte is used once per kernel, so L1 residency only
+// evicts the rows that are still being reduced.
+
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 r;
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+      : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+      : "l"(p));
+  return r;
+}
+
+// Plain cached 16-byte load (weights, tables: reused by every row).
+__device__ __forceinline__ uint4 ld_cached(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+// 8-byte cached load (half of a 16-byte vector of a 16-bit table).
+__device__ __forceinline__ uint2 ld_cached8(const void* p) {
+  return __ldg(reinterpret_cast<const uint2*>(p));
+}
+
+// Streaming store (evict-first): outputs are consumed by a later kernel, not this one.
+__device__ __forceinline__ void st_stream(void* p, const uint4& v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};"
+               :
+               : "l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Unpack a 16-byte vector of T into fp32 values.
+template <typename T> __device__ __forceinline__ void unpack(const uint4& v, float* f);
+
+template <> __device__ __forceinline__ void unpack<float>(const uint4& v, float* f) {
+  f[0] = __uint_as_float(v.x);
+  f[1] = __uint_as_float(v.y);
+  f[2] = __uint_as_float(v.z);
+  f[3] = __uint_as_float(v.w);
+}
+
+template <> __device__ __forceinline__ void unpack<__nv_bfloat16>(const uint4& v, float* f) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    // bf16 -> fp32 is exact: the bf16 bits are the high half of the fp32 bits.
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+template <> __device__ __forceinline__ void unpack<__half>(const uint4& v, float* f) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+    float2 t = __half22float2(h);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+// Pack fp32 values into a 16-byte vector of T with round-to-nearest-even.
+template <typename T> __device__ __forceinline__ uint4 pack(const float* f);
+
+template <> __device__ __forceinline__ uint4 pack<float>(const float* f) {
+  return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                    __float_as_uint(f[3]));
+}
+
+template <> __device__ __forceinline__ uint4 pack<__nv_bfloat16>(const float* f) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <> __device__ __forceinline__ uint4 pack<__half>(const float* f) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Load `n` consecutive elements of TW starting at p as fp32 (n is a compile-time
+// multiple of the TW vector width; p is 16-byte aligned).
+template <typename TW, int N>
+__device__ __forceinline__ void load_row_f32(const TW* p, float* f) {
+  constexpr int V = Vec16<TW>::N;
+  static_assert(N % V == 0, "N must be a multiple of the vector width");
+#pragma unroll
+  for (int i = 0; i < N / V; ++i) unpack<TW>(ld_cached(p + i * V), f + i * V);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// fp32 logistic function, sigma(g) = 1 / (1 + e^-g). Uses the CUDA fast exponential;
+// its relative error is far below the fp32 tolerances used by this library. For
+// g << 0 the exponential overflows to +inf and the quotient is exactly 0.
+__device__ __forceinline__ float sigmoid_f32(float g) { return 1.0f / (1.0f + __expf(-g)); }
+
+// ----------------------------------------------------------------------- host side --
+
+// Records `msg` as this thread's last error and returns `status`.
+int set_error(int status, const char* fmt, ...);
+// Clears this thread's last error and returns PT_OK.
+int ok();
+
+// Checks that `p` is device or managed memory of the current device.
+int check_device_ptr(const void* p, const char* name);
+
+// Current device and its SM count (cached per device, written once).
+int current_device_info(int* device, int* sm_count);
+
+// Maps the result of a kernel launch to a status.
+int check_launch(const char* what);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int dtype_size(int dtype) {
+  switch (dtype) {
+    case PT_FLOAT32: return 4;
+    case PT_FLOAT16: return 2;
+    case PT_BFLOAT16: return 2;
+    default: return 0;
+  }
+}
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+}  // namespace pt

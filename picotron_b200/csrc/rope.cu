@@ -1,0 +1,290 @@
+// Rotary position embedding (RoPE) forward/backward for sm_100a.
+//
+// Math follows src/picotron/nn/rope.py:35-51 (interleaved pairs) of the reference:
+//   out[2i]   = x[2i] * cos[s, i] - x[2i+1] * sin[s, i]
+//   out[2i+1] = x[2i] * sin[s, i] + x[2i+1] * cos[s, i]
+// The backward is the rotation by -angle (sin -> -sin), which is what autograd computes
+// for that forward. ROTATE_HALF pairs x[i] with x[i + D/2] instead.
+//
+// Layout: a logical [B, H, S, D] tensor with arbitrary strides in elements (stride of D
+// = 1), e.g. the reference's transposed view of [B, S, H, D] projections
+// (src/picotron/nn/attention.py:196-203), read in place with no .contiguous() copy. The
+// host orders the three outer dimensions by decreasing input stride so consecutive
+// threads walk memory in address order. Each thread rotates 16-byte vectors (U per
+// iteration, loads first); the angle tables are tiny and stay in L1/L2.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace pt {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 2;
+
+struct RopeGeom {
+  uint32_t n0, n1, n2;          // outer sizes, outermost first (memory order of x)
+  int64_t xs0, xs1, xs2;         // x strides of those dims (elements)
+  int64_t os0, os1, os2;         // out strides
+  int s_axis;                    // which of the three is the sequence axis
+  uint32_t vpr;                  // vectors handled per row (per (b, h, s))
+  int64_t table_stride;          // elements between table rows
+  float sign;                    // +1 forward, -1 backward
+};
+
+// Loads N consecutive table entries of TT starting at p as fp32. The host guarantees
+// that p is aligned to min(16, N * sizeof(TT)) bytes on the vector path.
+template <typename TT, int N>
+__device__ __forceinline__ void load_table(const TT* p, float* f) {
+  constexpr int kBytes = N * (int)sizeof(TT);
+  if constexpr (kBytes >= 16) {
+    constexpr int V = Vec16<TT>::N;
+#pragma unroll
+    for (int i = 0; i < N / V; ++i) unpack<TT>(ld_cached(p + i * V), f + i * V);
+  } else if constexpr (kBytes == 8) {
+    uint2 r = ld_cached8(p);
+    if constexpr (sizeof(TT) == 4) {
+      f[0] = __uint_as_float(r.x);
+      f[1] = __uint_as_float(r.y);
+    } else {
+      uint4 q = make_uint4(r.x, r.y, 0, 0);
+      float t[8];
+      unpack<TT>(q, t);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) f[i] = t[i];
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) f[i] = to_float(p[i]);
+  }
+}
+
+template <typename T, typename TT, bool kRotateHalf>
+__global__ void __launch_bounds__(kThreads)
+rope_vec(const T* __restrict__ x, T* __restrict__ out, const TT* __restrict__ cosine,
+         const TT* __restrict__ sine, RopeGeom g, int half_dim, uint32_t total) {
+  constexpr int V = Vec16<T>::N;
+  const uint32_t step = gridDim.x * blockDim.x * kUnroll;
+  for (uint32_t i0 = blockIdx.x * blockDim.x * kUnroll + threadIdx.x; i0 < total; i0 += step) {
+    uint4 a[kUnroll], b[kUnroll];
+    int64_t xo[kUnroll], oo[kUnroll];
+    uint32_t srow[kUnroll], vj[kUnroll];
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k) {
+      const uint32_t idx = i0 + k * blockDim.x;
+      if (idx >= total) continue;
+      vj[k] = idx % g.vpr;
+      uint32_t row = idx / g.vpr;
+      const uint32_t i2 = row % g.n2;
+      row /= g.n2;
+      const uint32_t i1 = row % g.n1;
+      const uint32_t i0_ = row / g.n1;
+      srow[k] = g.s_axis == 0 ? i0_ : (g.s_axis == 1 ? i1 : i2);
+      xo[k] = (int64_t)i0_ * g.xs0 + (int64_t)i1 * g.xs1 + (int64_t)i2 * g.xs2;
+      oo[k] = (int64_t)i0_ * g.os0 + (int64_t)i1 * g.os1 + (int64_t)i2 * g.os2;
+      const int64_t d0 = (int64_t)vj[k] * V;
+      a[k] = ld_stream(x + xo[k] + d0);
+      if (kRotateHalf) b[k] = ld_stream(x + xo[k] + d0 + half_dim);
+    }
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k) {
+      const uint32_t idx = i0 + k * blockDim.x;
+      if (idx >= total) continue;
+      const int64_t d0 = (int64_t)vj[k] * V;
+      if (!kRotateHalf) {
+        // V elements = V/2 interleaved pairs starting at pair index d0/2.
+        float c[V / 2], s[V / 2], f[V];
+        const int64_t t = (int64_t)srow[k] * g.table_stride + d0 / 2;
+        load_table<TT, V / 2>(cosine + t, c);
+        load_table<TT, V / 2>(sine + t, s);
+        unpack<T>(a[k], f);
+#pragma unroll
+        for (int p = 0; p < V / 2; ++p) {
+          const float e = f[2 * p], o = f[2 * p + 1], sn = g.sign * s[p];
+          f[2 * p] = e * c[p] - o * sn;
+          f[2 * p + 1] = e * sn + o * c[p];
+        }
+        st_stream(out + oo[k] + d0, pack<T>(f));
+      } else {
+        // First-half vector at d0 pairs with the second-half vector at d0 + D/2.
+        float c[V], s[V], f1[V], f2[V];
+        const int64_t t = (int64_t)srow[k] * g.table_stride + d0;
+        load_table<TT, V>(cosine + t, c);
+        load_table<TT, V>(sine + t, s);
+        unpack<T>(a[k], f1);
+        unpack<T>(b[k], f2);
+#pragma unroll
+        for (int p = 0; p < V; ++p) {
+          const float e = f1[p], o = f2[p], sn = g.sign * s[p];
+          f1[p] = e * c[p] - o * sn;
+          f2[p] = o * c[p] + e * sn;
+        }
+        st_stream(out + oo[k] + d0, pack<T>(f1));
+        st_stream(out + oo[k] + d0 + half_dim, pack<T>(f2));
+      }
+    }
+  }
+}
+
+// Scalar path: one pair per thread iteration, any even D, any strides and alignment.
+template <typename T, typename TT, bool kRotateHalf>
+__global__ void __launch_bounds__(kThreads)
+rope_scalar(const T* __restrict__ x, T* __restrict__ out, const TT* __restrict__ cosine,
+            const TT* __restrict__ sine, RopeGeom g, int half_dim, int64_t total) {
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t pi = idx % half_dim;  // pair index within the head
+    int64_t row = idx / half_dim;
+    const int64_t i2 = row % g.n2;
+    row /= g.n2;
+    const int64_t i1 = row % g.n1;
+    const int64_t i0 = row / g.n1;
+    const int64_t s_idx = g.s_axis == 0 ? i0 : (g.s_axis == 1 ? i1 : i2);
+    const int64_t xo = i0 * g.xs0 + i1 * g.xs1 + i2 * g.xs2;
+    const int64_t oo = i0 * g.os0 + i1 * g.os1 + i2 * g.os2;
+    const int64_t de = kRotateHalf ? pi : 2 * pi;
+    const int64_t dod = kRotateHalf ? pi + half_dim : 2 * pi + 1;
+    const float c = to_float(cosine[s_idx * g.table_stride + pi]);
+    const float sn = g.sign * to_float(sine[s_idx * g.table_stride + pi]);
+    const float e = to_float(x[xo + de]), o = to_float(x[xo + dod]);
+    out[oo + de] = from_float<T>(e * c - o * sn);
+    out[oo + dod] = from_float<T>(e * sn + o * c);
+  }
+}
+
+template <typename T, typename TT>
+int rope_impl(const void* x_, const int64_t* xst, void* out_, const int64_t* ost,
+              const int64_t* sizes, const void* cos_, const void* sin_, int64_t tstride,
+              int layout, float sign, cudaStream_t stream, const char* what) {
+  const T* x = static_cast<const T*>(x_);
+  T* out = static_cast<T*>(out_);
+  const TT* cosine = static_cast<const TT*>(cos_);
+  const TT* sine = static_cast<const TT*>(sin_);
+  int dev = 0, sms = 0;
+  if (int st = current_device_info(&dev, &sms)) return st;
+
+  // Order the outer dims (B, H, S) by decreasing x stride; remember where S went.
+  int order[3] = {0, 1, 2};
+  std::stable_sort(order, order + 3, [&](int a, int b) { return xst[a] > xst[b]; });
+  RopeGeom g;
+  g.n0 = (uint32_t)sizes[order[0]];
+  g.n1 = (uint32_t)sizes[order[1]];
+  g.n2 = (uint32_t)sizes[order[2]];
+  g.xs0 = xst[order[0]]; g.xs1 = xst[order[1]]; g.xs2 = xst[order[2]];
+  g.os0 = ost[order[0]]; g.os1 = ost[order[1]]; g.os2 = ost[order[2]];
+  g.s_axis = order[0] == 2 ? 0 : (order[1] == 2 ? 1 : 2);
+  g.table_stride = tstride;
+  g.sign = sign;
+  const int64_t D = sizes[3];
+  const int half = (int)(D / 2);
+  const bool rh = layout == PT_ROPE_ROTATE_HALF;
+  const int64_t rows = sizes[0] * sizes[1] * sizes[2];
+
+  constexpr int V = Vec16<T>::N;
+  // Vector path: whole vectors per row, 16-byte aligned rows, table runs aligned to
+  // their own size.
+  const int64_t span = rh ? half : D;  // elements covered by the vectors of one row
+  const int tbytes = (rh ? V : V / 2) * (int)sizeof(TT);
+  const int talign = tbytes >= 16 ? 16 : tbytes;
+  bool vec = span % V == 0 && aligned16(x) && aligned16(out);
+  for (int i = 0; i < 3 && vec; ++i)
+    vec = (xst[i] * (int64_t)sizeof(T)) % 16 == 0 && (ost[i] * (int64_t)sizeof(T)) % 16 == 0;
+  vec = vec && (reinterpret_cast<uintptr_t>(cosine) % talign == 0) &&
+        (reinterpret_cast<uintptr_t>(sine) % talign == 0) &&
+        ((tstride * (int64_t)sizeof(TT)) % talign == 0);
+  const int64_t total_vec = rows * (span / V);
+  if (vec && total_vec < (int64_t)UINT32_MAX - (int64_t)kThreads * kUnroll * sms * 8) {
+    g.vpr = (uint32_t)(span / V);
+    const int64_t blocks = (total_vec + (int64_t)kThreads * kUnroll - 1) / (kThreads * kUnroll);
+    const int64_t cap = (int64_t)sms * (2048 / kThreads);
+    const int grid = (int)std::max<int64_t>(1, std::min(blocks, cap));
+    if (rh)
+      rope_vec<T, TT, true><<<grid, kThreads, 0, stream>>>(x, out, cosine, sine, g, half,
+                                                            (uint32_t)total_vec);
+    else
+      rope_vec<T, TT, false><<<grid, kThreads, 0, stream>>>(x, out, cosine, sine, g, half,
+                                                             (uint32_t)total_vec);
+  } else {
+    g.vpr = 0;
+    const int64_t total = rows * half;
+    const int64_t blocks = (total + kThreads - 1) / kThreads;
+    const int64_t cap = (int64_t)sms * (2048 / kThreads);
+    const int grid = (int)std::max<int64_t>(1, std::min(blocks, cap));
+    if (rh)
+      rope_scalar<T, TT, true><<<grid, kThreads, 0, stream>>>(x, out, cosine, sine, g, half, total);
+    else
+      rope_scalar<T, TT, false><<<grid, kThreads, 0, stream>>>(x, out, cosine, sine, g, half,
+                                                               total);
+  }
+  return check_launch(what);
+}
+
+int rope_entry(const void* x, const int64_t* xst, void* out, const int64_t* ost,
+               const int64_t* sizes, const void* cosine, const void* sine, int64_t tstride,
+               int layout, int dtype, int table_dtype, float sign, void* stream,
+               const char* what) {
+  if (xst == nullptr || ost == nullptr || sizes == nullptr)
+    return set_error(PT_ERR_INVALID_ARGUMENT, "%s: strides/sizes must not be NULL", what);
+  if (layout != PT_ROPE_INTERLEAVED && layout != PT_ROPE_ROTATE_HALF)
+    return set_error(PT_ERR_INVALID_ARGUMENT, "%s: unknown layout %d", what, layout);
+  for (int i = 0; i < 4; ++i)
+    if (sizes[i] < 0)
+      return set_error(PT_ERR_SHAPE, "%s: sizes[%d] = %lld < 0", what, i, (long long)sizes[i]);
+  const int64_t D = sizes[3];
+  if (D <= 0 || D % 2 != 0)
+    return set_error(PT_ERR_SHAPE, "%s: head_dim must be even and positive (got %lld)", what,
+                     (long long)D);
+  if (xst[3] != 1 || ost[3] != 1)
+    return set_error(PT_ERR_SHAPE, "%s: the head_dim stride must be 1", what);
+  for (int i = 0; i < 3; ++i)
+    if (xst[i] < 0 || ost[i] < 0 || sizes[i] > (int64_t)UINT32_MAX)
+      return set_error(PT_ERR_SHAPE, "%s: negative stride or outer size too large", what);
+  if (tstride < D / 2)
+    return set_error(PT_ERR_SHAPE, "%s: table_row_stride (%lld) < head_dim/2 (%lld)", what,
+                     (long long)tstride, (long long)(D / 2));
+  if (dtype_size(dtype) == 0 || dtype_size(table_dtype) == 0)
+    return set_error(PT_ERR_UNSUPPORTED_DTYPE, "%s: unsupported dtype (%d, table %d)", what, dtype,
+                     table_dtype);
+  const int64_t rows = sizes[0] * sizes[1] * sizes[2];
+  if (rows == 0) return ok();
+  if (int st = check_device_ptr(x, "x")) return st;
+  if (int st = check_device_ptr(out, "out")) return st;
+  if (int st = check_device_ptr(cosine, "cosine")) return st;
+  if (int st = check_device_ptr(sine, "sine")) return st;
+  cudaStream_t s = as_stream(stream);
+#define PT_ROPE_CASE(DT, T, TDT, TT)                                                        \
+  if (dtype == DT && table_dtype == TDT)                                                    \
+    return rope_impl<T, TT>(x, xst, out, ost, sizes, cosine, sine, tstride, layout, sign, s, \
+                            what);
+  PT_ROPE_CASE(PT_BFLOAT16, __nv_bfloat16, PT_BFLOAT16, __nv_bfloat16)
+  PT_ROPE_CASE(PT_BFLOAT16, __nv_bfloat16, PT_FLOAT32, float)
+  PT_ROPE_CASE(PT_FLOAT16, __half, PT_FLOAT16, __half)
+  PT_ROPE_CASE(PT_FLOAT16, __half, PT_FLOAT32, float)
+  PT_ROPE_CASE(PT_FLOAT32, float, PT_FLOAT32, float)
+#undef PT_ROPE_CASE
+  return set_error(PT_ERR_UNSUPPORTED_DTYPE,
+                   "%s: unsupported (dtype, table_dtype) = (%d, %d); the table must have the "
+                   "states dtype or float32",
+                   what, dtype, table_dtype);
+}
+
+}  // namespace
+}  // namespace pt
+
+extern "C" {
+
+int pt_rope_fwd(const void* x, const int64_t x_strides[4], void* out, const int64_t out_strides[4],
+                const int64_t sizes[4], const void* cosine, const void* sine,
+                int64_t table_row_stride, int layout, int dtype, int table_dtype, void* stream) {
+  return pt::rope_entry(x, x_strides, out, out_strides, sizes, cosine, sine, table_row_stride,
+                        layout, dtype, table_dtype, 1.0f, stream, "pt_rope_fwd");
+}
+
+int pt_rope_bwd(const void* dy, const int64_t dy_strides[4], void* dx, const int64_t dx_strides[4],
+                const int64_t sizes[4], const void* cosine, const void* sine,
+                int64_t table_row_stride, int layout, int dtype, int table_dtype, void* stream) {
+  return pt::rope_entry(dy, dy_strides, dx, dx_strides, sizes, cosine, sine, table_row_stride,
+                        layout, dtype, table_dtype, -1.0f, stream, "pt_rope_bwd");
+}
+
+}  // extern "C"

@@ -1,0 +1,363 @@
+"""PyTorch custom ops (``torch.ops.picotron_b200.*``) over the C ABI, with autograd.
+
+Ops, each an opaque ``torch.library.custom_op`` with a fake (meta) implementation so
+``torch.compile`` can trace around it, and an autograd formula that calls the matching
+backward op:
+
+* ``rms_norm(x, weight, eps) -> y``                  (reference rmsnorm.py:87-160)
+* ``rms_norm_backward(dy, x, weight, eps) -> (dx, dweight)``
+* ``swiglu(gate, up) -> out``                        (reference swiglu.py:56-101)
+* ``swiglu_backward(dout, gate, up) -> (dgate, dup)``
+* ``rope(x, cosine, sine, layout) -> out``           (reference nn/rope.py:35-51)
+* ``rope_backward(dy, cosine, sine, layout) -> dx``
+
+All ops run only on CUDA tensors of a compute-capability-10.0 device and launch on the
+current stream of the tensors' device. Any failure raises the reference's exception
+type for that op (``Triton*Unavailable``); there is no fallback path.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from picotron_b200 import _capi
+from picotron_b200.errors import (
+    TritonRMSNormUnavailable,
+    TritonRoPEUnavailable,
+    TritonSwiGLUUnavailable,
+)
+
+DTYPE_CODES = {
+    torch.float32: _capi.PT_FLOAT32,
+    torch.float16: _capi.PT_FLOAT16,
+    torch.bfloat16: _capi.PT_BFLOAT16,
+}
+
+# RMSNorm (x dtype, weight dtype) pairs built into the library. Other weight dtypes are
+# converted to float32 (an exact widening for fp16/bf16) before the call.
+_RMSNORM_PAIRS = {
+    (torch.float32, torch.float32),
+    (torch.float16, torch.float16),
+    (torch.float16, torch.float32),
+    (torch.bfloat16, torch.bfloat16),
+    (torch.bfloat16, torch.float32),
+}
+
+LAYOUTS = {"interleaved": _capi.PT_ROPE_INTERLEAVED, "rotate_half": _capi.PT_ROPE_ROTATE_HALF}
+
+_device_ok: dict[int, bool] = {}
+
+
+def check_device(device: torch.device, error_type: type[Exception]) -> None:
+    """Raise ``error_type`` unless ``device`` is a CUDA device this library can run on."""
+
+    if device.type != "cuda":
+        raise error_type(f"requires CUDA tensors; got a tensor on {device}")
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    ok = _device_ok.get(index)
+    if ok is None:
+        try:
+            status, major, minor, _ = _capi.probe(index)
+        except _capi.LibraryUnavailable as error:
+            raise error_type(str(error)) from error
+        ok = status == _capi.PT_OK
+        _device_ok[index] = ok
+        if not ok:
+            raise error_type(_capi.last_error())
+    if not ok:
+        raise error_type(f"cuda:{index} is not a compute capability 10.0 (sm_100a) device")
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+class _OnDevice:
+    """Make ``device`` current for the duration of a C-ABI call (no-op when it is)."""
+
+    __slots__ = ("index", "previous")
+
+    def __init__(self, device: torch.device) -> None:
+        self.index = device.index
+        self.previous = None
+
+    def __enter__(self) -> None:
+        current = torch.cuda.current_device()
+        if self.index is not None and current != self.index:
+            self.previous = current
+            torch.cuda.set_device(self.index)
+
+    def __exit__(self, *exc) -> None:
+        if self.previous is not None:
+            torch.cuda.set_device(self.previous)
+
+
+def _dtype_code(t: Tensor, error_type: type[Exception]) -> int:
+    code = DTYPE_CODES.get(t.dtype)
+    if code is None:
+        raise error_type(f"unsupported dtype {t.dtype}; expected float32, float16 or bfloat16")
+    return code
+
+
+def _as_rows(t: Tensor, hidden: int) -> Tensor:
+    """View ``t`` as [rows, hidden] with contiguous columns, copying only if impossible."""
+
+    if t.dim() >= 1 and t.stride(-1) == 1:
+        try:
+            view = t.view(-1, hidden)
+            if view.stride(1) == 1:
+                return view
+        except RuntimeError:
+            pass
+    return t.contiguous().view(-1, hidden)
+
+
+# --------------------------------------------------------------------------- RMSNorm --
+
+
+def _rms_weight(x: Tensor, weight: Tensor) -> Tensor:
+    if (x.dtype, weight.dtype) in _RMSNORM_PAIRS:
+        return weight.contiguous()
+    return weight.to(torch.float32).contiguous()
+
+
+def _validate_rms(x: Tensor, weight: Tensor) -> int:
+    check_device(x.device, TritonRMSNormUnavailable)
+    if weight.device != x.device:
+        raise TritonRMSNormUnavailable("RMSNorm weight must be on the input's device.")
+    if x.dim() < 1 or weight.dim() != 1 or x.size(-1) != weight.numel():
+        raise TritonRMSNormUnavailable("RMSNorm hidden size must match the weight size.")
+    _dtype_code(x, TritonRMSNormUnavailable)
+    _dtype_code(weight, TritonRMSNormUnavailable)
+    return x.size(-1)
+
+
+@torch.library.custom_op("picotron_b200::rms_norm", mutates_args=())
+def rms_norm(x: Tensor, weight: Tensor, eps: float) -> Tensor:
+    hidden = _validate_rms(x, weight)
+    w = _rms_weight(x, weight)
+    y = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    if x.numel() == 0:
+        return y
+    xr = _as_rows(x, hidden)
+    yr = y.view(-1, hidden)
+    with _OnDevice(x.device):
+        _capi.rmsnorm_fwd(
+            xr.data_ptr(), xr.stride(0), w.data_ptr(), yr.data_ptr(), yr.stride(0), None,
+            xr.size(0), hidden, DTYPE_CODES[x.dtype], DTYPE_CODES[w.dtype], float(eps),
+            _stream(x.device), TritonRMSNormUnavailable,
+        )
+    return y
+
+
+@rms_norm.register_fake
+def _rms_norm_fake(x: Tensor, weight: Tensor, eps: float) -> Tensor:
+    return torch.empty(x.shape, dtype=x.dtype, device=x.device)
+
+
+@torch.library.custom_op("picotron_b200::rms_norm_backward", mutates_args=())
+def rms_norm_backward(dy: Tensor, x: Tensor, weight: Tensor, eps: float) -> tuple[Tensor, Tensor]:
+    hidden = _validate_rms(x, weight)
+    if dy.shape != x.shape:
+        raise TritonRMSNormUnavailable("RMSNorm grad_output must have the input's shape.")
+    if dy.dtype != x.dtype:
+        dy = dy.to(x.dtype)
+    w = _rms_weight(x, weight)
+    dx = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    dw = torch.empty(weight.shape, dtype=weight.dtype, device=x.device)
+    xr = _as_rows(x, hidden)
+    dyr = _as_rows(dy, hidden)
+    dxr = dx.view(-1, hidden)
+    rows = xr.size(0)
+    x_code, w_code = DTYPE_CODES[x.dtype], DTYPE_CODES[w.dtype]
+    with _OnDevice(x.device):
+        stream = _stream(x.device)
+        num_partials = _capi.rmsnorm_bwd_num_partials(rows, hidden, x_code, w_code,
+                                                      TritonRMSNormUnavailable)
+        partials = torch.empty((num_partials, hidden), dtype=torch.float32, device=x.device)
+        _capi.rmsnorm_bwd(
+            dyr.data_ptr(), dyr.stride(0), xr.data_ptr(), xr.stride(0), w.data_ptr(), None,
+            dxr.data_ptr(), dxr.stride(0), partials.data_ptr(), num_partials, rows, hidden,
+            x_code, w_code, float(eps), stream, TritonRMSNormUnavailable,
+        )
+        _capi.rmsnorm_dw_reduce(partials.data_ptr(), num_partials, hidden, dw.data_ptr(),
+                                DTYPE_CODES[dw.dtype], stream, TritonRMSNormUnavailable)
+    return dx, dw
+
+
+@rms_norm_backward.register_fake
+def _rms_norm_backward_fake(dy: Tensor, x: Tensor, weight: Tensor, eps: float):
+    return (torch.empty(x.shape, dtype=x.dtype, device=x.device),
+            torch.empty(weight.shape, dtype=weight.dtype, device=x.device))
+
+
+def _rms_setup(ctx, inputs, output) -> None:
+    x, weight, eps = inputs
+    ctx.save_for_backward(x, weight)
+    ctx.eps = eps
+
+
+def _rms_backward(ctx, grad: Tensor):
+    x, weight = ctx.saved_tensors
+    dx, dw = torch.ops.picotron_b200.rms_norm_backward(grad, x, weight, ctx.eps)
+    return dx, dw, None
+
+
+rms_norm.register_autograd(_rms_backward, setup_context=_rms_setup)
+
+
+# ---------------------------------------------------------------------------- SwiGLU --
+
+
+def _validate_swiglu(gate: Tensor, up: Tensor) -> None:
+    check_device(gate.device, TritonSwiGLUUnavailable)
+    if up.device != gate.device:
+        raise TritonSwiGLUUnavailable("SwiGLU gate and up must be on the same device.")
+    if gate.shape != up.shape or gate.dtype != up.dtype:
+        raise TritonSwiGLUUnavailable("SwiGLU requires gate and up of the same shape and dtype.")
+    _dtype_code(gate, TritonSwiGLUUnavailable)
+
+
+@torch.library.custom_op("picotron_b200::swiglu", mutates_args=())
+def swiglu(gate: Tensor, up: Tensor) -> Tensor:
+    _validate_swiglu(gate, up)
+    g, u = gate.contiguous(), up.contiguous()
+    out = torch.empty(gate.shape, dtype=gate.dtype, device=gate.device)
+    if gate.numel() == 0:
+        return out
+    with _OnDevice(gate.device):
+        _capi.swiglu_fwd(g.data_ptr(), u.data_ptr(), out.data_ptr(), g.numel(),
+                         DTYPE_CODES[g.dtype], _stream(gate.device), TritonSwiGLUUnavailable)
+    return out
+
+
+@swiglu.register_fake
+def _swiglu_fake(gate: Tensor, up: Tensor) -> Tensor:
+    return torch.empty(gate.shape, dtype=gate.dtype, device=gate.device)
+
+
+@torch.library.custom_op("picotron_b200::swiglu_backward", mutates_args=())
+def swiglu_backward(dout: Tensor, gate: Tensor, up: Tensor) -> tuple[Tensor, Tensor]:
+    _validate_swiglu(gate, up)
+    if dout.shape != gate.shape:
+        raise TritonSwiGLUUnavailable("SwiGLU grad_output must have the input's shape.")
+    if dout.dtype != gate.dtype:
+        dout = dout.to(gate.dtype)
+    o, g, u = dout.contiguous(), gate.contiguous(), up.contiguous()
+    dg = torch.empty(gate.shape, dtype=gate.dtype, device=gate.device)
+    du = torch.empty(gate.shape, dtype=gate.dtype, device=gate.device)
+    if gate.numel() == 0:
+        return dg, du
+    with _OnDevice(gate.device):
+        _capi.swiglu_bwd(o.data_ptr(), g.data_ptr(), u.data_ptr(), dg.data_ptr(), du.data_ptr(),
+                         g.numel(), DTYPE_CODES[g.dtype], _stream(gate.device),
+                         TritonSwiGLUUnavailable)
+    return dg, du
+
+
+@swiglu_backward.register_fake
+def _swiglu_backward_fake(dout: Tensor, gate: Tensor, up: Tensor):
+    return (torch.empty(gate.shape, dtype=gate.dtype, device=gate.device),
+            torch.empty(gate.shape, dtype=gate.dtype, device=gate.device))
+
+
+def _swiglu_setup(ctx, inputs, output) -> None:
+    gate, up = inputs
+    ctx.save_for_backward(gate, up)
+
+
+def _swiglu_bwd(ctx, grad: Tensor):
+    gate, up = ctx.saved_tensors
+    dg, du = torch.ops.picotron_b200.swiglu_backward(grad, gate, up)
+    return dg, du
+
+
+swiglu.register_autograd(_swiglu_bwd, setup_context=_swiglu_setup)
+
+
+# ------------------------------------------------------------------------------ RoPE --
+
+
+def _validate_rope(x: Tensor, cosine: Tensor, sine: Tensor, layout: int) -> None:
+    check_device(x.device, TritonRoPEUnavailable)
+    if cosine.device != x.device or sine.device != x.device:
+        raise TritonRoPEUnavailable("RoPE tables must be on the states' device.")
+    if layout not in (_capi.PT_ROPE_INTERLEAVED, _capi.PT_ROPE_ROTATE_HALF):
+        raise TritonRoPEUnavailable(f"unknown RoPE layout {layout}")
+    if (
+        x.dim() != 4
+        or x.size(-1) % 2 != 0
+        or cosine.dim() != 2
+        or cosine.shape != sine.shape
+        or cosine.size(-1) * 2 != x.size(-1)
+        or cosine.size(0) != x.size(-2)
+        or cosine.dtype != sine.dtype
+    ):
+        raise TritonRoPEUnavailable(
+            "RoPE requires states [B, H, S, D] and cosine/sine tables [S, D/2] of one dtype."
+        )
+    _dtype_code(x, TritonRoPEUnavailable)
+    _dtype_code(cosine, TritonRoPEUnavailable)
+
+
+def _rope_launch(direction: str, x: Tensor, cosine: Tensor, sine: Tensor, layout: int) -> Tensor:
+    _validate_rope(x, cosine, sine, layout)
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    if cosine.stride(-1) != 1 or sine.stride(-1) != 1 or cosine.stride(0) != sine.stride(0):
+        cosine, sine = cosine.contiguous(), sine.contiguous()
+    table = cosine if cosine.dtype in (x.dtype, torch.float32) else None
+    if table is None:
+        cosine, sine = cosine.to(torch.float32), sine.to(torch.float32)
+    # Same memory layout as the input when it is dense (e.g. the [B,S,H,D] memory of a
+    # transposed attention view), else contiguous.
+    out = torch.empty_like(x)
+    if out.stride(-1) != 1:
+        out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    if x.numel() == 0:
+        return out
+    with _OnDevice(x.device):
+        _capi.rope(direction, x.data_ptr(), x.stride(), out.data_ptr(), out.stride(),
+                   x.shape, cosine.data_ptr(), sine.data_ptr(), cosine.stride(0), layout,
+                   DTYPE_CODES[x.dtype], DTYPE_CODES[cosine.dtype], _stream(x.device),
+                   TritonRoPEUnavailable)
+    return out
+
+
+@torch.library.custom_op("picotron_b200::rope", mutates_args=())
+def rope(x: Tensor, cosine: Tensor, sine: Tensor, layout: int) -> Tensor:
+    return _rope_launch("fwd", x, cosine, sine, layout)
+
+
+@rope.register_fake
+def _rope_fake(x: Tensor, cosine: Tensor, sine: Tensor, layout: int) -> Tensor:
+    out = torch.empty_like(x)
+    return out if out.stride(-1) == 1 else torch.empty(x.shape, dtype=x.dtype, device=x.device)
+
+
+@torch.library.custom_op("picotron_b200::rope_backward", mutates_args=())
+def rope_backward(dy: Tensor, cosine: Tensor, sine: Tensor, layout: int) -> Tensor:
+    return _rope_launch("bwd", dy, cosine, sine, layout)
+
+
+@rope_backward.register_fake
+def _rope_backward_fake(dy: Tensor, cosine: Tensor, sine: Tensor, layout: int) -> Tensor:
+    out = torch.empty_like(dy)
+    return out if out.stride(-1) == 1 else torch.empty(dy.shape, dtype=dy.dtype, device=dy.device)
+
+
+def _rope_setup(ctx, inputs, output) -> None:
+    x, cosine, sine, layout = inputs
+    ctx.save_for_backward(cosine, sine)
+    ctx.layout = layout
+
+
+def _rope_bwd(ctx, grad: Tensor):
+    cosine, sine = ctx.saved_tensors
+    dx = torch.ops.picotron_b200.rope_backward(grad, cosine, sine, ctx.layout)
+    # The angle tables are constants of the position grid: no gradient flows to them.
+    return dx, None, None, None
+
+
+rope.register_autograd(_rope_bwd, setup_context=_rope_setup)

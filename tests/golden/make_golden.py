@@ -1,0 +1,168 @@
+"""Generate the golden fixtures by running the reference (picotron) itself on CPU.
+
+Run in the build container, where the reference is mounted read-only:
+
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py [--reference-src DIR]
+
+It imports the reference's own hot-path functions
+(``picotron.nn.triton_kernels.rmsnorm.rms_norm_with_pytorch_forward``,
+``picotron.nn.triton_kernels.swiglu.swiglu_with_pytorch_forward``,
+``picotron.nn.rope.rotary_cos_sin`` / ``apply_rotary_embedding``), runs each forward and
+``.backward(dy)`` on seeded inputs, and stores inputs and outputs in ``tests/golden``.
+Inputs are drawn on CPU in float32 from ``torch.Generator().manual_seed(seed)`` and then
+cast, so every consumer sees the same bits. One thread, so CPU reductions are ordered
+the same way on every run. The fixtures are committed; this script is not needed at test
+time and nothing at test time reads the reference.
+"""
+
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import os
+import sys
+from pathlib import Path
+
+import torch
+
+sys.dont_write_bytecode = True
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+import golden_io  # noqa: E402
+
+
+def _gen(seed: int) -> torch.Generator:
+    return torch.Generator().manual_seed(seed)
+
+
+def _rms(ref, x, w, dy, eps):
+    xg = x.clone().requires_grad_(True)
+    wg = w.clone().requires_grad_(True)
+    y = ref.rms_norm_with_pytorch_forward(xg, wg, eps)
+    y.backward(dy)
+    return {"y": y.detach(), "dx": xg.grad, "dw": wg.grad}
+
+
+def _swiglu(ref, g, u, dy):
+    gg = g.clone().requires_grad_(True)
+    ug = u.clone().requires_grad_(True)
+    out = ref.swiglu_with_pytorch_forward(gg, ug)
+    out.backward(dy)
+    return {"out": out.detach(), "dgate": gg.grad, "dup": ug.grad}
+
+
+def _rope(rope_mod, q_phys, theta, dy_phys):
+    """q_phys is [B, S, H, D] memory; the reference sees the [B, H, S, D] transposed view."""
+
+    qg = q_phys.clone().requires_grad_(True)
+    view = qg.transpose(1, 2)
+    cos, sin = rope_mod.rotary_cos_sin(view.size(-2), view.size(-1), theta, device=q_phys.device,
+                                       dtype=q_phys.dtype)
+    out = rope_mod.apply_rotary_embedding(view, cos, sin)
+    out.backward(dy_phys.transpose(1, 2))
+    return {"cos": cos, "sin": sin, "out": out.detach().contiguous(), "dq": qg.grad}
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--reference-src", default=os.environ.get("PICOTRON_REFERENCE_SRC",
+                                                                  "/root/reference/src"))
+    args = parser.parse_args()
+    sys.path.insert(0, args.reference_src)
+    torch.set_num_threads(1)
+    from picotron.nn import rope as rope_mod
+    from picotron.nn.triton_kernels import rmsnorm as rms_ref
+    from picotron.nn.triton_kernels import swiglu as swiglu_ref
+
+    written = []
+
+    # BASELINE config 1, RMSNorm part: fp32 x[128,128], gamma = 1 + 0.1 N(0,1), eps 1e-6.
+    g = _gen(0)
+    x = torch.randn(128, 128, generator=g)
+    w = 1 + 0.1 * torch.randn(128, generator=g)
+    dy = torch.randn(128, 128, generator=g)
+    res = _rms(rms_ref, x, w, dy, 1e-6)
+    written.append(golden_io.save("cfg1_rmsnorm_f32", {"x": x, "w": w, "dy": dy, **res},
+                                  {"eps": 1e-6, "seed": 0}))
+
+    # BASELINE config 1, SwiGLU part: fp32 gate, up [128, 256] ~ N(0,1), dy ~ N(0,1).
+    g = _gen(0)
+    gate = torch.randn(128, 256, generator=g)
+    up = torch.randn(128, 256, generator=g)
+    dy = torch.randn(128, 256, generator=g)
+    res = _swiglu(swiglu_ref, gate, up, dy)
+    written.append(golden_io.save("cfg1_swiglu_f32", {"gate": gate, "up": up, "dy": dy, **res},
+                                  {"seed": 0}))
+
+    # The reference's own RMSNorm test inputs (tests/test_triton_rmsnorm_backward.py:16-21):
+    # torch.manual_seed(23); dy, x [2,3,8], w [8] (signed weights), eps 1e-6.
+    torch.manual_seed(23)
+    dy = torch.randn(2, 3, 8)
+    x = torch.randn(2, 3, 8)
+    w = torch.randn(8)
+    res = _rms(rms_ref, x, w, dy, 1e-6)
+    written.append(golden_io.save("reftest_rmsnorm_f32", {"x": x, "w": w, "dy": dy, **res},
+                                  {"eps": 1e-6, "seed": 23}))
+
+    # The reference's own SwiGLU test inputs (tests/test_triton_swiglu_backward.py:12-15).
+    torch.manual_seed(31)
+    dy = torch.randn(2, 3, 7, dtype=torch.float64)
+    gate = torch.randn(2, 3, 7, dtype=torch.float64)
+    up = torch.randn(2, 3, 7, dtype=torch.float64)
+    res = _swiglu(swiglu_ref, gate, up, dy)
+    written.append(golden_io.save("reftest_swiglu_f64", {"gate": gate, "up": up, "dy": dy, **res},
+                                  {"seed": 31}))
+
+    # BASELINE config 2 shape family, bf16: x[8, 4096] ~ N(0,1), gamma = 1 + 0.02 N(0,1),
+    # eps 1e-5; gamma in bf16 and in fp32 (the module's parameter dtype).
+    g = _gen(0)
+    x = torch.randn(8, 4096, generator=g).to(torch.bfloat16)
+    wf = 1 + 0.02 * torch.randn(4096, generator=g)
+    dy = torch.randn(8, 4096, generator=g).to(torch.bfloat16)
+    res = _rms(rms_ref, x, wf.to(torch.bfloat16), dy, 1e-5)
+    written.append(golden_io.save("rmsnorm_bf16", {"x": x, "w": wf.to(torch.bfloat16), "dy": dy,
+                                                   **res}, {"eps": 1e-5, "seed": 0}))
+    res = _rms(rms_ref, x, wf, dy, 1e-5)
+    written.append(golden_io.save("rmsnorm_bf16_wf32", {"x": x, "w": wf, "dy": dy, **res},
+                                  {"eps": 1e-5, "seed": 0}))
+
+    # BASELINE config 3 family, bf16: gate, up ~ N(0,1) * 2, dy ~ N(0,1), [16, 1024].
+    g = _gen(0)
+    gate = (torch.randn(16, 1024, generator=g) * 2).to(torch.bfloat16)
+    up = (torch.randn(16, 1024, generator=g) * 2).to(torch.bfloat16)
+    dy = torch.randn(16, 1024, generator=g).to(torch.bfloat16)
+    res = _swiglu(swiglu_ref, gate, up, dy)
+    written.append(golden_io.save("swiglu_bf16", {"gate": gate, "up": up, "dy": dy, **res},
+                                  {"seed": 0}))
+
+    # BASELINE config 4 family, bf16: q as [B, S, H, D] = [2, 16, 4, 32] memory, theta 5e5.
+    g = _gen(0)
+    q = torch.randn(2, 16, 4, 32, generator=g).to(torch.bfloat16)
+    dq = torch.randn(2, 16, 4, 32, generator=g).to(torch.bfloat16)
+    res = _rope(rope_mod, q, 500_000.0, dq)
+    written.append(golden_io.save("rope_bf16", {"q": q, "dy": dq, **res},
+                                  {"theta": 500_000.0, "seed": 0}))
+
+    # fp32 RoPE, the reference test's geometry (tests/test_rope.py: head_dim 8, theta 1e4,
+    # 12 positions), with 3 heads and batch 2.
+    g = _gen(1)
+    q = torch.randn(2, 12, 3, 8, generator=g)
+    dq = torch.randn(2, 12, 3, 8, generator=g)
+    res = _rope(rope_mod, q, 10_000.0, dq)
+    written.append(golden_io.save("rope_f32", {"q": q, "dy": dq, **res},
+                                  {"theta": 10_000.0, "seed": 1}))
+
+    manifest = {
+        "generator": "tests/golden/make_golden.py",
+        "torch": torch.__version__,
+        "threads": torch.get_num_threads(),
+        "files": {p.name: hashlib.sha256(p.read_bytes()).hexdigest() for p in written},
+    }
+    (HERE / "MANIFEST.json").write_text(json.dumps(manifest, indent=1) + "\n")
+    for p in written:
+        print(p.name, p.stat().st_size)
+
+
+if __name__ == "__main__":
+    main()

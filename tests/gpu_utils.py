@@ -1,0 +1,92 @@
+"""Helpers for the ``-m gpu`` tests: seeded inputs and direct C-ABI calls on torch buffers.
+
+The wrappers below call the library's C entry points (through ``picotron_b200._capi``)
+with raw device addresses, exactly as a non-Python caller of ``include/picotron_b200.h``
+would; they allocate outputs with torch only for convenience.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from picotron_b200 import _capi
+from picotron_b200.ops import DTYPE_CODES
+
+DEV = torch.device("cuda", 0)
+
+
+def require_gpu() -> None:
+    """GPU tests fail (not skip) when no usable device or library is present."""
+
+    assert torch.cuda.is_available(), "the gpu tests need a CUDA device"
+    status, major, minor, sms = _capi.probe(0)
+    assert status == _capi.PT_OK, f"device 0 rejected by pt_probe: {_capi.last_error()}"
+
+
+def stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def randn(shape, seed: int, dtype=torch.float32, scale: float = 1.0, shift: float = 0.0,
+          device=DEV) -> torch.Tensor:
+    """N(shift, scale^2) drawn on CPU in fp32 from a seeded generator, then cast (so CPU
+    and GPU tests see identical bits)."""
+
+    g = torch.Generator().manual_seed(seed)
+    t = torch.randn(shape, generator=g) * scale + shift
+    return t.to(dtype).to(device)
+
+
+def rmsnorm_fwd(x2d: torch.Tensor, w: torch.Tensor, eps: float, want_rstd: bool = False):
+    rows, hidden = x2d.shape
+    y = torch.empty((rows, hidden), dtype=x2d.dtype, device=x2d.device)
+    rstd = torch.empty(rows, dtype=torch.float32, device=x2d.device) if want_rstd else None
+    _capi.rmsnorm_fwd(x2d.data_ptr(), x2d.stride(0), w.data_ptr(), y.data_ptr(), y.stride(0),
+                      rstd.data_ptr() if rstd is not None else None, rows, hidden,
+                      DTYPE_CODES[x2d.dtype], DTYPE_CODES[w.dtype], eps, stream())
+    return (y, rstd) if want_rstd else y
+
+
+def rmsnorm_bwd(dy2d, x2d, w, eps, num_partials=None, rstd=None, return_partials=False):
+    rows, hidden = x2d.shape
+    xc, wc = DTYPE_CODES[x2d.dtype], DTYPE_CODES[w.dtype]
+    if num_partials is None:
+        num_partials = _capi.rmsnorm_bwd_num_partials(rows, hidden, xc, wc)
+    dx = torch.empty((rows, hidden), dtype=x2d.dtype, device=x2d.device)
+    partials = torch.full((num_partials, hidden), float("nan"), dtype=torch.float32,
+                          device=x2d.device)
+    dw = torch.empty(hidden, dtype=w.dtype, device=x2d.device)
+    _capi.rmsnorm_bwd(dy2d.data_ptr(), dy2d.stride(0), x2d.data_ptr(), x2d.stride(0),
+                      w.data_ptr(), rstd.data_ptr() if rstd is not None else None,
+                      dx.data_ptr(), dx.stride(0), partials.data_ptr(), num_partials, rows,
+                      hidden, xc, wc, eps, stream())
+    _capi.rmsnorm_dw_reduce(partials.data_ptr(), num_partials, hidden, dw.data_ptr(),
+                            DTYPE_CODES[w.dtype], stream())
+    if return_partials:
+        return dx, dw, partials
+    return dx, dw
+
+
+def swiglu_fwd(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    out = torch.empty_like(g)
+    _capi.swiglu_fwd(g.data_ptr(), u.data_ptr(), out.data_ptr(), g.numel(), DTYPE_CODES[g.dtype],
+                     stream())
+    return out
+
+
+def swiglu_bwd(dout, g, u):
+    dg, du = torch.empty_like(g), torch.empty_like(g)
+    _capi.swiglu_bwd(dout.data_ptr(), g.data_ptr(), u.data_ptr(), dg.data_ptr(), du.data_ptr(),
+                     g.numel(), DTYPE_CODES[g.dtype], stream())
+    return dg, du
+
+
+def rope(direction: str, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+         layout: str = "interleaved", out: torch.Tensor | None = None) -> torch.Tensor:
+    code = {"interleaved": _capi.PT_ROPE_INTERLEAVED, "rotate_half": _capi.PT_ROPE_ROTATE_HALF}
+    if out is None:
+        out = torch.empty_like(x)
+    _capi.rope(direction, x.data_ptr(), x.stride(), out.data_ptr(), out.stride(), x.shape,
+               cos.data_ptr(), sin.data_ptr(), cos.stride(0), code[layout],
+               DTYPE_CODES[x.dtype], DTYPE_CODES[cos.dtype], stream())
+    return out

@@ -1,0 +1,137 @@
+"""RMSNorm forward/backward kernels vs the float64 oracle, through the C ABI.
+
+Tolerances (oracle/tolerance.py): fp32 outputs within 1e-5 abs + 1e-5 rel; bf16/fp16
+outputs within 2 ulp of the float64 value plus a 2^-16 * max|ref| fp32-accumulation floor.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import golden_io
+import gpu_utils as gu
+from oracle import picotron_oracle as po
+from oracle import tolerance
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _gpu():
+    gu.require_gpu()
+
+
+def _check_case(x, w, dy, eps, what, **bwd_kwargs):
+    y = gu.rmsnorm_fwd(x, w, eps)
+    dx, dw = gu.rmsnorm_bwd(dy, x, w, eps, **bwd_kwargs)
+    torch.cuda.synchronize()
+    ye, _ = po.rms_norm_forward(x.cpu(), w.cpu(), eps, "exact")
+    dxe, dwe = po.rms_norm_backward(x.cpu(), w.cpu(), dy.cpu(), eps, "exact")
+    tolerance.assert_close(y, ye, f"{what} y")
+    tolerance.assert_close(dx, dxe, f"{what} dx")
+    tolerance.assert_close(dw, dwe, f"{what} dw")
+    return y, dx, dw
+
+
+@pytest.mark.parametrize("case", ["cfg1_rmsnorm_f32", "reftest_rmsnorm_f32", "rmsnorm_bf16",
+                                  "rmsnorm_bf16_wf32"])
+def test_golden_fixtures(case):
+    t, meta = golden_io.load(case)
+    eps = float(meta["eps"])
+    h = t["x"].shape[-1]
+    x = t["x"].reshape(-1, h).to(gu.DEV)
+    dy = t["dy"].reshape(-1, h).to(gu.DEV)
+    w = t["w"].to(gu.DEV)
+    y, dx, dw = _check_case(x, w, dy, eps, case)
+    # Against the reference's own output: identical math up to fp32 summation order.
+    ref_dtype = t["y"].dtype
+    tolerance.assert_close(y, t["y"].reshape(-1, h).double(), f"{case} y vs reference",
+                           ref_dtype if ref_dtype != torch.float64 else torch.float32)
+    tolerance.assert_close(dw, t["dw"].double(), f"{case} dw vs reference", torch.float32)
+
+
+PAIRS = [
+    (torch.float32, torch.float32),
+    (torch.bfloat16, torch.bfloat16),
+    (torch.bfloat16, torch.float32),
+    (torch.float16, torch.float16),
+    (torch.float16, torch.float32),
+]
+SHAPES = [(1, 128), (128, 128), (37, 4096), (300, 4096), (64, 2048), (16, 1000), (33, 8),
+          (7, 6), (5, 65536), (40, 16384), (3, 12288), (149, 1024)]
+
+
+@pytest.mark.parametrize("xd,wd", PAIRS, ids=lambda d: str(d).split(".")[-1])
+@pytest.mark.parametrize("shape", SHAPES, ids=str)
+def test_dtypes_and_shapes(xd, wd, shape):
+    rows, h = shape
+    x = gu.randn(shape, 1, xd)
+    w = gu.randn(h, 2, wd, scale=0.1, shift=1.0)
+    dy = gu.randn(shape, 3, xd)
+    _check_case(x, w, dy, 1e-5, f"{xd}/{wd}{shape}")
+
+
+def test_strided_and_misaligned_rows():
+    h = 4096
+    base = gu.randn((64, h + 24), 4, torch.bfloat16)
+    x = base[:, :h]                      # row stride h + 24 (still 16-byte aligned rows)
+    dbase = gu.randn((64, h + 24), 5, torch.bfloat16)
+    dy = dbase[:, 8:8 + h]
+    w = gu.randn(h, 6, torch.float32, 0.02, 1.0)
+    _check_case(x, w, dy, 1e-5, "strided")
+    flat = gu.randn(64 * h + 1, 7, torch.bfloat16)
+    xm = flat[1:].view(64, h)            # 2-byte offset: generic path
+    _check_case(xm, w, dy.contiguous(), 1e-5, "misaligned")
+
+
+def test_saved_rstd_matches_recompute():
+    x = gu.randn((256, 4096), 8, torch.bfloat16)
+    w = gu.randn(4096, 9, torch.float32, 0.02, 1.0)
+    dy = gu.randn((256, 4096), 10, torch.bfloat16)
+    y, rstd = gu.rmsnorm_fwd(x, w, 1e-5, want_rstd=True)
+    _, inv = po.rms_norm_forward(x.cpu(), w.cpu(), 1e-5, "exact")
+    torch.testing.assert_close(rstd.cpu().double(), inv.reshape(-1), rtol=2e-6, atol=0)
+    dx1, dw1 = gu.rmsnorm_bwd(dy, x, w, 1e-5)
+    dx2, dw2 = gu.rmsnorm_bwd(dy, x, w, 1e-5, rstd=rstd)
+    dxe, dwe = po.rms_norm_backward(x.cpu(), w.cpu(), dy.cpu(), 1e-5, "exact")
+    tolerance.assert_close(dx2, dxe, "dx with rstd")
+    tolerance.assert_close(dw2, dwe, "dw with rstd")
+
+
+@pytest.mark.parametrize("num_partials", [1, 3, 148, 5000])
+def test_any_partial_count_and_determinism(num_partials):
+    x = gu.randn((777, 4096), 11, torch.bfloat16)
+    w = gu.randn(4096, 12, torch.float32, 0.02, 1.0)
+    dy = gu.randn((777, 4096), 13, torch.bfloat16)
+    dx1, dw1, p1 = gu.rmsnorm_bwd(dy, x, w, 1e-5, num_partials=num_partials, return_partials=True)
+    dx2, dw2 = gu.rmsnorm_bwd(dy, x, w, 1e-5, num_partials=num_partials)
+    assert torch.isfinite(p1).all()  # every partial row is written (zeros for idle CTAs)
+    assert torch.equal(dx1, dx2) and torch.equal(dw1, dw2)
+    _, dwe = po.rms_norm_backward(x.cpu(), w.cpu(), dy.cpu(), 1e-5, "exact")
+    tolerance.assert_close(dw1, dwe, f"dw P={num_partials}")
+
+
+def test_zero_rows_backward_gives_zero_dweight():
+    w = gu.randn(4096, 14, torch.float32)
+    x = torch.empty((0, 4096), dtype=torch.bfloat16, device=gu.DEV)
+    dx, dw = gu.rmsnorm_bwd(x, x, w, 1e-5, num_partials=5)
+    assert dx.numel() == 0 and torch.equal(dw, torch.zeros_like(dw))
+
+
+def test_full_size_config2_bf16():
+    # x[16384, 4096] ~ N(0,1), gamma = 1 + 0.02 N(0,1), eps 1e-5, dy ~ N(0,1).
+    n, h = 16384, 4096
+    x = gu.randn((n, h), 0, torch.bfloat16)
+    w = gu.randn(h, 1, torch.float32, 0.02, 1.0)
+    dy = gu.randn((n, h), 2, torch.bfloat16)
+    y = gu.rmsnorm_fwd(x, w, 1e-5)
+    dx, dw = gu.rmsnorm_bwd(dy, x, w, 1e-5)
+    ye, _ = po.rms_norm_forward(x, w, 1e-5, "exact")       # float64 on the GPU
+    tolerance.assert_close(y, ye, "cfg2 y")
+    del ye
+    dxe, dwe = po.rms_norm_backward(x, w, dy, 1e-5, "exact")
+    tolerance.assert_close(dx, dxe, "cfg2 dx")
+    tolerance.assert_close(dw, dwe, "cfg2 dw")
+    del dxe, dwe
+    torch.cuda.empty_cache()
