@@ -126,6 +126,13 @@ PT_API int pt_rmsnorm_bwd(const void* dy, int64_t dy_row_stride,
 PT_API int pt_rmsnorm_dw_reduce(const float* dw_partials, int num_partials, int64_t hidden,
                          void* dw, int dw_dtype, void* stream);
 
+/* Reads and clears this library's device-side error word of the current device
+ * (synchronous: waits for the device). *code = 0 means no kernel reported a problem;
+ * 1 means a kernel gave up waiting for one of its own TMA copies (after about a second)
+ * and skipped the rest of its rows, so outputs of the affected call are incomplete.
+ * No reference counterpart: the reference has no device-side waits. */
+PT_API int pt_take_device_error(int* code);
+
 /* ----------------------------------------------------------------- SwiGLU -------- */
 
 /* out = gate * sigmoid(gate) * up over n contiguous elements, fp32 math, one rounding.

@@ -64,6 +64,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                 _c_ptr, _c_int, _c_i64, _c_i64, _c_int, _c_int, _c_float,
                                 _c_ptr]),
     "pt_rmsnorm_dw_reduce": (_c_int, [_c_ptr, _c_int, _c_i64, _c_ptr, _c_int, _c_ptr]),
+    "pt_take_device_error": (_c_int, [ctypes.POINTER(_c_int)]),
     "pt_swiglu_fwd": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_i64, _c_int, _c_ptr]),
     "pt_swiglu_bwd": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_int, _c_ptr]),
     "pt_rope_fwd": (_c_int, [_c_ptr, _c_i64_4, _c_ptr, _c_i64_4, _c_i64_4, _c_ptr, _c_ptr,
@@ -195,6 +196,14 @@ def rmsnorm_dw_reduce(dw_partials: int, num_partials: int, hidden: int, dw: int,
     status = library().pt_rmsnorm_dw_reduce(dw_partials, num_partials, hidden, dw, dw_dtype,
                                             stream)
     _check("pt_rmsnorm_dw_reduce", status, error_type)
+
+
+def take_device_error() -> int:
+    """Read and clear the device-side error word of the current device (synchronous)."""
+
+    code = _c_int(0)
+    _check("pt_take_device_error", library().pt_take_device_error(ctypes.byref(code)), None)
+    return code.value
 
 
 def swiglu_fwd(gate: int, up: int, out: int, n: int, dtype: int, stream: int,

@@ -152,6 +152,146 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// r = 1 / sqrt(m) to about 1e-14 relative: fp32 hardware estimate refined by one
+// Newton step in fp64 (r1 = r0 * (1.5 - 0.5 * m * r0^2); the error squares).
+__device__ __forceinline__ double rsqrt_refined(double m) {
+  const double r0 = (double)rsqrtf((float)m);
+  return r0 * (1.5 - 0.5 * m * r0 * r0);
+}
+
+// Ring position of a row in a `stages`-slot pipeline, advanced without division.
+struct RingPos {
+  int slot = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void advance(int n, int stages) {
+    slot += n;
+    while (slot >= stages) {
+      slot -= stages;
+      phase ^= 1u;
+    }
+  }
+};
+
+// Compensated accumulation of p * (rh + rl) into (sum, comp) on the FP32 pipe, with p
+// exact and r = rh + rl to about 48 bits. The product's rounding error is recovered
+// exactly with an fma (t + e == p * rh), the low part of r is folded into e, and the sum
+// uses Kahan compensation (comp carries minus the lost low-order part), so the result is
+// the exact sum of the terms up to a few ulp of |sum| regardless of how many terms are
+// added. The _rn intrinsics keep the compiler from contracting the error terms.
+__device__ __forceinline__ void kahan_fma_acc(float& sum, float& comp, float p, float rh,
+                                              float rl) {
+  const float t = __fmul_rn(p, rh);
+  float e = fmaf(p, rh, -t);  // exact: p * rh - t
+  e = fmaf(p, rl, e);
+  const float y = __fsub_rn(t, __fsub_rn(comp, e));
+  const float s = __fadd_rn(sum, y);
+  comp = __fsub_rn(__fsub_rn(s, sum), y);
+  sum = s;
+}
+
+// Compensated (Kahan) accumulation: sum + (-comp) tracks the exact running sum; comp
+// carries minus the low-order part lost by each rounded addition. The _rn intrinsics keep
+// the compiler from reassociating or contracting the compensation away.
+__device__ __forceinline__ void kahan_add(float& sum, float& comp, float v) {
+  const float y = __fsub_rn(v, comp);
+  const float t = __fadd_rn(sum, y);
+  comp = __fsub_rn(__fsub_rn(t, sum), y);
+  sum = t;
+}
+
+// ----------------------------------------------------- TMA bulk copies + mbarriers --
+// 1-D bulk copies (cp.async.bulk, no tensor map, no multicast) from global memory into
+// this CTA's shared memory, completing on an mbarrier with a transaction count.
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+// Makes barrier initialisation visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Plain arrival (release semantics at CTA scope: prior writes of this thread are
+// visible to threads that observe the phase completion).
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// dst (shared) and src (global) 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Potentially blocking test of phase `parity`: the thread may sleep until the phase
+// completes or about kSuspendHintNs nanoseconds pass (0: the hardware's default limit).
+#ifndef PT_SUSPEND_NS
+#define PT_SUSPEND_NS 0
+#endif
+constexpr uint32_t kSuspendHintNs = PT_SUSPEND_NS;
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  if constexpr (kSuspendHintNs > 0) {
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendHintNs)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+  }
+  return done != 0;
+}
+
+// Waits for phase `parity` of `bar` to complete, giving up after about one second of SM
+// clock (kWaitLimitCycles); returns false on timeout. Every wait in this library is
+// bounded so that a lost copy can never hang the GPU.
+constexpr long long kWaitLimitCycles = 2000000000LL;
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitLimitCycles) return false;
+  }
+  return true;
+}
+
+// 16-byte shared-memory load.
+__device__ __forceinline__ uint4 lds128(const void* p) {
+  return *reinterpret_cast<const uint4*>(p);
+}
+
+// Device-side error codes reported through pt_take_device_error().
+constexpr int kDeviceErrWaitTimeout = 1;
+
 // fp32 logistic function, sigma(g) = 1 / (1 + e^-g). Uses the CUDA fast exponential;
 // its relative error is far below the fp32 tolerances used by this library. For
 // g << 0 the exponential overflows to +inf and the quotient is exactly 0.

@@ -3,20 +3,38 @@
 // Math follows src/picotron/nn/triton_kernels/rmsnorm.py of the reference:
 //   forward  (:25-46, :49-60)   r = rsqrt(mean(x^2) + eps), y = (x * r) * w, fp32 math
 //   backward (:109-134)          g = dy * w, dx = r * (g - (x * r^2) * mean(g * x)),
-//                                dw = sum_rows (dy * x) * r, fp32 math
+//                                dw = sum_rows (dy * x) * r
 //
 // Layout: x, y, dy, dx are [rows, hidden] with a row stride and contiguous columns.
 //
-// Fast path ("column-owner" kernels): each CTA owns a fixed set of 16-byte column
-// vectors (thread t owns vectors t, t + blockDim, ...; a warp therefore touches
-// contiguous 512-byte runs). The weight of those columns lives in registers for the
-// whole kernel, and so does the backward's dweight accumulator, so weight is read once
-// per CTA and dweight leaves the kernel as one fp32 partial row per CTA. A CTA
-// processes R rows per iteration (R rows' loads in flight before the first reduction),
-// one __syncthreads per iteration (the reduction buffer is double-buffered).
+// Fast path: a warp-specialised, persistent pipeline per CTA.
+//  * A producer warp streams the CTA's rows (b, b + G, b + 2G, ...) into a ring of
+//    `stages` shared-memory slots with 1-D TMA bulk copies (cp.async.bulk; one x row, or
+//    an x row and a dy row, per slot), completing on the slot's `full` mbarrier.
+//  * RW reducer warps each own whole rows (warp-per-row, no cross-warp dependency): a
+//    reducer reads its row from the slot, forms the row statistics (r, and in the
+//    backward c = r^2 mean(dy w x)) and publishes them on the slot's `stats` mbarrier.
+//  * C owner warps own fixed 16-byte column vectors of every row (lane l of warp w owns
+//    vectors l + 32 (w + C k)) and keep their columns' weight, and in the backward an
+//    fp64 dweight accumulator, in registers for the whole kernel. Once a row's statistics
+//    are published they do only elementwise work (y, or dx and dweight), then arrive on
+//    the slot's `empty` mbarrier, which hands the slot back to the producer.
+//  No CTA-wide barrier and no cross-warp reduction run in the loop: the reductions of
+//  later rows proceed while owners stream out earlier rows.
+// Every mbarrier wait is bounded (about 1 s); a timeout records kDeviceErrWaitTimeout in
+// the device error word and the CTA stops after a bounded drain of its copies.
+//
+// dweight precision: r is refined to fp64 precision from an fp64 row sum and carried as
+// two floats (r = rh + rl); each term (dy * x) * r is accumulated with compensated
+// summation on the FP32 pipe, its product rounding recovered exactly by an fma (dy * x
+// of two 16-bit floats is exact in fp32; for fp32 inputs that product's own rounding
+// error is recovered the same way). Each CTA's partial is therefore the exact sum up to
+// a few fp32 ulp, however many rows it reduces, and pt_rmsnorm_dw_reduce adds the
+// partials in fp64. Per-element fp64 arithmetic would make this kernel FP64-bound.
 //
 // Generic path: any hidden size, stride or alignment; one row per CTA iteration with
 // scalar accesses and two passes over the row (the second one hits L2).
+#include <algorithm>
 #include <mutex>
 #include <type_traits>
 #include <unordered_map>
@@ -24,20 +42,52 @@
 #include "common.cuh"
 
 namespace pt {
+
+// Device-side error word of this library on each device (0 = none). Kernels that give up
+// on a bounded wait record kDeviceErrWaitTimeout here; pt_take_device_error reads it.
+__device__ int g_device_error = 0;
+
 namespace {
 
-// Tuning table. A fast-path CTA has at most kMaxThreads threads; each thread owns VPT
-// 16-byte column vectors and keeps R rows in flight. Forward holds one input row per
-// row in flight, backward two (x and dy) plus the dweight accumulator, so backward
-// keeps fewer rows in flight to stay clear of register spills.
-#ifndef PT_RMS_MAX_THREADS
-#define PT_RMS_MAX_THREADS 512
+// Tuning knobs (compile-time overridable for sweeps).
+#ifndef PT_RMS_ELEMS_FWD
+#define PT_RMS_ELEMS_FWD 32  // elements of a row owned by each forward owner thread
 #endif
-constexpr int kMaxThreads = PT_RMS_MAX_THREADS;
+#ifndef PT_RMS_ELEMS_BWD
+#define PT_RMS_ELEMS_BWD 16  // backward owners also hold a compensated dweight pair each
+#endif
+#ifndef PT_RMS_SMEM_FWD
+#define PT_RMS_SMEM_FWD (48 * 1024)  // forward ring budget per CTA
+#endif
+#ifndef PT_RMS_SMEM_BWD
+#define PT_RMS_SMEM_BWD (64 * 1024)  // backward ring budget per CTA (plus the staged weight)
+#endif
+#ifndef PT_RMS_MIN_BLOCKS_FWD
+#define PT_RMS_MIN_BLOCKS_FWD 2
+#endif
+#ifndef PT_RMS_MIN_BLOCKS_BWD
+#define PT_RMS_MIN_BLOCKS_BWD 2
+#endif
+#ifndef PT_RMS_MIN_STAGES
+#define PT_RMS_MIN_STAGES 3
+#endif
+#ifndef PT_RMS_REDUCERS
+#define PT_RMS_REDUCERS 4  // reducer warps per CTA
+#endif
+constexpr int kElemsFwd = PT_RMS_ELEMS_FWD;
+constexpr int kElemsBwd = PT_RMS_ELEMS_BWD;
+constexpr int kSmemFwd = PT_RMS_SMEM_FWD;
+constexpr int kSmemBwd = PT_RMS_SMEM_BWD;
+constexpr int kMinStages = PT_RMS_MIN_STAGES;
+constexpr int kReducers = PT_RMS_REDUCERS;
+constexpr int kMaxStages = 16;
+static_assert(kReducers >= 1 && kReducers <= kMaxStages, "reducer count must fit the ring");
+constexpr int kMaxConsumers = 16;  // owner warps per CTA
+// CTAs of up to this many owner warps (rows of up to 4096 elements) get a tighter
+// launch bound (two CTAs per SM); the backward owners hold half as many elements.
+constexpr int kSmallConsumers(bool bwd) { return bwd ? 8 : 4; }
+constexpr int kMaxSlotBytes = 64 * 1024;
 constexpr int kGenericThreads = 256;
-
-constexpr int fwd_rows_in_flight(int vpt) { return vpt == 1 ? 4 : (vpt == 2 ? 2 : 1); }
-constexpr int bwd_rows_in_flight(int vpt) { return vpt == 1 ? 2 : 1; }
 
 // Sum of `v` over the CTA; `red` is a 32-float shared buffer owned by the caller.
 // Leaves the result in every thread. No trailing barrier: callers alternate buffers.
@@ -50,197 +100,275 @@ __device__ __forceinline__ float block_sum_nosync(float v, float* red) {
   return warp_sum(t);
 }
 
-// ---------------------------------------------------------------- fast forward -----
-template <typename T, typename TW, int VPT, int R>
-__global__ void __launch_bounds__(kMaxThreads)
-rmsnorm_fwd_vec(const T* __restrict__ x, int64_t xs, const TW* __restrict__ w,
-                T* __restrict__ y, int64_t ys, float* __restrict__ rstd, int64_t rows,
-                int nvec, float hidden_f, float eps) {
-  constexpr int V = Vec16<T>::N;
-  __shared__ float red[2][R][32];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
-
-  float wf[VPT][V];
-  bool valid[VPT];
-#pragma unroll
-  for (int k = 0; k < VPT; ++k) {
-    const int v = tid + k * blockDim.x;
-    valid[k] = v < nvec;
-    if (valid[k]) {
-      load_row_f32<TW, V>(w + (int64_t)v * V, wf[k]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < V; ++j) wf[k][j] = 0.0f;
-    }
-  }
-
-  int p = 0;
-  for (int64_t base = (int64_t)blockIdx.x * R; base < rows; base += (int64_t)gridDim.x * R) {
-    uint4 xv[R][VPT];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int64_t row = base + r;
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-        if (row < rows && valid[k])
-          xv[r][k] = ld_stream(x + row * xs + (int64_t)(tid + k * blockDim.x) * V);
-        else
-          xv[r][k] = make_uint4(0, 0, 0, 0);
-      }
-    }
-    float ss[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      ss[r] = 0.0f;
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-        float f[V];
-        unpack<T>(xv[r][k], f);
-#pragma unroll
-        for (int j = 0; j < V; ++j) ss[r] = fmaf(f[j], f[j], ss[r]);
-      }
-      ss[r] = warp_sum(ss[r]);
-      if (lane == 0) red[p][r][warp] = ss[r];
-    }
-    __syncthreads();
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      float t = lane < nwarps ? red[p][r][lane] : 0.0f;
-      t = warp_sum(t);
-      const float inv = rsqrtf(t / hidden_f + eps);
-      const int64_t row = base + r;
-      if (row < rows) {
-#pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-          if (!valid[k]) continue;
-          float f[V];
-          unpack<T>(xv[r][k], f);
-#pragma unroll
-          for (int j = 0; j < V; ++j) f[j] = (f[j] * inv) * wf[k][j];
-          st_stream(y + row * ys + (int64_t)(tid + k * blockDim.x) * V, pack<T>(f));
-        }
-        if (rstd != nullptr && tid == 0) rstd[row] = inv;
-      }
-    }
-    p ^= 1;
-  }
+// Rows of this CTA in the strided assignment row(j) = blockIdx.x + j * gridDim.x.
+__device__ __forceinline__ int64_t local_rows(int64_t rows) {
+  const int64_t b = blockIdx.x;
+  return rows > b ? (rows - 1 - b) / gridDim.x + 1 : 0;
 }
 
-// --------------------------------------------------------------- fast backward -----
-template <typename T, typename TW, int VPT, int R, bool kHasRstd>
-__global__ void __launch_bounds__(kMaxThreads)
-rmsnorm_bwd_vec(const T* __restrict__ dy, int64_t dys, const T* __restrict__ x, int64_t xs,
-                const TW* __restrict__ w, const float* __restrict__ rstd, T* __restrict__ dx,
-                int64_t dxs, float* __restrict__ partials, int64_t rows, int nvec, int hidden,
-                float hidden_f, float eps) {
-  constexpr int V = Vec16<T>::N;
-  __shared__ float red[2][2 * R][32];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+__device__ __forceinline__ void record_timeout() {
+  atomicExch(&g_device_error, kDeviceErrWaitTimeout);
+}
 
-  float wf[VPT][V];
-  float acc[VPT][V];
+// ------------------------------------------------------------ fast fwd / bwd -------
+// Warp roles: warps [0, C) own columns, warps [C, C + RW) reduce rows, warp C + RW is the
+// TMA producer.
+template <typename T, typename TW, int VPT, bool kBwd, bool kHasRstd, int kMaxWarps>
+__global__ void __launch_bounds__(kMaxWarps * 32,
+                                  kMaxWarps <= 16 ? (kBwd ? PT_RMS_MIN_BLOCKS_BWD
+                                                          : PT_RMS_MIN_BLOCKS_FWD)
+                                                  : 1)
+rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_t dys,
+           const TW* __restrict__ w, const float* __restrict__ rstd_in, T* __restrict__ out,
+           int64_t os, float* __restrict__ rstd_out, float* __restrict__ partials, int64_t rows,
+           int nvec, int hidden, int stages, int C, int RW, float hidden_f, float eps) {
+  constexpr int V = Vec16<T>::N;
+  constexpr int kRowsPerSlot = kBwd ? 2 : 1;
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ __align__(8) uint64_t full[kMaxStages];
+  __shared__ __align__(8) uint64_t stats[kMaxStages];
+  __shared__ __align__(8) uint64_t empty[kMaxStages];
+  __shared__ double stat_inv[kMaxStages];
+  __shared__ float stat_c[kMaxStages];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row_elems = nvec * V;
+  const uint32_t row_bytes = (uint32_t)nvec * 16u;
+  T* slots = reinterpret_cast<T*>(smem);
+  // Backward: the reducers need the weight of every column; it is staged once, in fp32,
+  // after the ring.
+  float* wsm = reinterpret_cast<float*>(smem + (size_t)stages * kRowsPerSlot * row_bytes);
+  const int64_t G = gridDim.x;
+  const int64_t n_local = local_rows(rows);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&stats[s], 1);
+      mbar_init(&empty[s], C);
+    }
+    fence_mbar_init();
+  }
+  if constexpr (kBwd) {
+    for (int i = threadIdx.x; i < nvec * V; i += blockDim.x) wsm[i] = to_float(w[i]);
+  }
+  __syncthreads();
+
+  // ---------------------------------------------------------------- producer warp --
+  if (warp == C + RW) {
+    if (lane == 0) {
+      RingPos pos;
+      const T* xr = x + (int64_t)blockIdx.x * xs;
+      const T* gr = kBwd ? dy + (int64_t)blockIdx.x * dys : nullptr;
+      for (int64_t j = 0; j < n_local; ++j) {
+        // The k-th refill of a slot waits for the owners to release use k-1.
+        if (j >= stages && !mbar_wait_bounded(&empty[pos.slot], pos.phase ^ 1u)) {
+          record_timeout();
+          break;
+        }
+        mbar_arrive_expect_tx(&full[pos.slot], kRowsPerSlot * row_bytes);
+        T* dst = slots + (int64_t)(kRowsPerSlot * pos.slot) * row_elems;
+        bulk_load(dst, xr, row_bytes, &full[pos.slot]);
+        xr += G * xs;
+        if constexpr (kBwd) {
+          bulk_load(dst + row_elems, gr, row_bytes, &full[pos.slot]);
+          gr += G * dys;
+        }
+        pos.advance(1, stages);
+      }
+    }
+    return;
+  }
+
+  // ----------------------------------------------------------------- reducer warps --
+  // Reducer r owns local rows r, r + RW, ...: it reads the whole row from its slot
+  // (lane l takes vectors l, l + 32, ...), forms sum(x^2) (and sum(dy * w * x)), and
+  // publishes r = rsqrt(mean(x^2) + eps) (and c = r^2 * mean(dy * w * x)) for the slot.
+  if (warp >= C) {
+    const int rid = warp - C;
+    RingPos pos;
+    pos.advance(rid, stages);
+    for (int64_t j = rid; j < n_local; j += RW) {
+      if (!mbar_wait_bounded(&full[pos.slot], pos.phase)) {
+        record_timeout();
+        return;
+      }
+      const T* sx = slots + (int64_t)(kRowsPerSlot * pos.slot) * row_elems;
+      // Four independent accumulators (one per vector of an unrolled group of four).
+      float ss[4] = {0.0f, 0.0f, 0.0f, 0.0f}, dot[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      auto accumulate = [&](int v, int q) {
+        float fx[V];
+        unpack<T>(lds128(sx + v * V), fx);
+        if constexpr (kBwd) {
+          float fg[V];
+          unpack<T>(lds128(sx + row_elems + v * V), fg);
+          const float* wv = wsm + v * V;
+#pragma unroll
+          for (int e = 0; e < V; ++e) {
+            if (!kHasRstd) ss[q] = fmaf(fx[e], fx[e], ss[q]);
+            dot[q] = fmaf(fg[e] * wv[e], fx[e], dot[q]);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < V; ++e) ss[q] = fmaf(fx[e], fx[e], ss[q]);
+        }
+      };
+      int v = lane;
+      for (; v + 96 < nvec; v += 128) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) accumulate(v + 32 * q, q);
+      }
+      for (int q = 0; v < nvec; v += 32, ++q) {
+        if (q == 0) accumulate(v, 0);
+        else if (q == 1) accumulate(v, 1);
+        else accumulate(v, 2);
+      }
+      const int64_t row = blockIdx.x + j * G;
+      if constexpr (kBwd) {
+        double invd;
+        if constexpr (kHasRstd) {
+          invd = (double)__ldg(rstd_in + row);
+        } else {
+          double ssd = ((double)ss[0] + (double)ss[1]) + ((double)ss[2] + (double)ss[3]);
+          ssd = warp_sum(ssd);
+          invd = rsqrt_refined(ssd / (double)hidden + (double)eps);
+        }
+        float d = (dot[0] + dot[1]) + (dot[2] + dot[3]);
+        d = warp_sum(d);
+        if (lane == 0) {
+          const float inv = (float)invd;
+          stat_inv[pos.slot] = invd;
+          stat_c[pos.slot] = (inv * inv) * (d / hidden_f);
+        }
+      } else {
+        float t = (ss[0] + ss[1]) + (ss[2] + ss[3]);
+        t = warp_sum(t);
+        if (lane == 0) {
+          const float inv = rsqrtf(t / hidden_f + eps);
+          stat_inv[pos.slot] = (double)inv;
+          if (rstd_out != nullptr) rstd_out[row] = inv;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&stats[pos.slot]);
+      pos.advance(RW, stages);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ owner warps --
+  // Forward: the owners' weights live in registers. Backward: they are read from the
+  // staged fp32 copy, leaving the registers to the fp64 dweight accumulators (two CTAs per
+  // SM fit only that way).
+  float wf[kBwd ? 1 : VPT][V];
+  float acc[kBwd ? VPT : 1][kBwd ? V : 1], comp[kBwd ? VPT : 1][kBwd ? V : 1];
   bool valid[VPT];
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
-    const int v = tid + k * blockDim.x;
+    const int v = lane + 32 * (warp + C * k);
     valid[k] = v < nvec;
-#pragma unroll
-    for (int j = 0; j < V; ++j) acc[k][j] = 0.0f;
-    if (valid[k]) {
-      load_row_f32<TW, V>(w + (int64_t)v * V, wf[k]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < V; ++j) wf[k][j] = 0.0f;
-    }
-  }
-
-  int p = 0;
-  for (int64_t base = (int64_t)blockIdx.x * R; base < rows; base += (int64_t)gridDim.x * R) {
-    uint4 xv[R][VPT], gv[R][VPT];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int64_t row = base + r;
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-        const int64_t col = (int64_t)(tid + k * blockDim.x) * V;
-        if (row < rows && valid[k]) {
-          xv[r][k] = ld_stream(x + row * xs + col);
-          gv[r][k] = ld_stream(dy + row * dys + col);
-        } else {
-          xv[r][k] = make_uint4(0, 0, 0, 0);
-          gv[r][k] = make_uint4(0, 0, 0, 0);
-        }
-      }
-    }
-    // Per-row partial sums: sum(x^2) (unless rstd is given) and sum(g * x), g = dy * w.
-    float ss[R], dot[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      ss[r] = 0.0f;
-      dot[r] = 0.0f;
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-        float fx[V], fg[V];
-        unpack<T>(xv[r][k], fx);
-        unpack<T>(gv[r][k], fg);
-#pragma unroll
-        for (int j = 0; j < V; ++j) {
-          if (!kHasRstd) ss[r] = fmaf(fx[j], fx[j], ss[r]);
-          dot[r] = fmaf(fg[j] * wf[k][j], fx[j], dot[r]);
-        }
-      }
-      if (!kHasRstd) ss[r] = warp_sum(ss[r]);
-      dot[r] = warp_sum(dot[r]);
-      if (lane == 0) {
-        red[p][2 * r][warp] = ss[r];
-        red[p][2 * r + 1][warp] = dot[r];
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int64_t row = base + r;
-      float tdot = lane < nwarps ? red[p][2 * r + 1][lane] : 0.0f;
-      tdot = warp_sum(tdot);
-      float inv;
-      if (kHasRstd) {
-        inv = row < rows ? __ldg(rstd + row) : 0.0f;
+    if constexpr (!kBwd) {
+      if (valid[k]) {
+        load_row_f32<TW, V>(w + (int64_t)v * V, wf[k]);
       } else {
-        float tss = lane < nwarps ? red[p][2 * r][lane] : 0.0f;
-        tss = warp_sum(tss);
-        inv = rsqrtf(tss / hidden_f + eps);
-      }
-      if (row < rows) {
-        const float dot_mean = tdot / hidden_f;
-        const float c = (inv * inv) * dot_mean;
 #pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-          if (!valid[k]) continue;
-          float fx[V], fg[V], fo[V];
-          unpack<T>(xv[r][k], fx);
-          unpack<T>(gv[r][k], fg);
-#pragma unroll
-          for (int j = 0; j < V; ++j) {
-            const float g = fg[j] * wf[k][j];
-            fo[j] = inv * (g - fx[j] * c);
-            acc[k][j] = fmaf(fg[j] * fx[j], inv, acc[k][j]);
-          }
-          st_stream(dx + row * dxs + (int64_t)(tid + k * blockDim.x) * V, pack<T>(fo));
-        }
+        for (int e = 0; e < V; ++e) wf[k][e] = 0.0f;
       }
     }
-    p ^= 1;
+  }
+  if constexpr (kBwd) {
+#pragma unroll
+    for (int k = 0; k < VPT; ++k)
+#pragma unroll
+      for (int e = 0; e < V; ++e) acc[k][e] = comp[k][e] = 0.0f;
   }
 
-  // This CTA's dweight partial row (zeros when it owned no rows).
-  float* prow = partials + (int64_t)blockIdx.x * hidden;
+  RingPos pos;
+  int64_t j = 0;
+  bool ok = true;
+  for (; j < n_local; ++j) {
+    // The slot's data (full) and its statistics (stats) must both have landed.
+    ok = mbar_wait_bounded(&full[pos.slot], pos.phase) &&
+         mbar_wait_bounded(&stats[pos.slot], pos.phase);
+    if (!ok) break;
+    const int64_t row = blockIdx.x + j * G;
+    const T* sx = slots + (int64_t)(kRowsPerSlot * pos.slot) * row_elems;
+    if constexpr (!kBwd) {
+      const float inv = (float)stat_inv[pos.slot];
 #pragma unroll
-  for (int k = 0; k < VPT; ++k) {
-    if (!valid[k]) continue;
-    float4* dst = reinterpret_cast<float4*>(prow + (int64_t)(tid + k * blockDim.x) * V);
+      for (int k = 0; k < VPT; ++k) {
+        if (!valid[k]) continue;
+        const int off = (lane + 32 * (warp + C * k)) * V;
+        float f[V];
+        unpack<T>(lds128(sx + off), f);
 #pragma unroll
-    for (int j = 0; j < V / 4; ++j)
-      dst[j] = make_float4(acc[k][4 * j], acc[k][4 * j + 1], acc[k][4 * j + 2], acc[k][4 * j + 3]);
+        for (int e = 0; e < V; ++e) f[e] = (f[e] * inv) * wf[k][e];
+        st_stream(out + row * os + off, pack<T>(f));
+      }
+    } else {
+      const double invd = stat_inv[pos.slot];
+      const float inv = (float)invd;
+      const float inv_lo = (float)(invd - (double)inv);  // r = inv + inv_lo to ~48 bits
+      const float c = stat_c[pos.slot];
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        if (!valid[k]) continue;
+        const int off = (lane + 32 * (warp + C * k)) * V;
+        float fx[V], fg[V], fo[V], wv[V];
+        unpack<T>(lds128(sx + off), fx);
+        unpack<T>(lds128(sx + row_elems + off), fg);
+#pragma unroll
+        for (int q = 0; q < V / 4; ++q) {
+          const float4 t = *reinterpret_cast<const float4*>(wsm + off + 4 * q);
+          wv[4 * q] = t.x;
+          wv[4 * q + 1] = t.y;
+          wv[4 * q + 2] = t.z;
+          wv[4 * q + 3] = t.w;
+        }
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          fo[e] = inv * (fg[e] * wv[e] - fx[e] * c);
+          const float pxy = __fmul_rn(fg[e], fx[e]);  // exact for 16-bit inputs
+          kahan_fma_acc(acc[k][e], comp[k][e], pxy, inv, inv_lo);
+          if constexpr (sizeof(T) == 4) {
+            // fp32 inputs: the rounding error of dy * x, recovered exactly, times r.
+            comp[k][e] = __fsub_rn(comp[k][e], __fmul_rn(fmaf(fg[e], fx[e], -pxy), inv));
+          }
+        }
+        st_stream(out + row * os + off, pack<T>(fo));
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[pos.slot]);
+    pos.advance(1, stages);
+  }
+
+  if (!ok) {
+    // Give copies that may still land in this CTA's slots a bounded chance to finish.
+    record_timeout();
+    for (int64_t i = j; i < n_local && i < j + stages; ++i) {
+      mbar_wait_bounded(&full[pos.slot], pos.phase);
+      pos.advance(1, stages);
+    }
+    return;
+  }
+
+  if constexpr (kBwd) {
+    // This CTA's dweight partial row (zeros when it owned no rows).
+    float* prow = partials + (int64_t)blockIdx.x * hidden;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      if (!valid[k]) continue;
+      float4* dst =
+          reinterpret_cast<float4*>(prow + (int64_t)(lane + 32 * (warp + C * k)) * V);
+#pragma unroll
+      for (int q = 0; q < V / 4; ++q) {
+        float o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = __fsub_rn(acc[k][4 * q + i], comp[k][4 * q + i]);
+        dst[q] = make_float4(o[0], o[1], o[2], o[3]);
+      }
+    }
   }
 }
 
@@ -308,80 +436,155 @@ rmsnorm_bwd_generic(const T* __restrict__ dy, int64_t dys, const T* __restrict__
   }
 }
 
+constexpr int kReduceWarps = 32;
+constexpr int kReduceUnroll = 4;
+
 template <typename TW>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kReduceWarps * 32)
 rmsnorm_dw_reduce_kernel(const float* __restrict__ partials, int num_partials, int64_t hidden,
                          TW* __restrict__ dw) {
-  // 32 columns per CTA (one per lane), 8 warps split the partial rows; warp w sums rows
-  // w, w + 8, ... in increasing order, then warp sums are added in warp order. The order
-  // depends only on num_partials, so the result is deterministic.
-  __shared__ float s[8][33];
+  // 32 columns per CTA (one per lane). Warp w sums the partial rows p = w*U + u + i*W*U
+  // (u < U) into U independent compensated fp32 accumulators, in increasing i; the U
+  // compensated sums are combined in fp64, the W warp sums are added in fp64 in warp
+  // order, and the result is rounded once. The order depends only on num_partials, so the
+  // result is deterministic, and the compensation keeps it correctly rounded in practice
+  // even when the partials cancel.
+  __shared__ double s[kReduceWarps][33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t c = (int64_t)blockIdx.x * 32 + lane;
-  float acc = 0.0f;
-  if (c < hidden)
-    for (int p = warp; p < num_partials; p += 8) acc += partials[(int64_t)p * hidden + c];
-  s[warp][lane] = acc;
+  float acc[kReduceUnroll], comp[kReduceUnroll];
+#pragma unroll
+  for (int u = 0; u < kReduceUnroll; ++u) acc[u] = comp[u] = 0.0f;
+  if (c < hidden) {
+    for (int p0 = warp * kReduceUnroll; p0 < num_partials; p0 += kReduceWarps * kReduceUnroll) {
+      float v[kReduceUnroll];
+#pragma unroll
+      for (int u = 0; u < kReduceUnroll; ++u)
+        v[u] = p0 + u < num_partials ? partials[(int64_t)(p0 + u) * hidden + c] : 0.0f;
+#pragma unroll
+      for (int u = 0; u < kReduceUnroll; ++u) kahan_add(acc[u], comp[u], v[u]);
+    }
+  }
+  double t = 0.0;
+#pragma unroll
+  for (int u = 0; u < kReduceUnroll; ++u) t += (double)acc[u] - (double)comp[u];
+  s[warp][lane] = t;
   __syncthreads();
   if (warp == 0 && c < hidden) {
-    float t = 0.0f;
+    double sum = 0.0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) t += s[i][lane];
-    dw[c] = from_float<TW>(t);
+    for (int i = 0; i < kReduceWarps; ++i) sum += s[i][lane];
+    dw[c] = from_float<TW>((float)sum);
   }
 }
 
 // ------------------------------------------------------------------ host helpers ---
 
-// Resident CTAs per SM for a kernel at a block size; cached, the value never changes.
-int blocks_per_sm(const void* func, int threads) {
+// Resident CTAs per SM for a kernel at a block size and dynamic shared memory; cached.
+// On first use of a kernel, raises its dynamic shared memory limit to everything the
+// device allows beside the kernel's static shared memory (one fixed value per kernel, so
+// launches of any smaller size stay valid). Returns 0 when the kernel cannot run with
+// `smem` bytes.
+int blocks_per_sm(const void* func, int threads, int smem) {
   static std::mutex mu;
   static std::unordered_map<uint64_t, int> cache;
+  static std::unordered_map<uint64_t, int> limit;  // (func, device) -> max dynamic smem
   int dev = 0;
   cudaGetDevice(&dev);
-  const uint64_t key = (reinterpret_cast<uint64_t>(func) * 1315423911ull) ^
-                       ((uint64_t)threads << 8) ^ (uint64_t)dev;
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    auto it = cache.find(key);
-    if (it != cache.end()) return it->second;
+  const uint64_t fkey = (reinterpret_cast<uint64_t>(func) * 1315423911ull) ^ (uint64_t)dev;
+  const uint64_t key = fkey ^ ((uint64_t)threads << 40) ^ ((uint64_t)smem << 8);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  auto lt = limit.find(fkey);
+  if (lt == limit.end()) {
+    int optin = 0;
+    cudaFuncAttributes attr;
+    int max_dyn = 48 * 1024;
+    if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) ==
+            cudaSuccess &&
+        cudaFuncGetAttributes(&attr, func) == cudaSuccess) {
+      const int want = optin - (int)attr.sharedSizeBytes;
+      if (want > max_dyn &&
+          cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, want) ==
+              cudaSuccess)
+        max_dyn = want;
+    }
+    cudaGetLastError();
+    lt = limit.emplace(fkey, max_dyn).first;
   }
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, func, threads, 0) != cudaSuccess) {
+  if (smem <= lt->second &&
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, func, threads, smem) != cudaSuccess) {
     cudaGetLastError();
-    n = 1;
+    n = 0;
   }
-  if (n < 1) n = 1;
-  std::lock_guard<std::mutex> lock(mu);
   cache[key] = n;
   return n;
 }
 
 struct FastPlan {
   bool ok = false;
-  int vpt = 0;
-  int threads = 0;
+  int vpt = 0;        // vectors per owner thread (template parameter)
+  int consumers = 0;  // owner warps
+  int reducers = 0;   // reducer warps
   int nvec = 0;
+  int stages = 0;
+  int smem = 0;
 };
 
-// Chooses the column-owner layout: the fewest vectors per thread that keep the CTA
-// within kMaxThreads. Returns ok=false when the row shape needs the generic path.
-template <typename T>
+// Largest vectors-per-thread built for a direction: kElemsFwd / kElemsBwd elements per
+// owner thread. Smaller rows use half or a quarter of it (at least 1 vector).
+template <typename T, bool kBwd> constexpr int vpt_max() {
+  return (kBwd ? kElemsBwd : kElemsFwd) / Vec16<T>::N > 0
+             ? (kBwd ? kElemsBwd : kElemsFwd) / Vec16<T>::N
+             : 1;
+}
+template <typename T, bool kBwd> constexpr int vpt_half() {
+  return vpt_max<T, kBwd>() / 2 > 0 ? vpt_max<T, kBwd>() / 2 : 1;
+}
+template <typename T, bool kBwd> constexpr int vpt_quarter() {
+  return vpt_max<T, kBwd>() / 4 > 0 ? vpt_max<T, kBwd>() / 4 : 1;
+}
+
+// Owner layout and ring depth: the fewest owner warps that give each thread at most
+// kElemsPerThread elements, the smallest built vectors-per-thread that covers the row
+// with them, and a ring of as many slots as fit in the forward or backward budget (at
+// least kMinStages, a multiple of the reducer count). ok=false when the row needs the
+// generic path.
+template <typename T, bool kBwd>
 FastPlan plan_fast(int64_t hidden) {
   FastPlan plan;
   constexpr int V = Vec16<T>::N;
   if (hidden <= 0 || hidden % V != 0) return plan;
   const int64_t nvec = hidden / V;
-  for (int vpt : {1, 2, 4}) {
-    const int64_t need = (nvec + vpt - 1) / vpt;
-    if (need <= kMaxThreads) {
-      plan.ok = true;
-      plan.vpt = vpt;
-      plan.nvec = (int)nvec;
-      plan.threads = (int)((need + 31) / 32 * 32);
-      return plan;
+  const int64_t slot_bytes = nvec * 16 * (kBwd ? 2 : 1);
+  if (slot_bytes > kMaxSlotBytes) return plan;
+  const int vmax = vpt_max<T, kBwd>();
+  const int64_t consumers = (nvec + 32 * vmax - 1) / (32 * vmax);
+  if (consumers > kMaxConsumers) return plan;
+  const int64_t need = (nvec + 32 * consumers - 1) / (32 * consumers);
+  int vpt = vmax;
+  if (consumers <= kSmallConsumers(kBwd)) {
+    if (need <= vpt_quarter<T, kBwd>()) {
+      vpt = vpt_quarter<T, kBwd>();
+    } else if (need <= vpt_half<T, kBwd>()) {
+      vpt = vpt_half<T, kBwd>();
     }
   }
+  plan.vpt = vpt;
+  plan.consumers = (int)consumers;
+  plan.nvec = (int)nvec;
+  // stages must be a multiple of the reducer count: then each slot is served by exactly
+  // one reducer, which visits it in row order, so no waiter can reach a slot's barrier two
+  // phases early (try_wait.parity cannot tell use k from use k - 2).
+  int stages = (int)std::min<int64_t>(kMaxStages, (kBwd ? kSmemBwd : kSmemFwd) / slot_bytes);
+  stages = std::max(stages, kMinStages);
+  stages = std::max(kReducers, stages / kReducers * kReducers);
+  plan.stages = stages;
+  plan.reducers = kReducers;
+  plan.smem = (int)(stages * slot_bytes + (kBwd ? nvec * V * 4 : 0));
+  plan.ok = true;
   return plan;
 }
 
@@ -389,6 +592,47 @@ template <typename T>
 bool rows_aligned(const void* p, int64_t stride) {
   return aligned16(p) && ((stride * (int64_t)sizeof(T)) % 16 == 0);
 }
+
+// Kernel instance for a plan: CTAs of up to kSmallConsumers consumer warps (rows of up to
+// 4 * 32 * kElemsPerThread elements) use any of the three vectors-per-thread shapes under
+// a 5-warp launch bound; bigger CTAs use the full shape under a 17-warp bound.
+#define PT_WS(VPT_, MAXW_) rmsnorm_ws<T, TW, VPT_, kBwd, kHasRstd, MAXW_>
+template <bool kBwd> constexpr int small_warps() { return kSmallConsumers(kBwd) + kReducers + 1; }
+constexpr int kBigWarps = kMaxConsumers + kReducers + 1;
+inline int ws_threads(const FastPlan& plan) {
+  return (plan.consumers + plan.reducers + 1) * 32;
+}
+template <typename T, typename TW, bool kBwd, bool kHasRstd>
+const void* ws_kernel(const FastPlan& plan) {
+  constexpr int SW = small_warps<kBwd>();
+  if (plan.consumers > kSmallConsumers(kBwd))
+    return (const void*)PT_WS((vpt_max<T, kBwd>()), kBigWarps);
+  if (plan.vpt == vpt_max<T, kBwd>()) return (const void*)PT_WS((vpt_max<T, kBwd>()), SW);
+  if (plan.vpt == vpt_half<T, kBwd>()) return (const void*)PT_WS((vpt_half<T, kBwd>()), SW);
+  return (const void*)PT_WS((vpt_quarter<T, kBwd>()), SW);
+}
+
+template <typename T, typename TW, bool kBwd, bool kHasRstd>
+void ws_launch(const FastPlan& plan, int grid, cudaStream_t stream, const T* x, int64_t xs,
+               const T* dy, int64_t dys, const TW* w, const float* rstd_in, T* out, int64_t os,
+               float* rstd_out, float* partials, int64_t rows, int hidden, float eps) {
+  constexpr int SW = small_warps<kBwd>();
+  const int threads = ws_threads(plan);
+  const float hf = (float)hidden;
+#define PT_WS_ARGS                                                                         \
+  x, xs, dy, dys, w, rstd_in, out, os, rstd_out, partials, rows, plan.nvec, hidden,        \
+      plan.stages, plan.consumers, plan.reducers, hf, eps
+  if (plan.consumers > kSmallConsumers(kBwd))
+    PT_WS((vpt_max<T, kBwd>()), kBigWarps)<<<grid, threads, plan.smem, stream>>>(PT_WS_ARGS);
+  else if (plan.vpt == vpt_max<T, kBwd>())
+    PT_WS((vpt_max<T, kBwd>()), SW)<<<grid, threads, plan.smem, stream>>>(PT_WS_ARGS);
+  else if (plan.vpt == vpt_half<T, kBwd>())
+    PT_WS((vpt_half<T, kBwd>()), SW)<<<grid, threads, plan.smem, stream>>>(PT_WS_ARGS);
+  else
+    PT_WS((vpt_quarter<T, kBwd>()), SW)<<<grid, threads, plan.smem, stream>>>(PT_WS_ARGS);
+#undef PT_WS_ARGS
+}
+#undef PT_WS
 
 template <typename T, typename TW>
 int fwd_impl(const void* x_, int64_t xs, const void* w_, void* y_, int64_t ys, float* rstd,
@@ -398,36 +642,22 @@ int fwd_impl(const void* x_, int64_t xs, const void* w_, void* y_, int64_t ys, f
   T* y = static_cast<T*>(y_);
   int dev = 0, sms = 0;
   if (int st = current_device_info(&dev, &sms)) return st;
-  FastPlan plan = plan_fast<T>(hidden);
-  const bool fast = plan.ok && rows_aligned<T>(x, xs) && rows_aligned<T>(y, ys) && aligned16(w);
+  FastPlan plan = plan_fast<T, false>(hidden);
+  bool fast = plan.ok && rows_aligned<T>(x, xs) && rows_aligned<T>(y, ys) && aligned16(w);
+  int occ = 0;
   if (fast) {
-#define PT_FWD_KERNEL(VPT) rmsnorm_fwd_vec<T, TW, VPT, fwd_rows_in_flight(VPT)>
-    const void* fn = plan.vpt == 1   ? (const void*)PT_FWD_KERNEL(1)
-                     : plan.vpt == 2 ? (const void*)PT_FWD_KERNEL(2)
-                                     : (const void*)PT_FWD_KERNEL(4);
-    const int R = fwd_rows_in_flight(plan.vpt);
-    const int64_t groups = (rows + R - 1) / R;
-    const int64_t resident = (int64_t)sms * blocks_per_sm(fn, plan.threads);
-    const int grid = (int)(groups < resident ? groups : resident);
-    const float hf = (float)hidden;
-    switch (plan.vpt) {
-      case 1:
-        PT_FWD_KERNEL(1)<<<grid, plan.threads, 0, stream>>>(x, xs, w, y, ys, rstd, rows,
-                                                            plan.nvec, hf, eps);
-        break;
-      case 2:
-        PT_FWD_KERNEL(2)<<<grid, plan.threads, 0, stream>>>(x, xs, w, y, ys, rstd, rows,
-                                                            plan.nvec, hf, eps);
-        break;
-      default:
-        PT_FWD_KERNEL(4)<<<grid, plan.threads, 0, stream>>>(x, xs, w, y, ys, rstd, rows,
-                                                            plan.nvec, hf, eps);
-        break;
-    }
-#undef PT_FWD_KERNEL
+    occ = blocks_per_sm(ws_kernel<T, TW, false, false>(plan), ws_threads(plan),
+                        plan.smem);
+    fast = occ > 0;
+  }
+  if (fast) {
+    const int64_t resident = (int64_t)sms * occ;
+    const int grid = (int)(rows < resident ? rows : resident);
+    ws_launch<T, TW, false, false>(plan, grid, stream, x, xs, nullptr, 0, w, nullptr, y, ys, rstd,
+                                   nullptr, rows, (int)hidden, eps);
   } else {
     const void* fn = (const void*)rmsnorm_fwd_generic<T, TW>;
-    const int64_t resident = (int64_t)sms * blocks_per_sm(fn, kGenericThreads);
+    const int64_t resident = (int64_t)sms * std::max(1, blocks_per_sm(fn, kGenericThreads, 0));
     const int grid = (int)(rows < resident ? rows : resident);
     rmsnorm_fwd_generic<T, TW><<<grid, kGenericThreads, 0, stream>>>(x, xs, w, y, ys, rstd, rows,
                                                                      (int)hidden, eps);
@@ -435,32 +665,23 @@ int fwd_impl(const void* x_, int64_t xs, const void* w_, void* y_, int64_t ys, f
   return check_launch("pt_rmsnorm_fwd");
 }
 
-#define PT_BWD_KERNEL(VPT, HR) rmsnorm_bwd_vec<T, TW, VPT, bwd_rows_in_flight(VPT), HR>
-
-template <typename T, typename TW>
-const void* bwd_kernel_for(const FastPlan& plan, bool has_rstd) {
-  switch (plan.vpt) {
-    case 1: return has_rstd ? (const void*)PT_BWD_KERNEL(1, true) : (const void*)PT_BWD_KERNEL(1, false);
-    case 2: return has_rstd ? (const void*)PT_BWD_KERNEL(2, true) : (const void*)PT_BWD_KERNEL(2, false);
-    default: return has_rstd ? (const void*)PT_BWD_KERNEL(4, true) : (const void*)PT_BWD_KERNEL(4, false);
-  }
-}
-
 template <typename T, typename TW>
 int num_partials_impl(int64_t rows, int64_t hidden, int* out) {
   int dev = 0, sms = 0;
   if (int st = current_device_info(&dev, &sms)) return st;
-  FastPlan plan = plan_fast<T>(hidden);
+  FastPlan plan = plan_fast<T, true>(hidden);
+  int occ = 0;
+  if (plan.ok)
+    occ = blocks_per_sm(ws_kernel<T, TW, true, false>(plan), ws_threads(plan),
+                        plan.smem);
   int64_t n;
-  if (plan.ok) {
-    const int R = bwd_rows_in_flight(plan.vpt);
-    const int64_t groups = (rows + R - 1) / R;
-    n = (int64_t)sms * blocks_per_sm(bwd_kernel_for<T, TW>(plan, false), plan.threads);
-    if (groups < n) n = groups;
+  if (occ > 0) {
+    n = (int64_t)sms * occ;
   } else {
-    n = (int64_t)sms * blocks_per_sm((const void*)rmsnorm_bwd_generic<T, TW>, kGenericThreads);
-    if (rows < n) n = rows;
+    n = (int64_t)sms *
+        std::max(1, blocks_per_sm((const void*)rmsnorm_bwd_generic<T, TW>, kGenericThreads, 0));
   }
+  if (rows < n) n = rows;
   if (n < 1) n = 1;
   *out = (int)n;
   return ok();
@@ -474,21 +695,22 @@ int bwd_impl(const void* dy_, int64_t dys, const void* x_, int64_t xs, const voi
   const T* x = static_cast<const T*>(x_);
   const TW* w = static_cast<const TW*>(w_);
   T* dx = static_cast<T*>(dx_);
-  FastPlan plan = plan_fast<T>(hidden);
-  const bool fast = plan.ok && rows_aligned<T>(x, xs) && rows_aligned<T>(dy, dys) &&
-                    rows_aligned<T>(dx, dxs) && aligned16(w) && aligned16(partials);
-  const float hf = (float)hidden;
+  FastPlan plan = plan_fast<T, true>(hidden);
+  bool fast = plan.ok && rows_aligned<T>(x, xs) && rows_aligned<T>(dy, dys) &&
+              rows_aligned<T>(dx, dxs) && aligned16(w) && aligned16(partials);
+  const bool hr = rstd != nullptr;
   if (fast) {
-    const bool hr = rstd != nullptr;
-#define PT_BWD_LAUNCH(VPT, HR)                                                              \
-  PT_BWD_KERNEL(VPT, HR)<<<num_partials, plan.threads, 0, stream>>>(                        \
-      dy, dys, x, xs, w, rstd, dx, dxs, partials, rows, plan.nvec, (int)hidden, hf, eps)
-    switch (plan.vpt) {
-      case 1: if (hr) PT_BWD_LAUNCH(1, true); else PT_BWD_LAUNCH(1, false); break;
-      case 2: if (hr) PT_BWD_LAUNCH(2, true); else PT_BWD_LAUNCH(2, false); break;
-      default: if (hr) PT_BWD_LAUNCH(4, true); else PT_BWD_LAUNCH(4, false); break;
-    }
-#undef PT_BWD_LAUNCH
+    const void* fn = hr ? ws_kernel<T, TW, true, true>(plan)
+                        : ws_kernel<T, TW, true, false>(plan);
+    fast = blocks_per_sm(fn, ws_threads(plan), plan.smem) > 0;
+  }
+  if (fast) {
+    if (hr)
+      ws_launch<T, TW, true, true>(plan, num_partials, stream, x, xs, dy, dys, w, rstd, dx, dxs,
+                                   nullptr, partials, rows, (int)hidden, eps);
+    else
+      ws_launch<T, TW, true, false>(plan, num_partials, stream, x, xs, dy, dys, w, nullptr, dx,
+                                    dxs, nullptr, partials, rows, (int)hidden, eps);
   } else {
     rmsnorm_bwd_generic<T, TW><<<num_partials, kGenericThreads, 0, stream>>>(
         dy, dys, x, xs, w, rstd, dx, dxs, partials, rows, (int)hidden, eps);
@@ -603,24 +825,46 @@ int pt_rmsnorm_dw_reduce(const float* dw_partials, int num_partials, int64_t hid
   if (int st = check_device_ptr(dw_partials, "dw_partials")) return st;
   if (int st = check_device_ptr(dw, "dw")) return st;
   const int grid = (int)((hidden + 31) / 32);
+  const int threads = kReduceWarps * 32;
   cudaStream_t s = as_stream(stream);
   switch (dw_dtype) {
     case PT_FLOAT32:
-      rmsnorm_dw_reduce_kernel<float><<<grid, 256, 0, s>>>(dw_partials, num_partials, hidden,
-                                                           static_cast<float*>(dw));
+      rmsnorm_dw_reduce_kernel<float><<<grid, threads, 0, s>>>(dw_partials, num_partials, hidden,
+                                                               static_cast<float*>(dw));
       break;
     case PT_FLOAT16:
-      rmsnorm_dw_reduce_kernel<__half><<<grid, 256, 0, s>>>(dw_partials, num_partials, hidden,
-                                                            static_cast<__half*>(dw));
+      rmsnorm_dw_reduce_kernel<__half><<<grid, threads, 0, s>>>(dw_partials, num_partials, hidden,
+                                                                static_cast<__half*>(dw));
       break;
     case PT_BFLOAT16:
-      rmsnorm_dw_reduce_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+      rmsnorm_dw_reduce_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>(
           dw_partials, num_partials, hidden, static_cast<__nv_bfloat16*>(dw));
       break;
     default:
       return set_error(PT_ERR_UNSUPPORTED_DTYPE, "unsupported dw_dtype %d", dw_dtype);
   }
   return check_launch("pt_rmsnorm_dw_reduce");
+}
+
+int pt_take_device_error(int* code) {
+  if (code == nullptr) return set_error(PT_ERR_INVALID_ARGUMENT, "code is NULL");
+  int value = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&value, g_device_error, sizeof(int));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(PT_ERR_CUDA, "cannot read the device error word: %s", cudaGetErrorString(e));
+  }
+  if (value != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return set_error(PT_ERR_CUDA, "cannot clear the device error word: %s",
+                       cudaGetErrorString(e));
+    }
+  }
+  *code = value;
+  return ok();
 }
 
 }  // extern "C"
