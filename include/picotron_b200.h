@@ -126,6 +126,28 @@ PT_API int pt_rmsnorm_bwd(const void* dy, int64_t dy_row_stride,
 PT_API int pt_rmsnorm_dw_reduce(const float* dw_partials, int num_partials, int64_t hidden,
                          void* dw, int dw_dtype, void* stream);
 
+/* pt_rmsnorm_bwd without any device allocation, for callers that cannot allocate device
+ * memory themselves: a host runtime whose memory pool owns all of the device's memory, a
+ * training step that must not pay cudaMalloc/cudaFree's implicit device synchronisation,
+ * or a thin FFI binding with no allocator to size and keep a dw_partials buffer. Computes
+ * dx (x dtype) and dw (w_dtype) directly. It has no counterpart in the reference.
+ * The dweight partials go to a scratch array inside the library (2^21 floats = 8 MiB per
+ * device, kept until the process exits); hidden above 2^21 is rejected with PT_ERR_SHAPE.
+ * The first call on a device looks up that array's address (cudaGetSymbolAddress), so
+ * make it before any stream capture. All calls share the one array: calls whose work
+ * overlaps on the GPU (different streams, or different host threads on one device without
+ * ordering) race on it and must be serialised by the caller. Nothing in the array needs
+ * to start at zero: each call writes every partial it later reads. */
+PT_API int pt_rmsnorm_bwd_noalloc(const void* dy, int64_t dy_row_stride,
+                                  const void* x, int64_t x_row_stride,
+                                  const void* weight,
+                                  const float* rstd,
+                                  void* dx, int64_t dx_row_stride,
+                                  void* dw,
+                                  int64_t rows, int64_t hidden,
+                                  int x_dtype, int w_dtype, float eps,
+                                  void* stream);
+
 /* Reads and clears this library's device-side error word of the current device
  * (synchronous: waits for the device). *code = 0 means no kernel reported a problem;
  * 1 means a kernel gave up waiting for one of its own TMA copies (after about a second)

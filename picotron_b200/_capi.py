@@ -64,6 +64,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                 _c_ptr, _c_int, _c_i64, _c_i64, _c_int, _c_int, _c_float,
                                 _c_ptr]),
     "pt_rmsnorm_dw_reduce": (_c_int, [_c_ptr, _c_int, _c_i64, _c_ptr, _c_int, _c_ptr]),
+    "pt_rmsnorm_bwd_noalloc": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_ptr,
+                                        _c_i64, _c_ptr, _c_i64, _c_i64, _c_int, _c_int,
+                                        _c_float, _c_ptr]),
     "pt_take_device_error": (_c_int, [ctypes.POINTER(_c_int)]),
     "pt_swiglu_fwd": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_i64, _c_int, _c_ptr]),
     "pt_swiglu_bwd": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_int, _c_ptr]),
@@ -196,6 +199,18 @@ def rmsnorm_dw_reduce(dw_partials: int, num_partials: int, hidden: int, dw: int,
     status = library().pt_rmsnorm_dw_reduce(dw_partials, num_partials, hidden, dw, dw_dtype,
                                             stream)
     _check("pt_rmsnorm_dw_reduce", status, error_type)
+
+
+def rmsnorm_bwd_noalloc(dy: int, dy_row_stride: int, x: int, x_row_stride: int, weight: int,
+                        rstd: int | None, dx: int, dx_row_stride: int, dw: int, rows: int,
+                        hidden: int, x_dtype: int, w_dtype: int, eps: float, stream: int,
+                        error_type: type[Exception] | None = None) -> None:
+    """RMSNorm backward that allocates nothing (see pt_rmsnorm_bwd_noalloc)."""
+
+    status = library().pt_rmsnorm_bwd_noalloc(dy, dy_row_stride, x, x_row_stride, weight, rstd,
+                                              dx, dx_row_stride, dw, rows, hidden, x_dtype,
+                                              w_dtype, eps, stream)
+    _check("pt_rmsnorm_bwd_noalloc", status, error_type)
 
 
 def take_device_error() -> int:

@@ -846,6 +846,71 @@ int pt_rmsnorm_dw_reduce(const float* dw_partials, int num_partials, int64_t hid
   return check_launch("pt_rmsnorm_dw_reduce");
 }
 
+// ------------------------------------------------------- allocation-free backward --
+// Scratch for pt_rmsnorm_bwd_noalloc: the dweight partials live in this file-scope device
+// array (kNoAllocFloats floats = 8 MiB, held by every device that loads the library until
+// the process exits). Host code must not use the symbol itself as a device address: its
+// address on a device comes from cudaGetSymbolAddress, taken once per device.
+namespace pt {
+namespace {
+constexpr int64_t kNoAllocFloats = int64_t(1) << 21;
+constexpr int kNoAllocMaxDevices = 64;
+__device__ __align__(256) float g_noalloc_partials[kNoAllocFloats];
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+int noalloc_scratch(float** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(PT_ERR_DEVICE, "no current CUDA device");
+  }
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return set_error(PT_ERR_DEVICE, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+    if (e != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return set_error(PT_ERR_CUDA, "cannot get the scratch address on device %d: %s", dev,
+                       cudaGetErrorString(e));
+    }
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return PT_OK;
+}
+}  // namespace
+}  // namespace pt
+
+int pt_rmsnorm_bwd_noalloc(const void* dy, int64_t dy_row_stride, const void* x,
+                           int64_t x_row_stride, const void* weight, const float* rstd, void* dx,
+                           int64_t dx_row_stride, void* dw, int64_t rows, int64_t hidden,
+                           int x_dtype, int w_dtype, float eps, void* stream) {
+  if (int st = check_shape(rows, hidden)) return st;
+  if (hidden > kNoAllocFloats)
+    return set_error(PT_ERR_SHAPE,
+                     "pt_rmsnorm_bwd_noalloc: hidden (%lld) exceeds its scratch of %lld floats; "
+                     "use pt_rmsnorm_bwd with a caller-provided dw_partials buffer",
+                     (long long)hidden, (long long)kNoAllocFloats);
+  if (int st = check_device_ptr(dw, "dw")) return st;
+  int num_partials = 0;
+  if (int st = pt_rmsnorm_bwd_num_partials(rows, hidden, x_dtype, w_dtype, &num_partials))
+    return st;
+  const int64_t fit = kNoAllocFloats / hidden;
+  if (num_partials > fit) num_partials = (int)fit;
+  float* scratch = nullptr;
+  if (int st = noalloc_scratch(&scratch)) return st;
+  // Every partial row [0, num_partials) is written by the backward before the reduce
+  // reads it, so the scratch needs no clearing between calls.
+  if (int st = pt_rmsnorm_bwd(dy, dy_row_stride, x, x_row_stride, weight, rstd, dx,
+                              dx_row_stride, scratch, num_partials, rows, hidden, x_dtype,
+                              w_dtype, eps, stream))
+    return st;
+  return pt_rmsnorm_dw_reduce(scratch, num_partials, hidden, dw, w_dtype, stream);
+}
+
 int pt_take_device_error(int* code) {
   if (code == nullptr) return set_error(PT_ERR_INVALID_ARGUMENT, "code is NULL");
   int value = 0;
