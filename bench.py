@@ -258,6 +258,9 @@ class Stack:
         self.partials = torch.empty((self.num_partials, HIDDEN), device=device,
                                     dtype=torch.float32)
         self.launches_per_step = layers * 8
+        self.events_per_step = layers  # one (start, end) pair per SwiGLU backward launch
+        self.dominant = ("swiglu_bwd_vec (SwiGLU backward)", 5 * tokens * INTER * BF16)
+        self.traffic_key = "swiglu_bwd"
 
     # algorithmic bytes (each input read once, each output written once)
     def bytes_per_step(self) -> int:
@@ -302,6 +305,107 @@ class Stack:
                                                      self.bucket.slot(2 * l + k).data_ptr(), f32,
                                                      stream), "dw reduce")
         self.bucket.all_reduce()
+
+
+class OpWorkload:
+    """One hot-path op (3, 4) forward + backward per step through the C
+    ABI, on `tokens` rows with rotating input sets larger than L2. Used for per-kernel
+    measurement and for small ncu captures; the default workload is the stack."""
+
+    def __init__(self, op: str, tokens: int, device: torch.device, seed: int) -> None:
+        from picotron_b200 import _capi
+
+        self.capi, self.lib, self.op, self.tokens, self.device = _capi, _capi.library(), op, tokens, device
+        gen = torch.Generator(device=device).manual_seed(seed)
+        bf = torch.bfloat16
+        sets = 3
+        if op == "rmsnorm":
+            self.x = [torch.randn((tokens, HIDDEN), generator=gen, device=device, dtype=bf)
+                      for _ in range(sets)]
+            self.dy = [torch.randn((tokens, HIDDEN), generator=gen, device=device, dtype=bf)
+                       for _ in range(sets)]
+            self.w = 1 + 0.02 * torch.randn(HIDDEN, generator=gen, device=device)
+            self.y = torch.empty((tokens, HIDDEN), device=device, dtype=bf)
+            self.dx = torch.empty_like(self.y)
+            self.dw = torch.empty(HIDDEN, device=device)
+            self.P = _capi.rmsnorm_bwd_num_partials(tokens, HIDDEN, _capi.PT_BFLOAT16, _capi.PT_FLOAT32)
+            self.part = torch.empty((self.P, HIDDEN), device=device)
+            self.bytes = 5 * tokens * HIDDEN * BF16
+            self.launches_per_step = 3
+            self.dominant = ("rmsnorm_ws (backward)", 3 * tokens * HIDDEN * BF16)
+        elif op == "swiglu":
+            mk = lambda scale: [torch.randn((tokens, INTER), generator=gen, device=device, dtype=bf) * scale
+                                for _ in range(sets)]
+            self.g, self.u, self.do = mk(2.0), mk(2.0), mk(1.0)
+            self.out = torch.empty((tokens, INTER), device=device, dtype=bf)
+            self.dg, self.du = torch.empty_like(self.out), torch.empty_like(self.out)
+            self.bytes = 8 * tokens * INTER * BF16
+            self.launches_per_step = 2
+            self.dominant = ("swiglu_bwd_vec", 5 * tokens * INTER * BF16)
+        elif op == "rope":
+            # BASELINE config 4 per 2048-token sequence: q [B,S,32,128], k [B,S,8,128] memory.
+            b = max(1, tokens // 2048)
+            self.q = [torch.randn((b, 2048, 32, 128), generator=gen, device=device, dtype=bf)
+                      for _ in range(sets)]
+            self.k = [torch.randn((b, 2048, 8, 128), generator=gen, device=device, dtype=bf)
+                      for _ in range(sets)]
+            self.qo, self.ko = torch.empty_like(self.q[0]), torch.empty_like(self.k[0])
+            from picotron_b200.modules import rotary_cos_sin
+
+            self.cos, self.sin = rotary_cos_sin(2048, 128, 500000.0, device=device, dtype=bf)
+            self.bytes = 4 * (self.q[0].numel() + self.k[0].numel()) * BF16
+            self.launches_per_step = 4
+            self.dominant = ("rope_vec (q)", 2 * self.q[0].numel() * BF16)
+            self.tokens = b * 2048
+        else:
+            raise SystemExit(f"unknown workload {op}")
+        self.i = 0
+        self.events_per_step = 1
+        self.traffic_key = {"rmsnorm": "rmsnorm_bwd", "swiglu": "swiglu_bwd", "rope": "rope_fwd"}[op]
+
+    def bytes_per_step(self) -> int:
+        return self.bytes
+
+    def _check(self, status: int, name: str) -> None:
+        if status != 0:
+            raise RuntimeError(f"{name}: {self.capi.last_error()}")
+
+    def step(self, stream: int, world: int, dominant_events: list | None = None) -> None:
+        lib, c, T = self.lib, self.capi, self.tokens
+        i = self.i % 3
+        self.i += 1
+        ev = dominant_events[0] if dominant_events else None
+        if self.op == "rmsnorm":
+            self._check(lib.pt_rmsnorm_fwd(self.x[i].data_ptr(), HIDDEN, self.w.data_ptr(),
+                                           self.y.data_ptr(), HIDDEN, None, T, HIDDEN,
+                                           c.PT_BFLOAT16, c.PT_FLOAT32, EPS, stream), "fwd")
+            if ev: ev[0].record()
+            self._check(lib.pt_rmsnorm_bwd(self.dy[i].data_ptr(), HIDDEN, self.x[i].data_ptr(),
+                                           HIDDEN, self.w.data_ptr(), None, self.dx.data_ptr(),
+                                           HIDDEN, self.part.data_ptr(), self.P, T, HIDDEN,
+                                           c.PT_BFLOAT16, c.PT_FLOAT32, EPS, stream), "bwd")
+            if ev: ev[1].record()
+            self._check(lib.pt_rmsnorm_dw_reduce(self.part.data_ptr(), self.P, HIDDEN,
+                                                 self.dw.data_ptr(), c.PT_FLOAT32, stream), "red")
+        elif self.op == "swiglu":
+            n = T * INTER
+            self._check(lib.pt_swiglu_fwd(self.g[i].data_ptr(), self.u[i].data_ptr(),
+                                          self.out.data_ptr(), n, c.PT_BFLOAT16, stream), "fwd")
+            if ev: ev[0].record()
+            self._check(lib.pt_swiglu_bwd(self.do[i].data_ptr(), self.g[i].data_ptr(),
+                                          self.u[i].data_ptr(), self.dg.data_ptr(),
+                                          self.du.data_ptr(), n, c.PT_BFLOAT16, stream), "bwd")
+            if ev: ev[1].record()
+        else:
+            for t, o, direction in ((self.q[i], self.qo, "fwd"), (self.k[i], self.ko, "fwd"),
+                                    (self.qo, self.q[i], "bwd"), (self.ko, self.k[i], "bwd")):
+                xv, ov = t.transpose(1, 2), o.transpose(1, 2)
+                first = ev is not None and t is self.q[i] and direction == "fwd"
+                if first: ev[0].record()
+                c.rope(direction, xv.data_ptr(), xv.stride(), ov.data_ptr(), ov.stride(), xv.shape,
+                       self.cos.data_ptr(), self.sin.data_ptr(), self.cos.stride(0),
+                       c.PT_ROPE_INTERLEAVED, c.PT_BFLOAT16, c.PT_BFLOAT16, stream)
+                if first: ev[1].record()
 
 
 def e2e_run(stack: Stack, steps: int, warmup: int, world: int) -> dict:
@@ -384,18 +488,28 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tokens", type=int, default=2048)
+    ap.add_argument("--workload", choices=["stack", "rmsnorm", "swiglu", "rope"], default="stack",
+                    help="stack = BASELINE config 5 (the headline); the others are configs 2, 3 "
+                         "and 4, one op forward+backward per step, for per-kernel measurement")
     args = ap.parse_args()
+    if args.workload != "stack":
+        args.no_e2e = True
+        args.no_cpu_baseline = True
     if args.warmup < 3 and args.impl == "ours":
         print("note: warm-up raised to the minimum of 3 steps", file=sys.stderr)
         args.warmup = 3
 
+    names = {"stack": "llama3-8b norm/act stack (BASELINE config 5)",
+             "rmsnorm": "RMSNorm fwd+bwd bf16 h4096 (BASELINE config 2)",
+             "swiglu": "SwiGLU fwd+bwd bf16 i14336 (BASELINE config 3)",
+             "rope": "RoPE q+k fwd+bwd bf16 (BASELINE config 4)"}
     config = {
-        "workload": "llama3-8b norm/act stack (BASELINE config 5)",
+        "workload": names[args.workload],
         "layers": args.layers,
         "tokens_per_gpu": args.tokens,
         "hidden": HIDDEN,
         "intermediate": INTER,
-        "global_batch": 4 * args.gpus * args.tokens // 16384,
+        "global_batch": max(1, args.gpus * args.tokens // 4096),
         "seq_len": 4096,
         "parallelism": f"dp{args.gpus}",
         "eps": EPS,
@@ -433,16 +547,20 @@ def main() -> None:
     if status != 0:
         raise SystemExit(f"device rejected: {_capi.last_error()}")
 
-    stack = Stack(args.layers, args.tokens, device, seed=1234 + rank)
+    if args.workload == "stack":
+        work = Stack(args.layers, args.tokens, device, seed=1234 + rank)
+    else:
+        work = OpWorkload(args.workload, args.tokens, device, seed=1234 + rank)
     stream = torch.cuda.current_stream(device).cuda_stream
     torch.cuda.synchronize()
 
     for _ in range(args.warmup):
-        stack.step(stream, world)
+        work.step(stream, world)
     torch.cuda.synchronize()
 
+    E = work.events_per_step
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.layers * args.steps)]
+          for _ in range(E * args.steps)]
     uuids = []
     for i in range(torch.cuda.device_count()):
         try:
@@ -455,24 +573,24 @@ def main() -> None:
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
         for s in range(args.steps):
-            stack.step(stream, world, ev[s * args.layers:(s + 1) * args.layers])
+            work.step(stream, world, ev[s * E:(s + 1) * E])
         end.record()
         torch.cuda.synchronize()
         barrier(world)
     elapsed = start.elapsed_time(end)
     ms = max_over_ranks(elapsed, world, device) / args.steps
-    swiglu_ms = statistics.fmean(a.elapsed_time(b) for a, b in ev)
-    swiglu_ms = max_over_ranks(swiglu_ms, world, device)
+    dom_ms = statistics.fmean(a.elapsed_time(b) for a, b in ev)
+    dom_ms = max_over_ranks(dom_ms, world, device)
 
     peak, peak_kind = measured_peaks()
-    bytes_step = stack.bytes_per_step()
-    swiglu_bytes = 5 * args.tokens * INTER * BF16
-    achieved = swiglu_bytes / (swiglu_ms / 1e3) / 1e9
-    traffic = dram_traffic_per_launch("swiglu_bwd", args.tokens)
+    bytes_step = work.bytes_per_step()
+    dom_name, dom_bytes = work.dominant
+    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+    traffic = dram_traffic_per_launch(work.traffic_key, work.tokens)
 
     e2e = None
     if not args.no_e2e:
-        e2e = e2e_run(stack, max(1, args.e2e_steps), 1, world)
+        e2e = e2e_run(work, max(1, args.e2e_steps), 1, world)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -482,7 +600,7 @@ def main() -> None:
     if rank == 0:
         line = {
             "metric": METRIC,
-            "value": world * args.tokens / (ms / 1e3),
+            "value": world * work.tokens / (ms / 1e3),
             "unit": "tokens/s",
             "n_gpus": world,
             "steps": args.steps,
@@ -497,7 +615,7 @@ def main() -> None:
             "hbm_gbs_per_gpu": bytes_step / (ms / 1e3) / 1e9,
             "hbm_frac_per_gpu": bytes_step / (ms / 1e3) / 1e9 / peak,
             "roofline": {
-                "kernel": "swiglu_bwd_vec (SwiGLU backward)",
+                "kernel": dom_name,
                 "bound": "hbm",
                 "achieved": achieved,
                 "peak": peak,
@@ -505,12 +623,12 @@ def main() -> None:
                 "unit": "GB/s",
                 "frac": achieved / peak,
                 "traffic": traffic,
-                "algorithmic_bytes_per_launch": swiglu_bytes,
-                "mean_launch_us": swiglu_ms * 1e3,
+                "algorithmic_bytes_per_launch": dom_bytes,
+                "mean_launch_us": dom_ms * 1e3,
             },
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": stack.launches_per_step * args.steps,
+            "gpu_launches": work.launches_per_step * args.steps,
             "clocks": clocks.summary() if rank == 0 else None,
         }
         print(json.dumps(line), flush=True)
