@@ -140,6 +140,9 @@ def init_distributed(gpus: int):
     if world > 1:
         import torch.distributed as dist
 
+        # rank 0 must print exactly one line on stdout: keep NCCL's version banner off it
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))

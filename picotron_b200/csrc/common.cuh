@@ -108,6 +108,17 @@ template <> __device__ __forceinline__ void unpack<__half>(const uint4& v, float
   }
 }
 
+// Unpack a 16-byte vector of T into V/2 fp32 pairs (element 2i in .x, 2i+1 in .y).
+template <typename T> __device__ __forceinline__ void unpack2(const uint4& v, float2* f) {
+  float t[Vec16<T>::N];
+  unpack<T>(v, t);
+#pragma unroll
+  for (int i = 0; i < Vec16<T>::N / 2; ++i) f[i] = make_float2(t[2 * i], t[2 * i + 1]);
+}
+
+__device__ __forceinline__ float2 neg2(float2 a) { return make_float2(-a.x, -a.y); }
+__device__ __forceinline__ float2 splat2(float a) { return make_float2(a, a); }
+
 // Pack fp32 values into a 16-byte vector of T with round-to-nearest-even.
 template <typename T> __device__ __forceinline__ uint4 pack(const float* f);
 
@@ -192,6 +203,19 @@ __device__ __forceinline__ void kahan_fma_acc(float& sum, float& comp, float p, 
   const float y = __fsub_rn(t, __fsub_rn(comp, e));
   const float s = __fadd_rn(sum, y);
   comp = __fsub_rn(__fsub_rn(s, sum), y);
+  sum = s;
+}
+
+// Paired form of kahan_fma_acc on two lanes at once, using sm_100's paired FP32
+// instructions (one instruction per two values). Same arithmetic, same exactness.
+__device__ __forceinline__ void kahan_fma_acc2(float2& sum, float2& comp, float2 p, float2 rh,
+                                               float2 rl) {
+  const float2 t = __fmul2_rn(p, rh);
+  float2 e = __ffma2_rn(p, rh, neg2(t));  // exact: p * rh - t
+  e = __ffma2_rn(p, rl, e);
+  const float2 y = __fadd2_rn(t, neg2(__fadd2_rn(comp, neg2(e))));
+  const float2 s = __fadd2_rn(sum, y);
+  comp = __fadd2_rn(__fadd2_rn(s, neg2(sum)), neg2(y));
   sum = s;
 }
 

@@ -136,8 +136,11 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
   const uint32_t row_bytes = (uint32_t)nvec * 16u;
   T* slots = reinterpret_cast<T*>(smem);
   // Backward: the reducers need the weight of every column; it is staged once, in fp32,
-  // after the ring.
-  float* wsm = reinterpret_cast<float*>(smem + (size_t)stages * kRowsPerSlot * row_bytes);
+  // after the ring, in planes of four floats: float4 number v of plane q holds the weights
+  // of elements 4q .. 4q+3 of column vector v. A warp reading plane q of 32 consecutive
+  // vectors then touches 512 contiguous bytes (no bank conflicts).
+  float4* wsm = reinterpret_cast<float4*>(smem + (size_t)stages * kRowsPerSlot * row_bytes);
+  constexpr int kPlanes = V / 4;
   const int64_t G = gridDim.x;
   const int64_t n_local = local_rows(rows);
 
@@ -150,7 +153,11 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
     fence_mbar_init();
   }
   if constexpr (kBwd) {
-    for (int i = threadIdx.x; i < nvec * V; i += blockDim.x) wsm[i] = to_float(w[i]);
+    float* wf32 = reinterpret_cast<float*>(wsm);
+    for (int i = threadIdx.x; i < nvec * V; i += blockDim.x) {
+      const int v = i / V, e = i - v * V;
+      wf32[((e >> 2) * nvec + v) * 4 + (e & 3)] = to_float(w[i]);
+    }
   }
   __syncthreads();
 
@@ -194,23 +201,31 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
         return;
       }
       const T* sx = slots + (int64_t)(kRowsPerSlot * pos.slot) * row_elems;
-      // Four independent accumulators (one per vector of an unrolled group of four).
-      float ss[4] = {0.0f, 0.0f, 0.0f, 0.0f}, dot[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      auto accumulate = [&](int v, int q) {
-        float fx[V];
-        unpack<T>(lds128(sx + v * V), fx);
-        if constexpr (kBwd) {
-          float fg[V];
-          unpack<T>(lds128(sx + row_elems + v * V), fg);
-          const float* wv = wsm + v * V;
+      // Four independent paired accumulators (one per vector of an unrolled group of four).
+      float2 ss[4], dot[4];
 #pragma unroll
-          for (int e = 0; e < V; ++e) {
-            if (!kHasRstd) ss[q] = fmaf(fx[e], fx[e], ss[q]);
-            dot[q] = fmaf(fg[e] * wv[e], fx[e], dot[q]);
+      for (int q = 0; q < 4; ++q) ss[q] = dot[q] = make_float2(0.0f, 0.0f);
+      auto accumulate = [&](int v, int q) {
+        float2 fx[V / 2];
+        unpack2<T>(lds128(sx + v * V), fx);
+        if constexpr (kBwd) {
+          float2 fg[V / 2];
+          unpack2<T>(lds128(sx + row_elems + v * V), fg);
+          float2 wv[V / 2];
+#pragma unroll
+          for (int q = 0; q < kPlanes; ++q) {
+            const float4 t = wsm[q * nvec + v];
+            wv[2 * q] = make_float2(t.x, t.y);
+            wv[2 * q + 1] = make_float2(t.z, t.w);
+          }
+#pragma unroll
+          for (int e = 0; e < V / 2; ++e) {
+            if (!kHasRstd) ss[q] = __ffma2_rn(fx[e], fx[e], ss[q]);
+            dot[q] = __ffma2_rn(__fmul2_rn(fg[e], wv[e]), fx[e], dot[q]);
           }
         } else {
 #pragma unroll
-          for (int e = 0; e < V; ++e) ss[q] = fmaf(fx[e], fx[e], ss[q]);
+          for (int e = 0; e < V / 2; ++e) ss[q] = __ffma2_rn(fx[e], fx[e], ss[q]);
         }
       };
       int v = lane;
@@ -229,11 +244,13 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
         if constexpr (kHasRstd) {
           invd = (double)__ldg(rstd_in + row);
         } else {
-          double ssd = ((double)ss[0] + (double)ss[1]) + ((double)ss[2] + (double)ss[3]);
+          double ssd = ((double)ss[0].x + (double)ss[0].y) + ((double)ss[1].x + (double)ss[1].y) +
+                       ((double)ss[2].x + (double)ss[2].y) + ((double)ss[3].x + (double)ss[3].y);
           ssd = warp_sum(ssd);
           invd = rsqrt_refined(ssd / (double)hidden + (double)eps);
         }
-        float d = (dot[0] + dot[1]) + (dot[2] + dot[3]);
+        float d = ((dot[0].x + dot[0].y) + (dot[1].x + dot[1].y)) +
+                  ((dot[2].x + dot[2].y) + (dot[3].x + dot[3].y));
         d = warp_sum(d);
         if (lane == 0) {
           const float inv = (float)invd;
@@ -241,7 +258,8 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
           stat_c[pos.slot] = (inv * inv) * (d / hidden_f);
         }
       } else {
-        float t = (ss[0] + ss[1]) + (ss[2] + ss[3]);
+        float t = ((ss[0].x + ss[0].y) + (ss[1].x + ss[1].y)) +
+                  ((ss[2].x + ss[2].y) + (ss[3].x + ss[3].y));
         t = warp_sum(t);
         if (lane == 0) {
           const float inv = rsqrtf(t / hidden_f + eps);
@@ -261,7 +279,9 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
   // staged fp32 copy, leaving the registers to the fp64 dweight accumulators (two CTAs per
   // SM fit only that way).
   float wf[kBwd ? 1 : VPT][V];
-  float acc[kBwd ? VPT : 1][kBwd ? V : 1], comp[kBwd ? VPT : 1][kBwd ? V : 1];
+  // Backward: one compensated (sum, comp) pair per element, held as fp32 pairs.
+  constexpr int V2 = V / 2;
+  float2 acc[kBwd ? VPT : 1][kBwd ? V2 : 1], comp[kBwd ? VPT : 1][kBwd ? V2 : 1];
   bool valid[VPT];
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
@@ -280,7 +300,7 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
 #pragma unroll
     for (int k = 0; k < VPT; ++k)
 #pragma unroll
-      for (int e = 0; e < V; ++e) acc[k][e] = comp[k][e] = 0.0f;
+      for (int e = 0; e < V2; ++e) acc[k][e] = comp[k][e] = make_float2(0.0f, 0.0f);
   }
 
   RingPos pos;
@@ -299,10 +319,17 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
       for (int k = 0; k < VPT; ++k) {
         if (!valid[k]) continue;
         const int off = (lane + 32 * (warp + C * k)) * V;
+        float2 f2[V / 2];
+        unpack2<T>(lds128(sx + off), f2);
         float f[V];
-        unpack<T>(lds128(sx + off), f);
+        const float2 inv2 = splat2(inv);
 #pragma unroll
-        for (int e = 0; e < V; ++e) f[e] = (f[e] * inv) * wf[k][e];
+        for (int e = 0; e < V / 2; ++e) {
+          const float2 o = __fmul2_rn(__fmul2_rn(f2[e], inv2),
+                                      make_float2(wf[k][2 * e], wf[k][2 * e + 1]));
+          f[2 * e] = o.x;
+          f[2 * e + 1] = o.y;
+        }
         st_stream(out + row * os + off, pack<T>(f));
       }
     } else {
@@ -314,25 +341,30 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
       for (int k = 0; k < VPT; ++k) {
         if (!valid[k]) continue;
         const int off = (lane + 32 * (warp + C * k)) * V;
-        float fx[V], fg[V], fo[V], wv[V];
-        unpack<T>(lds128(sx + off), fx);
-        unpack<T>(lds128(sx + row_elems + off), fg);
+        float2 fx[V2], fg[V2], wv[V2];
+        float fo[V];
+        unpack2<T>(lds128(sx + off), fx);
+        unpack2<T>(lds128(sx + row_elems + off), fg);
+        const int vec = lane + 32 * (warp + C * k);
 #pragma unroll
-        for (int q = 0; q < V / 4; ++q) {
-          const float4 t = *reinterpret_cast<const float4*>(wsm + off + 4 * q);
-          wv[4 * q] = t.x;
-          wv[4 * q + 1] = t.y;
-          wv[4 * q + 2] = t.z;
-          wv[4 * q + 3] = t.w;
+        for (int q = 0; q < kPlanes; ++q) {
+          const float4 t = wsm[q * nvec + vec];
+          wv[2 * q] = make_float2(t.x, t.y);
+          wv[2 * q + 1] = make_float2(t.z, t.w);
         }
+        const float2 inv2 = splat2(inv), inv_lo2 = splat2(inv_lo), c2 = splat2(c);
 #pragma unroll
-        for (int e = 0; e < V; ++e) {
-          fo[e] = inv * (fg[e] * wv[e] - fx[e] * c);
-          const float pxy = __fmul_rn(fg[e], fx[e]);  // exact for 16-bit inputs
-          kahan_fma_acc(acc[k][e], comp[k][e], pxy, inv, inv_lo);
+        for (int e = 0; e < V2; ++e) {
+          // dx = r * (dy * w - x * c)
+          const float2 o = __fmul2_rn(inv2, __ffma2_rn(neg2(fx[e]), c2, __fmul2_rn(fg[e], wv[e])));
+          fo[2 * e] = o.x;
+          fo[2 * e + 1] = o.y;
+          const float2 pxy = __fmul2_rn(fg[e], fx[e]);  // exact for 16-bit inputs
+          kahan_fma_acc2(acc[k][e], comp[k][e], pxy, inv2, inv_lo2);
           if constexpr (sizeof(T) == 4) {
             // fp32 inputs: the rounding error of dy * x, recovered exactly, times r.
-            comp[k][e] = __fsub_rn(comp[k][e], __fmul_rn(fmaf(fg[e], fx[e], -pxy), inv));
+            const float2 pe = __ffma2_rn(fg[e], fx[e], neg2(pxy));
+            comp[k][e] = __fadd2_rn(comp[k][e], neg2(__fmul2_rn(pe, inv2)));
           }
         }
         st_stream(out + row * os + off, pack<T>(fo));
@@ -363,10 +395,9 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
           reinterpret_cast<float4*>(prow + (int64_t)(lane + 32 * (warp + C * k)) * V);
 #pragma unroll
       for (int q = 0; q < V / 4; ++q) {
-        float o[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) o[i] = __fsub_rn(acc[k][4 * q + i], comp[k][4 * q + i]);
-        dst[q] = make_float4(o[0], o[1], o[2], o[3]);
+        const float2 a = __fadd2_rn(acc[k][2 * q], neg2(comp[k][2 * q]));
+        const float2 b = __fadd2_rn(acc[k][2 * q + 1], neg2(comp[k][2 * q + 1]));
+        dst[q] = make_float4(a.x, a.y, b.x, b.y);
       }
     }
   }
