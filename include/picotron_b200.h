@@ -96,15 +96,19 @@ PT_API int pt_rmsnorm_fwd(const void* x, int64_t x_row_stride,
                    void* stream);
 
 /* Number of dweight partial rows that pt_rmsnorm_bwd should be given for this problem on
- * the current device: one per resident CTA of the backward kernel. Any positive value
- * is valid; the result of the backward depends only on (inputs, num_partials). */
+ * the current device: two per resident CTA of the backward kernel (a sum row and an error
+ * row). Any positive value is valid; the result of the backward depends only on (inputs,
+ * num_partials). */
 PT_API int pt_rmsnorm_bwd_num_partials(int64_t rows, int64_t hidden, int x_dtype, int w_dtype,
                                 int* num_partials);
 
 /* Backward of pt_rmsnorm_fwd. With r = rsqrt(mean(x^2) + eps) (read from `rstd` when it
  * is not NULL, else recomputed from x) and g = dy * weight:
  *   dx = r * (g - x * r^2 * mean(g * x))              (written in the x dtype)
- *   dw_partials[p, :] = sum over the rows that CTA p owns of dy * x * r   (fp32)
+ *   dw_partials[p, :] + dw_partials[G + p, :] = sum over the rows that CTA p owns of
+ *   dy * x * r, as an fp32 (sum, accumulated rounding error) pair, G = num_partials / 2
+ *   CTAs (an odd last row is written as zeros; num_partials == 1 gives one CTA whose
+ *   rounded total fills row 0).
  * dw_partials is caller-owned scratch of num_partials * hidden floats; every element is
  * written. Reduce it with pt_rmsnorm_dw_reduce. Deterministic for fixed num_partials.
  * dy has the x dtype. Replaces _RMSNormAutogradFunction.backward

@@ -189,44 +189,45 @@ struct RingPos {
   }
 };
 
-// Compensated accumulation of p * (rh + rl) into (sum, comp) on the FP32 pipe, with p
-// exact and r = rh + rl to about 48 bits. The product's rounding error is recovered
-// exactly with an fma (t + e == p * rh), the low part of r is folded into e, and the sum
-// uses Kahan compensation (comp carries minus the lost low-order part), so the result is
-// the exact sum of the terms up to a few ulp of |sum| regardless of how many terms are
-// added. The _rn intrinsics keep the compiler from contracting the error terms.
-__device__ __forceinline__ void kahan_fma_acc(float& sum, float& comp, float p, float rh,
-                                              float rl) {
-  const float t = __fmul_rn(p, rh);
-  float e = fmaf(p, rh, -t);  // exact: p * rh - t
-  e = fmaf(p, rl, e);
-  const float y = __fsub_rn(t, __fsub_rn(comp, e));
-  const float s = __fadd_rn(sum, y);
-  comp = __fsub_rn(__fsub_rn(s, sum), y);
+// Paired FP32 subtraction, a - b on both lanes (sm_100 f32x2 form, round to nearest).
+__device__ __forceinline__ float2 fsub2_rn(float2 a, float2 b) {
+  unsigned long long d;
+  asm("sub.rn.f32x2 %0, %1, %2;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<const unsigned long long*>(&a)),
+        "l"(*reinterpret_cast<const unsigned long long*>(&b)));
+  return *reinterpret_cast<const float2*>(&d);
+}
+
+// Doubly compensated summation ("Sum2": Knuth's TwoSum error-free transformation with the
+// errors gathered in a second accumulator). Each addition sum + t is split exactly into its
+// rounded value s and its rounding error e, whatever the magnitudes of sum and t; the errors
+// are summed in err, whose own rounding is second order. sum + err therefore carries the
+// exact sum to about twice fp32 precision however many terms are added and however much they
+// cancel (plain Kahan summation, by contrast, still loses up to one ulp of every term). The
+// _rn intrinsics keep the compiler from reassociating or contracting the error terms.
+__device__ __forceinline__ void sum2_add(float& sum, float& err, float t) {
+  const float s = __fadd_rn(sum, t);
+  const float z = __fsub_rn(s, sum);
+  const float e = __fadd_rn(__fsub_rn(sum, __fsub_rn(s, z)), __fsub_rn(t, z));
+  err = __fadd_rn(err, e);
   sum = s;
 }
 
-// Paired form of kahan_fma_acc on two lanes at once, using sm_100's paired FP32
-// instructions (one instruction per two values). Same arithmetic, same exactness.
-__device__ __forceinline__ void kahan_fma_acc2(float2& sum, float2& comp, float2 p, float2 rh,
-                                               float2 rl) {
+// Paired Sum2 accumulation of p * r on two lanes, with r = rh + rl given as a high part rh
+// and a low part rl (|rl| much smaller than |rh|). kExactHi: p * rh is exact in fp32 (the
+// caller chose rh with few enough significant bits); otherwise its rounding error is
+// recovered with an fma. The small p * rl term goes straight into err.
+template <bool kExactHi>
+__device__ __forceinline__ void sum2_fma_acc2(float2& sum, float2& err, float2 p, float2 rh,
+                                              float2 rl) {
   const float2 t = __fmul2_rn(p, rh);
-  float2 e = __ffma2_rn(p, rh, neg2(t));  // exact: p * rh - t
-  e = __ffma2_rn(p, rl, e);
-  const float2 y = __fadd2_rn(t, neg2(__fadd2_rn(comp, neg2(e))));
-  const float2 s = __fadd2_rn(sum, y);
-  comp = __fadd2_rn(__fadd2_rn(s, neg2(sum)), neg2(y));
+  const float2 s = __fadd2_rn(sum, t);
+  const float2 z = fsub2_rn(s, sum);
+  float2 e = __fadd2_rn(fsub2_rn(sum, fsub2_rn(s, z)), fsub2_rn(t, z));
+  if constexpr (!kExactHi) e = __fadd2_rn(e, __ffma2_rn(p, rh, neg2(t)));  // p * rh - t
+  err = __ffma2_rn(p, rl, __fadd2_rn(err, e));
   sum = s;
-}
-
-// Compensated (Kahan) accumulation: sum + (-comp) tracks the exact running sum; comp
-// carries minus the low-order part lost by each rounded addition. The _rn intrinsics keep
-// the compiler from reassociating or contracting the compensation away.
-__device__ __forceinline__ void kahan_add(float& sum, float& comp, float v) {
-  const float y = __fsub_rn(v, comp);
-  const float t = __fadd_rn(sum, y);
-  comp = __fsub_rn(__fsub_rn(t, sum), y);
-  sum = t;
 }
 
 // ----------------------------------------------------- TMA bulk copies + mbarriers --

@@ -120,7 +120,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32,
                                                   : 1)
 rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_t dys,
            const TW* __restrict__ w, const float* __restrict__ rstd_in, T* __restrict__ out,
-           int64_t os, float* __restrict__ rstd_out, float* __restrict__ partials, int64_t rows,
+           int64_t os, float* __restrict__ rstd_out, float* __restrict__ partials,
+           float* __restrict__ partials_lo, float* __restrict__ zero_row, int64_t rows,
            int nvec, int hidden, int stages, int C, int RW, float hidden_f, float eps) {
   constexpr int V = Vec16<T>::N;
   constexpr int kRowsPerSlot = kBwd ? 2 : 1;
@@ -279,9 +280,12 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
   // staged fp32 copy, leaving the registers to the fp64 dweight accumulators (two CTAs per
   // SM fit only that way).
   float wf[kBwd ? 1 : VPT][V];
-  // Backward: one compensated (sum, comp) pair per element, held as fp32 pairs.
+  // Backward: one doubly compensated (sum, err) pair per element, held as fp32 pairs.
   constexpr int V2 = V / 2;
   float2 acc[kBwd ? VPT : 1][kBwd ? V2 : 1], comp[kBwd ? VPT : 1][kBwd ? V2 : 1];
+  // bf16 inputs: dy * x has at most 16 significant bits, so with r's high part cut to 8
+  // significant bits the product p * r_hi is exact in fp32.
+  constexpr bool kExactHi = std::is_same<T, __nv_bfloat16>::value;
   bool valid[VPT];
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
@@ -335,8 +339,10 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
     } else {
       const double invd = stat_inv[pos.slot];
       const float inv = (float)invd;
-      const float inv_lo = (float)(invd - (double)inv);  // r = inv + inv_lo to ~48 bits
-      const float c = stat_c[pos.slot];
+      // r = r_hi + r_lo to about 48 bits, r_hi with 8 significant bits when kExactHi.
+      const float r_hi = kExactHi ? __uint_as_float(__float_as_uint(inv) & 0xFFFF0000u) : inv;
+      const float r_lo = (float)(invd - (double)r_hi);
+      const float nc = -stat_c[pos.slot];
 #pragma unroll
       for (int k = 0; k < VPT; ++k) {
         if (!valid[k]) continue;
@@ -352,19 +358,20 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
           wv[2 * q] = make_float2(t.x, t.y);
           wv[2 * q + 1] = make_float2(t.z, t.w);
         }
-        const float2 inv2 = splat2(inv), inv_lo2 = splat2(inv_lo), c2 = splat2(c);
+        const float2 inv2 = splat2(inv), rh2 = splat2(r_hi), rl2 = splat2(r_lo),
+                     nc2 = splat2(nc);
 #pragma unroll
         for (int e = 0; e < V2; ++e) {
           // dx = r * (dy * w - x * c)
-          const float2 o = __fmul2_rn(inv2, __ffma2_rn(neg2(fx[e]), c2, __fmul2_rn(fg[e], wv[e])));
+          const float2 o = __fmul2_rn(inv2, __ffma2_rn(fx[e], nc2, __fmul2_rn(fg[e], wv[e])));
           fo[2 * e] = o.x;
           fo[2 * e + 1] = o.y;
           const float2 pxy = __fmul2_rn(fg[e], fx[e]);  // exact for 16-bit inputs
-          kahan_fma_acc2(acc[k][e], comp[k][e], pxy, inv2, inv_lo2);
+          sum2_fma_acc2<kExactHi>(acc[k][e], comp[k][e], pxy, rh2, rl2);
           if constexpr (sizeof(T) == 4) {
             // fp32 inputs: the rounding error of dy * x, recovered exactly, times r.
             const float2 pe = __ffma2_rn(fg[e], fx[e], neg2(pxy));
-            comp[k][e] = __fadd2_rn(comp[k][e], neg2(__fmul2_rn(pe, inv2)));
+            comp[k][e] = __ffma2_rn(pe, rh2, comp[k][e]);
           }
         }
         st_stream(out + row * os + off, pack<T>(fo));
@@ -386,18 +393,31 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
   }
 
   if constexpr (kBwd) {
-    // This CTA's dweight partial row (zeros when it owned no rows).
+    // This CTA's dweight partial rows (zeros when it owned no rows): the running sums in
+    // row blockIdx.x of `partials` and their accumulated errors in row blockIdx.x of
+    // `partials_lo`, or, without a lo row, their fp32-rounded total.
     float* prow = partials + (int64_t)blockIdx.x * hidden;
+    float* lrow = partials_lo != nullptr ? partials_lo + (int64_t)blockIdx.x * hidden : nullptr;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       if (!valid[k]) continue;
-      float4* dst =
-          reinterpret_cast<float4*>(prow + (int64_t)(lane + 32 * (warp + C * k)) * V);
+      const int64_t col = (int64_t)(lane + 32 * (warp + C * k)) * V;
+      float4* dst = reinterpret_cast<float4*>(prow + col);
+      float4* dlo = lrow != nullptr ? reinterpret_cast<float4*>(lrow + col) : nullptr;
+      float4* dz = zero_row != nullptr && blockIdx.x == 0
+                       ? reinterpret_cast<float4*>(zero_row + col) : nullptr;
 #pragma unroll
       for (int q = 0; q < V / 4; ++q) {
-        const float2 a = __fadd2_rn(acc[k][2 * q], neg2(comp[k][2 * q]));
-        const float2 b = __fadd2_rn(acc[k][2 * q + 1], neg2(comp[k][2 * q + 1]));
-        dst[q] = make_float4(a.x, a.y, b.x, b.y);
+        const float2 a = acc[k][2 * q], b = acc[k][2 * q + 1];
+        const float2 ea = comp[k][2 * q], eb = comp[k][2 * q + 1];
+        if (dlo != nullptr) {
+          dst[q] = make_float4(a.x, a.y, b.x, b.y);
+          dlo[q] = make_float4(ea.x, ea.y, eb.x, eb.y);
+        } else {
+          const float2 ta = __fadd2_rn(a, ea), tb = __fadd2_rn(b, eb);
+          dst[q] = make_float4(ta.x, ta.y, tb.x, tb.y);
+        }
+        if (dz != nullptr) dz[q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       }
     }
   }
@@ -432,12 +452,22 @@ __global__ void __launch_bounds__(kGenericThreads)
 rmsnorm_bwd_generic(const T* __restrict__ dy, int64_t dys, const T* __restrict__ x, int64_t xs,
                     const TW* __restrict__ w, const float* __restrict__ rstd,
                     T* __restrict__ dx, int64_t dxs, float* __restrict__ partials,
-                    int64_t rows, int hidden, float eps) {
+                    float* __restrict__ partials_lo, float* __restrict__ zero_row, int64_t rows,
+                    int hidden, float eps) {
   __shared__ float red[4][32];
   // Each thread only ever touches the partial columns c = threadIdx.x + k * blockDim.x of
-  // this CTA's partial row, so no barrier is needed around the accumulation.
+  // this CTA's partial rows, so no barrier is needed around the accumulation. The sums
+  // (prow) and their Sum2 errors (lrow) accumulate in place; without an error row they are
+  // folded together at the end.
   float* prow = partials + (int64_t)blockIdx.x * hidden;
-  for (int c = threadIdx.x; c < hidden; c += blockDim.x) prow[c] = 0.0f;
+  float* lrow = partials_lo != nullptr ? partials_lo + (int64_t)blockIdx.x * hidden : nullptr;
+  for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
+    prow[c] = 0.0f;
+    if (lrow != nullptr) lrow[c] = 0.0f;
+  }
+  if (zero_row != nullptr && blockIdx.x == 0)
+    for (int c = threadIdx.x; c < hidden; c += blockDim.x) zero_row[c] = 0.0f;
+  float* erow = lrow;
   int p = 0;
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const T* xr = x + row * xs;
@@ -448,12 +478,15 @@ rmsnorm_bwd_generic(const T* __restrict__ dy, int64_t dys, const T* __restrict__
       ss = fmaf(fx, fx, ss);
       dot = fmaf(to_float(gr[c]) * to_float(w[c]), fx, dot);
     }
-    float inv;
+    double invd;
     if (rstd != nullptr) {
-      inv = rstd[row];
+      invd = (double)rstd[row];
     } else {
-      inv = rsqrtf(block_sum_nosync(ss, red[2 * p]) / (float)hidden + eps);
+      invd = rsqrt_refined((double)block_sum_nosync(ss, red[2 * p]) / (double)hidden +
+                           (double)eps);
     }
+    const float inv = (float)invd;
+    const float inv_lo = (float)(invd - (double)inv);
     const float dot_mean = block_sum_nosync(dot, red[2 * p + 1]) / (float)hidden;
     const float cc = (inv * inv) * dot_mean;
     T* dr = dx + row * dxs;
@@ -461,7 +494,17 @@ rmsnorm_bwd_generic(const T* __restrict__ dy, int64_t dys, const T* __restrict__
       const float fx = to_float(xr[c]);
       const float fg = to_float(gr[c]);
       dr[c] = from_float<T>(inv * (fg * to_float(w[c]) - fx * cc));
-      prow[c] = fmaf(fg * fx, inv, prow[c]);
+      const float pxy = __fmul_rn(fg, fx);
+      const float t = __fmul_rn(pxy, inv);
+      // Low-order parts: the rounding of p * inv, p * inv_lo and (fp32 inputs) of dy * x.
+      float lo = fmaf(pxy, inv_lo, fmaf(pxy, inv, -t));
+      if (sizeof(T) == 4) lo = fmaf(fmaf(fg, fx, -pxy), inv, lo);
+      float sum = prow[c], err = erow != nullptr ? erow[c] : 0.0f;
+      sum2_add(sum, err, t);
+      err = __fadd_rn(err, lo);
+      prow[c] = sum;
+      if (erow != nullptr) erow[c] = err;
+      else prow[c] = __fadd_rn(sum, err);
     }
     p ^= 1;
   }
@@ -475,11 +518,11 @@ __global__ void __launch_bounds__(kReduceWarps * 32)
 rmsnorm_dw_reduce_kernel(const float* __restrict__ partials, int num_partials, int64_t hidden,
                          TW* __restrict__ dw) {
   // 32 columns per CTA (one per lane). Warp w sums the partial rows p = w*U + u + i*W*U
-  // (u < U) into U independent compensated fp32 accumulators, in increasing i; the U
-  // compensated sums are combined in fp64, the W warp sums are added in fp64 in warp
-  // order, and the result is rounded once. The order depends only on num_partials, so the
-  // result is deterministic, and the compensation keeps it correctly rounded in practice
-  // even when the partials cancel.
+  // (u < U) into U independent doubly compensated (Sum2) fp32 accumulators, in increasing
+  // i; the U (sum, error) pairs are combined in fp64, the W warp sums are added in fp64 in
+  // warp order, and the result is rounded once. The order depends only on num_partials, so
+  // the result is deterministic, and Sum2 keeps it correctly rounded in practice even when
+  // the partials cancel.
   __shared__ double s[kReduceWarps][33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t c = (int64_t)blockIdx.x * 32 + lane;
@@ -493,12 +536,12 @@ rmsnorm_dw_reduce_kernel(const float* __restrict__ partials, int num_partials, i
       for (int u = 0; u < kReduceUnroll; ++u)
         v[u] = p0 + u < num_partials ? partials[(int64_t)(p0 + u) * hidden + c] : 0.0f;
 #pragma unroll
-      for (int u = 0; u < kReduceUnroll; ++u) kahan_add(acc[u], comp[u], v[u]);
+      for (int u = 0; u < kReduceUnroll; ++u) sum2_add(acc[u], comp[u], v[u]);
     }
   }
   double t = 0.0;
 #pragma unroll
-  for (int u = 0; u < kReduceUnroll; ++u) t += (double)acc[u] - (double)comp[u];
+  for (int u = 0; u < kReduceUnroll; ++u) t += (double)acc[u] + (double)comp[u];
   s[warp][lane] = t;
   __syncthreads();
   if (warp == 0 && c < hidden) {
@@ -646,13 +689,14 @@ const void* ws_kernel(const FastPlan& plan) {
 template <typename T, typename TW, bool kBwd, bool kHasRstd>
 void ws_launch(const FastPlan& plan, int grid, cudaStream_t stream, const T* x, int64_t xs,
                const T* dy, int64_t dys, const TW* w, const float* rstd_in, T* out, int64_t os,
-               float* rstd_out, float* partials, int64_t rows, int hidden, float eps) {
+               float* rstd_out, float* partials, float* partials_lo, float* zero_row,
+               int64_t rows, int hidden, float eps) {
   constexpr int SW = small_warps<kBwd>();
   const int threads = ws_threads(plan);
   const float hf = (float)hidden;
 #define PT_WS_ARGS                                                                         \
-  x, xs, dy, dys, w, rstd_in, out, os, rstd_out, partials, rows, plan.nvec, hidden,        \
-      plan.stages, plan.consumers, plan.reducers, hf, eps
+  x, xs, dy, dys, w, rstd_in, out, os, rstd_out, partials, partials_lo, zero_row, rows,    \
+      plan.nvec, hidden, plan.stages, plan.consumers, plan.reducers, hf, eps
   if (plan.consumers > kSmallConsumers(kBwd))
     PT_WS((vpt_max<T, kBwd>()), kBigWarps)<<<grid, threads, plan.smem, stream>>>(PT_WS_ARGS);
   else if (plan.vpt == vpt_max<T, kBwd>())
@@ -685,7 +729,7 @@ int fwd_impl(const void* x_, int64_t xs, const void* w_, void* y_, int64_t ys, f
     const int64_t resident = (int64_t)sms * occ;
     const int grid = (int)(rows < resident ? rows : resident);
     ws_launch<T, TW, false, false>(plan, grid, stream, x, xs, nullptr, 0, w, nullptr, y, ys, rstd,
-                                   nullptr, rows, (int)hidden, eps);
+                                   nullptr, nullptr, nullptr, rows, (int)hidden, eps);
   } else {
     const void* fn = (const void*)rmsnorm_fwd_generic<T, TW>;
     const int64_t resident = (int64_t)sms * std::max(1, blocks_per_sm(fn, kGenericThreads, 0));
@@ -714,8 +758,24 @@ int num_partials_impl(int64_t rows, int64_t hidden, int* out) {
   }
   if (rows < n) n = rows;
   if (n < 1) n = 1;
-  *out = (int)n;
+  *out = (int)(2 * n);  // a sum row and an error row per CTA
   return ok();
+}
+
+// How the backward lays its CTAs over a caller's [num_partials, hidden] partial buffer:
+// CTA b writes its running sums to row b and their accumulated errors to row G + b
+// (G = num_partials / 2 CTAs); an odd last row is zeroed. A single row holds one CTA's
+// rounded total.
+struct PartialLayout {
+  int grid;
+  float* lo;
+  float* zero_row;
+};
+PartialLayout partial_layout(float* partials, int num_partials, int64_t hidden) {
+  if (num_partials < 2) return {1, nullptr, nullptr};
+  const int g = num_partials / 2;
+  return {g, partials + (int64_t)g * hidden,
+          (num_partials & 1) ? partials + (int64_t)2 * g * hidden : nullptr};
 }
 
 template <typename T, typename TW>
@@ -735,16 +795,20 @@ int bwd_impl(const void* dy_, int64_t dys, const void* x_, int64_t xs, const voi
                         : ws_kernel<T, TW, true, false>(plan);
     fast = blocks_per_sm(fn, ws_threads(plan), plan.smem) > 0;
   }
+  const PartialLayout lay = partial_layout(partials, num_partials, hidden);
   if (fast) {
     if (hr)
-      ws_launch<T, TW, true, true>(plan, num_partials, stream, x, xs, dy, dys, w, rstd, dx, dxs,
-                                   nullptr, partials, rows, (int)hidden, eps);
+      ws_launch<T, TW, true, true>(plan, lay.grid, stream, x, xs, dy, dys, w, rstd, dx, dxs,
+                                   nullptr, partials, lay.lo, lay.zero_row, rows, (int)hidden,
+                                   eps);
     else
-      ws_launch<T, TW, true, false>(plan, num_partials, stream, x, xs, dy, dys, w, nullptr, dx,
-                                    dxs, nullptr, partials, rows, (int)hidden, eps);
+      ws_launch<T, TW, true, false>(plan, lay.grid, stream, x, xs, dy, dys, w, nullptr, dx, dxs,
+                                    nullptr, partials, lay.lo, lay.zero_row, rows, (int)hidden,
+                                    eps);
   } else {
-    rmsnorm_bwd_generic<T, TW><<<num_partials, kGenericThreads, 0, stream>>>(
-        dy, dys, x, xs, w, rstd, dx, dxs, partials, rows, (int)hidden, eps);
+    rmsnorm_bwd_generic<T, TW><<<lay.grid, kGenericThreads, 0, stream>>>(
+        dy, dys, x, xs, w, rstd, dx, dxs, partials, lay.lo, lay.zero_row, rows, (int)hidden,
+        eps);
   }
   return check_launch("pt_rmsnorm_bwd");
 }
