@@ -336,6 +336,23 @@ class OpWorkload:
             self.bytes = 5 * tokens * HIDDEN * BF16
             self.launches_per_step = 3
             self.dominant = ("rmsnorm_ws (backward)", 3 * tokens * HIDDEN * BF16)
+        elif op == "addnorm":
+            # Fused residual add + RMSNorm (the next-step row): h = res + branch, y = norm(h);
+            # backward dx = norm_bwd(dy, h) + dh. Config 2 shapes and distributions.
+            mk = lambda: [torch.randn((tokens, HIDDEN), generator=gen, device=device, dtype=bf)
+                          for _ in range(sets)]
+            self.res, self.br, self.dy, self.dhs = mk(), mk(), mk(), mk()
+            self.w = 1 + 0.02 * torch.randn(HIDDEN, generator=gen, device=device)
+            self.h = [torch.empty((tokens, HIDDEN), device=device, dtype=bf) for _ in range(sets)]
+            self.y = torch.empty((tokens, HIDDEN), device=device, dtype=bf)
+            self.dx = torch.empty_like(self.y)
+            self.dw = torch.empty(HIDDEN, device=device)
+            self.P = _capi.add_rmsnorm_bwd_num_partials(tokens, HIDDEN, _capi.PT_BFLOAT16,
+                                                        _capi.PT_FLOAT32)
+            self.part = torch.empty((self.P, HIDDEN), device=device)
+            self.bytes = 8 * tokens * HIDDEN * BF16
+            self.launches_per_step = 3
+            self.dominant = ("rmsnorm_ws (fused add, backward)", 4 * tokens * HIDDEN * BF16)
         elif op == "swiglu":
             mk = lambda scale: [torch.randn((tokens, INTER), generator=gen, device=device, dtype=bf) * scale
                                 for _ in range(sets)]
@@ -364,7 +381,8 @@ class OpWorkload:
             raise SystemExit(f"unknown workload {op}")
         self.i = 0
         self.events_per_step = 1
-        self.traffic_key = {"rmsnorm": "rmsnorm_bwd", "swiglu": "swiglu_bwd", "rope": "rope_fwd"}[op]
+        self.traffic_key = {"rmsnorm": "rmsnorm_bwd", "swiglu": "swiglu_bwd", "rope": "rope_fwd",
+                            "addnorm": "add_rmsnorm_bwd"}[op]
 
     def bytes_per_step(self) -> int:
         return self.bytes
@@ -387,6 +405,20 @@ class OpWorkload:
                                            HIDDEN, self.w.data_ptr(), None, self.dx.data_ptr(),
                                            HIDDEN, self.part.data_ptr(), self.P, T, HIDDEN,
                                            c.PT_BFLOAT16, c.PT_FLOAT32, EPS, stream), "bwd")
+            if ev: ev[1].record()
+            self._check(lib.pt_rmsnorm_dw_reduce(self.part.data_ptr(), self.P, HIDDEN,
+                                                 self.dw.data_ptr(), c.PT_FLOAT32, stream), "red")
+        elif self.op == "addnorm":
+            self._check(lib.pt_add_rmsnorm_fwd(self.res[i].data_ptr(), HIDDEN, self.br[i].data_ptr(),
+                                               HIDDEN, self.w.data_ptr(), self.h[i].data_ptr(),
+                                               HIDDEN, self.y.data_ptr(), HIDDEN, None, T, HIDDEN,
+                                               c.PT_BFLOAT16, c.PT_FLOAT32, EPS, stream), "fwd")
+            if ev: ev[0].record()
+            self._check(lib.pt_add_rmsnorm_bwd(self.dy[i].data_ptr(), HIDDEN, self.dhs[i].data_ptr(),
+                                               HIDDEN, self.h[i].data_ptr(), HIDDEN,
+                                               self.w.data_ptr(), None, self.dx.data_ptr(), HIDDEN,
+                                               self.part.data_ptr(), self.P, T, HIDDEN,
+                                               c.PT_BFLOAT16, c.PT_FLOAT32, EPS, stream), "bwd")
             if ev: ev[1].record()
             self._check(lib.pt_rmsnorm_dw_reduce(self.part.data_ptr(), self.P, HIDDEN,
                                                  self.dw.data_ptr(), c.PT_FLOAT32, stream), "red")
@@ -491,9 +523,11 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tokens", type=int, default=2048)
-    ap.add_argument("--workload", choices=["stack", "rmsnorm", "swiglu", "rope"], default="stack",
-                    help="stack = BASELINE config 5 (the headline); the others are configs 2, 3 "
-                         "and 4, one op forward+backward per step, for per-kernel measurement")
+    ap.add_argument("--workload", choices=["stack", "rmsnorm", "swiglu", "rope", "addnorm"],
+                    default="stack",
+                    help="stack = BASELINE config 5 (the headline); rmsnorm, swiglu, rope are "
+                         "configs 2, 3 and 4, one op forward+backward per step, for per-kernel "
+                         "measurement; addnorm = fused residual add + RMSNorm at config 2 shapes")
     args = ap.parse_args()
     if args.workload != "stack":
         args.no_e2e = True
@@ -505,7 +539,8 @@ def main() -> None:
     names = {"stack": "llama3-8b norm/act stack (BASELINE config 5)",
              "rmsnorm": "RMSNorm fwd+bwd bf16 h4096 (BASELINE config 2)",
              "swiglu": "SwiGLU fwd+bwd bf16 i14336 (BASELINE config 3)",
-             "rope": "RoPE q+k fwd+bwd bf16 (BASELINE config 4)"}
+             "rope": "RoPE q+k fwd+bwd bf16 (BASELINE config 4)",
+             "addnorm": "fused residual add + RMSNorm fwd+bwd bf16 h4096 (config 2 shapes)"}
     config = {
         "workload": names[args.workload],
         "layers": args.layers,

@@ -152,6 +152,49 @@ PT_API int pt_rmsnorm_bwd_noalloc(const void* dy, int64_t dy_row_stride,
                                   int x_dtype, int w_dtype, float eps,
                                   void* stream);
 
+/* ------------------------------------------------- fused residual add + RMSNorm -- */
+
+/* h = residual + branch (fp32 add, rounded to the x dtype, written to h_out) and
+ * y = h * r * weight with r = rsqrt(mean(h^2) + eps) over the stored (rounded) h, in one
+ * pass. Replaces the pair `hidden_states = hidden_states + attention(...)` followed by
+ * `self.mlp_norm(hidden_states)` in DecoderBlock.forward_with_auxiliary_loss
+ * (src/picotron/models/picotron_decoder.py:116-123), and the block output
+ * `hidden_states + mlp_output` followed by the next block's attention_norm: one read of
+ * each input and one write of each output instead of an add pass plus a norm pass.
+ * residual, branch, h_out and y share x_dtype; h_out may be residual itself (in-place
+ * update of the residual stream); y aliases nothing. rstd as in pt_rmsnorm_fwd. */
+PT_API int pt_add_rmsnorm_fwd(const void* residual, int64_t residual_row_stride,
+                              const void* branch, int64_t branch_row_stride,
+                              const void* weight,
+                              void* h_out, int64_t h_row_stride,
+                              void* y, int64_t y_row_stride,
+                              float* rstd,
+                              int64_t rows, int64_t hidden,
+                              int x_dtype, int w_dtype, float eps,
+                              void* stream);
+
+/* Partial rows for pt_add_rmsnorm_bwd (same meaning as pt_rmsnorm_bwd_num_partials). */
+PT_API int pt_add_rmsnorm_bwd_num_partials(int64_t rows, int64_t hidden, int x_dtype,
+                                           int w_dtype, int* num_partials);
+
+/* Backward of pt_add_rmsnorm_fwd: dx = (RMSNorm backward of dy at h, as pt_rmsnorm_bwd) +
+ * dh, rounded once, where dh is the gradient that reaches h through its other use (the
+ * residual stream); dx is the gradient of both residual and branch. dw_partials as in
+ * pt_rmsnorm_bwd (reduce with pt_rmsnorm_dw_reduce). dx may alias dh; dh == NULL means no
+ * other use (plain pt_rmsnorm_bwd). Replaces the autograd of the add + RMSNorm pair at
+ * picotron_decoder.py:116-123 (RMSNorm backward, rmsnorm.py:109-134, then the gradient
+ * accumulation of the residual add). */
+PT_API int pt_add_rmsnorm_bwd(const void* dy, int64_t dy_row_stride,
+                              const void* dh, int64_t dh_row_stride,
+                              const void* h, int64_t h_row_stride,
+                              const void* weight,
+                              const float* rstd,
+                              void* dx, int64_t dx_row_stride,
+                              float* dw_partials, int num_partials,
+                              int64_t rows, int64_t hidden,
+                              int x_dtype, int w_dtype, float eps,
+                              void* stream);
+
 /* Reads and clears this library's device-side error word of the current device
  * (synchronous: waits for the device). *code = 0 means no kernel reported a problem;
  * 1 means a kernel gave up waiting for one of its own TMA copies (after about a second)

@@ -70,6 +70,40 @@ def rms_norm_backward(x: Tensor, weight: Tensor, dy: Tensor, eps: float, mode: s
     return dx.to(dtype=x.dtype), dw.to(dtype=weight.dtype)
 
 
+def add_rms_norm_forward(residual: Tensor, branch: Tensor, weight: Tensor, eps: float,
+                         mode: str = "eager"):
+    """Returns (h, y, inverse_rms) for the residual add followed by RMSNorm.
+
+    The caller restated is DecoderBlock.forward_with_auxiliary_loss
+    (src/picotron/models/picotron_decoder.py:116-123): ``h = residual + branch`` (one PyTorch
+    add in the tensors' dtype, so the fp32 sum rounded once) and then the block's RMSNorm
+    module on h (rms_norm_forward above). h is materialised by the reference in that dtype
+    in both modes; exact evaluates the RMSNorm of that stored h in float64.
+    """
+
+    _check_mode(mode)
+    h = residual + branch
+    y, inv = rms_norm_forward(h, weight, eps, mode)
+    return h, y, inv
+
+
+def add_rms_norm_backward(h: Tensor, weight: Tensor, dy: Tensor, dh: Tensor | None, eps: float,
+                          mode: str = "eager"):
+    """Returns (dx, dweight): the gradient of residual and of branch (they are equal) and
+    of the weight, for the add + RMSNorm pair of picotron_decoder.py:116-123.
+
+    Autograd of the reference: the RMSNorm backward at h (rms_norm_backward above, dx cast to
+    the dtype) plus dh, the gradient reaching h through its other use, accumulated in that
+    dtype. exact: the float64 RMSNorm gradient plus dh, unrounded.
+    """
+
+    _check_mode(mode)
+    dx, dw = rms_norm_backward(h, weight, dy, eps, mode)
+    if dh is not None:
+        dx = dx + (dh.double() if mode == "exact" else dh)
+    return dx, dw
+
+
 # ---------------------------------------------------------------------------- SwiGLU --
 
 

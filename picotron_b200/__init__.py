@@ -23,6 +23,7 @@ from picotron_b200.errors import (
 )
 from picotron_b200.hardware import TritonReport, detect_triton_support, probe_hot_path
 from picotron_b200.kernels import (
+    fused_add_rms_norm,
     rms_norm_with_pytorch_forward,
     swiglu_with_pytorch_forward,
     triton_apply_rotary_embedding,
@@ -39,6 +40,7 @@ from picotron_b200.modules import (
 
 __all__ = [
     "ops",
+    "fused_add_rms_norm",
     "RMSNorm",
     "RotaryEmbedding",
     "SwiGLU",

@@ -64,6 +64,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                 _c_ptr, _c_int, _c_i64, _c_i64, _c_int, _c_int, _c_float,
                                 _c_ptr]),
     "pt_rmsnorm_dw_reduce": (_c_int, [_c_ptr, _c_int, _c_i64, _c_ptr, _c_int, _c_ptr]),
+    "pt_add_rmsnorm_fwd": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64,
+                                    _c_ptr, _c_i64, _c_ptr, _c_i64, _c_i64, _c_int, _c_int,
+                                    _c_float, _c_ptr]),
+    "pt_add_rmsnorm_bwd_num_partials": (_c_int, [_c_i64, _c_i64, _c_int, _c_int,
+                                                 ctypes.POINTER(_c_int)]),
+    "pt_add_rmsnorm_bwd": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr,
+                                    _c_ptr, _c_ptr, _c_i64, _c_ptr, _c_int, _c_i64, _c_i64,
+                                    _c_int, _c_int, _c_float, _c_ptr]),
     "pt_rmsnorm_bwd_noalloc": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_ptr,
                                         _c_i64, _c_ptr, _c_i64, _c_i64, _c_int, _c_int,
                                         _c_float, _c_ptr]),
@@ -211,6 +219,43 @@ def rmsnorm_bwd_noalloc(dy: int, dy_row_stride: int, x: int, x_row_stride: int, 
                                               dx, dx_row_stride, dw, rows, hidden, x_dtype,
                                               w_dtype, eps, stream)
     _check("pt_rmsnorm_bwd_noalloc", status, error_type)
+
+
+def add_rmsnorm_fwd(residual: int, residual_row_stride: int, branch: int,
+                    branch_row_stride: int, weight: int, h_out: int, h_row_stride: int,
+                    y: int, y_row_stride: int, rstd: int | None, rows: int, hidden: int,
+                    x_dtype: int, w_dtype: int, eps: float, stream: int,
+                    error_type: type[Exception] | None = None) -> None:
+    """Fused residual add + RMSNorm forward (see pt_add_rmsnorm_fwd)."""
+
+    status = library().pt_add_rmsnorm_fwd(residual, residual_row_stride, branch,
+                                          branch_row_stride, weight, h_out, h_row_stride, y,
+                                          y_row_stride, rstd, rows, hidden, x_dtype, w_dtype,
+                                          eps, stream)
+    _check("pt_add_rmsnorm_fwd", status, error_type)
+
+
+def add_rmsnorm_bwd_num_partials(rows: int, hidden: int, x_dtype: int, w_dtype: int,
+                                 error_type: type[Exception] | None = None) -> int:
+    out = _c_int(0)
+    status = library().pt_add_rmsnorm_bwd_num_partials(rows, hidden, x_dtype, w_dtype,
+                                                       ctypes.byref(out))
+    _check("pt_add_rmsnorm_bwd_num_partials", status, error_type)
+    return out.value
+
+
+def add_rmsnorm_bwd(dy: int, dy_row_stride: int, dh: int | None, dh_row_stride: int, h: int,
+                    h_row_stride: int, weight: int, rstd: int | None, dx: int,
+                    dx_row_stride: int, dw_partials: int, num_partials: int, rows: int,
+                    hidden: int, x_dtype: int, w_dtype: int, eps: float, stream: int,
+                    error_type: type[Exception] | None = None) -> None:
+    """Fused residual add + RMSNorm backward (see pt_add_rmsnorm_bwd)."""
+
+    status = library().pt_add_rmsnorm_bwd(dy, dy_row_stride, dh, dh_row_stride, h,
+                                          h_row_stride, weight, rstd, dx, dx_row_stride,
+                                          dw_partials, num_partials, rows, hidden, x_dtype,
+                                          w_dtype, eps, stream)
+    _check("pt_add_rmsnorm_bwd", status, error_type)
 
 
 def take_device_error() -> int:

@@ -119,6 +119,16 @@ template <typename T> __device__ __forceinline__ void unpack2(const uint4& v, fl
 __device__ __forceinline__ float2 neg2(float2 a) { return make_float2(-a.x, -a.y); }
 __device__ __forceinline__ float2 splat2(float a) { return make_float2(a, a); }
 
+// Round both lanes to T (nearest even) and widen back: the value a T store would keep.
+template <typename T> __device__ __forceinline__ float2 round2(float2 v);
+template <> __device__ __forceinline__ float2 round2<float>(float2 v) { return v; }
+template <> __device__ __forceinline__ float2 round2<__nv_bfloat16>(float2 v) {
+  return __bfloat1622float2(__float22bfloat162_rn(v));
+}
+template <> __device__ __forceinline__ float2 round2<__half>(float2 v) {
+  return __half22float2(__float22half2_rn(v));
+}
+
 // Pack fp32 values into a 16-byte vector of T with round-to-nearest-even.
 template <typename T> __device__ __forceinline__ uint4 pack(const float* f);
 

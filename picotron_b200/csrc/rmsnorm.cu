@@ -113,7 +113,10 @@ __device__ __forceinline__ void record_timeout() {
 // ------------------------------------------------------------ fast fwd / bwd -------
 // Warp roles: warps [0, C) own columns, warps [C, C + RW) reduce rows, warp C + RW is the
 // TMA producer.
-template <typename T, typename TW, int VPT, bool kBwd, bool kHasRstd, int kMaxWarps>
+// kAdd (fused residual add): the forward normalizes h = x + aux (aux = the branch output,
+// h rounded to T and written to h_out); the backward adds aux (the gradient that reaches h
+// from its other uses) to dx.
+template <typename T, typename TW, int VPT, bool kBwd, bool kHasRstd, bool kAdd, int kMaxWarps>
 __global__ void __launch_bounds__(kMaxWarps * 32,
                                   kMaxWarps <= 16 ? (kBwd ? PT_RMS_MIN_BLOCKS_BWD
                                                           : PT_RMS_MIN_BLOCKS_FWD)
@@ -121,10 +124,14 @@ __global__ void __launch_bounds__(kMaxWarps * 32,
 rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_t dys,
            const TW* __restrict__ w, const float* __restrict__ rstd_in, T* __restrict__ out,
            int64_t os, float* __restrict__ rstd_out, float* __restrict__ partials,
-           float* __restrict__ partials_lo, float* __restrict__ zero_row, int64_t rows,
-           int nvec, int hidden, int stages, int C, int RW, float hidden_f, float eps) {
+           float* __restrict__ partials_lo, float* __restrict__ zero_row,
+           const T* __restrict__ aux, int64_t as, T* __restrict__ h_out, int64_t hs,
+           int64_t rows, int nvec, int hidden, int stages, int C, int RW, float hidden_f,
+           float eps) {
   constexpr int V = Vec16<T>::N;
-  constexpr int kRowsPerSlot = kBwd ? 2 : 1;
+  // Slot layout: x | dy (backward) | aux (kAdd).
+  constexpr int kRowsPerSlot = (kBwd ? 2 : 1) + (kAdd ? 1 : 0);
+  constexpr int kAuxRow = kRowsPerSlot - 1;
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t full[kMaxStages];
   __shared__ __align__(8) uint64_t stats[kMaxStages];
@@ -168,6 +175,7 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
       RingPos pos;
       const T* xr = x + (int64_t)blockIdx.x * xs;
       const T* gr = kBwd ? dy + (int64_t)blockIdx.x * dys : nullptr;
+      const T* ar = kAdd ? aux + (int64_t)blockIdx.x * as : nullptr;
       for (int64_t j = 0; j < n_local; ++j) {
         // The k-th refill of a slot waits for the owners to release use k-1.
         if (j >= stages && !mbar_wait_bounded(&empty[pos.slot], pos.phase ^ 1u)) {
@@ -181,6 +189,10 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
         if constexpr (kBwd) {
           bulk_load(dst + row_elems, gr, row_bytes, &full[pos.slot]);
           gr += G * dys;
+        }
+        if constexpr (kAdd) {
+          bulk_load(dst + kAuxRow * row_elems, ar, row_bytes, &full[pos.slot]);
+          ar += G * as;
         }
         pos.advance(1, stages);
       }
@@ -209,6 +221,13 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
       auto accumulate = [&](int v, int q) {
         float2 fx[V / 2];
         unpack2<T>(lds128(sx + v * V), fx);
+        if constexpr (kAdd && !kBwd) {
+          // h = x + aux, rounded to T as stored in h_out.
+          float2 fa[V / 2];
+          unpack2<T>(lds128(sx + kAuxRow * row_elems + v * V), fa);
+#pragma unroll
+          for (int e = 0; e < V / 2; ++e) fx[e] = round2<T>(__fadd2_rn(fx[e], fa[e]));
+        }
         if constexpr (kBwd) {
           float2 fg[V / 2];
           unpack2<T>(lds128(sx + row_elems + v * V), fg);
@@ -325,6 +344,18 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
         const int off = (lane + 32 * (warp + C * k)) * V;
         float2 f2[V / 2];
         unpack2<T>(lds128(sx + off), f2);
+        if constexpr (kAdd) {
+          float2 fa[V / 2];
+          unpack2<T>(lds128(sx + kAuxRow * row_elems + off), fa);
+          float hf[V];
+#pragma unroll
+          for (int e = 0; e < V / 2; ++e) {
+            f2[e] = round2<T>(__fadd2_rn(f2[e], fa[e]));
+            hf[2 * e] = f2[e].x;
+            hf[2 * e + 1] = f2[e].y;
+          }
+          st_stream(h_out + row * hs + off, pack<T>(hf));
+        }
         float f[V];
         const float2 inv2 = splat2(inv);
 #pragma unroll
@@ -347,10 +378,11 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
       for (int k = 0; k < VPT; ++k) {
         if (!valid[k]) continue;
         const int off = (lane + 32 * (warp + C * k)) * V;
-        float2 fx[V2], fg[V2], wv[V2];
+        float2 fx[V2], fg[V2], wv[V2], fa[kAdd ? V2 : 1];
         float fo[V];
         unpack2<T>(lds128(sx + off), fx);
         unpack2<T>(lds128(sx + row_elems + off), fg);
+        if constexpr (kAdd) unpack2<T>(lds128(sx + kAuxRow * row_elems + off), fa);
         const int vec = lane + 32 * (warp + C * k);
 #pragma unroll
         for (int q = 0; q < kPlanes; ++q) {
@@ -363,7 +395,8 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
 #pragma unroll
         for (int e = 0; e < V2; ++e) {
           // dx = r * (dy * w - x * c)
-          const float2 o = __fmul2_rn(inv2, __ffma2_rn(fx[e], nc2, __fmul2_rn(fg[e], wv[e])));
+          float2 o = __fmul2_rn(inv2, __ffma2_rn(fx[e], nc2, __fmul2_rn(fg[e], wv[e])));
+          if constexpr (kAdd) o = __fadd2_rn(o, fa[e]);
           fo[2 * e] = o.x;
           fo[2 * e + 1] = o.y;
           const float2 pxy = __fmul2_rn(fg[e], fx[e]);  // exact for 16-bit inputs
@@ -426,22 +459,32 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
 // --------------------------------------------------------------- generic paths -----
 template <typename T, typename TW>
 __global__ void __launch_bounds__(kGenericThreads)
-rmsnorm_fwd_generic(const T* __restrict__ x, int64_t xs, const TW* __restrict__ w,
-                    T* __restrict__ y, int64_t ys, float* __restrict__ rstd, int64_t rows,
-                    int hidden, float eps) {
+rmsnorm_fwd_generic(const T* x, int64_t xs, const TW* __restrict__ w, T* __restrict__ y,
+                    int64_t ys, float* __restrict__ rstd, int64_t rows, int hidden, float eps,
+                    const T* aux, int64_t as, T* h_out, int64_t hs) {
+  // With aux (fused residual add) the normalized row is h = x + aux, rounded to T and
+  // written to h_out (which may be x itself: every element is read, then written, by the
+  // same thread) and read back from there.
   __shared__ float red[2][32];
   int p = 0;
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const T* xr = x + row * xs;
+    T* hr = aux != nullptr ? h_out + row * hs : nullptr;
     float ss = 0.0f;
     for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
-      const float f = to_float(xr[c]);
+      float f = to_float(xr[c]);
+      if (aux != nullptr) {
+        const T h = from_float<T>(f + to_float(aux[row * as + c]));
+        hr[c] = h;
+        f = to_float(h);
+      }
       ss = fmaf(f, f, ss);
     }
     const float inv = rsqrtf(block_sum_nosync(ss, red[p]) / (float)hidden + eps);
     T* yr = y + row * ys;
+    const T* src = aux != nullptr ? hr : xr;
     for (int c = threadIdx.x; c < hidden; c += blockDim.x)
-      yr[c] = from_float<T>((to_float(xr[c]) * inv) * to_float(w[c]));
+      yr[c] = from_float<T>((to_float(src[c]) * inv) * to_float(w[c]));
     if (rstd != nullptr && threadIdx.x == 0) rstd[row] = inv;
     p ^= 1;
   }
@@ -451,9 +494,9 @@ template <typename T, typename TW>
 __global__ void __launch_bounds__(kGenericThreads)
 rmsnorm_bwd_generic(const T* __restrict__ dy, int64_t dys, const T* __restrict__ x, int64_t xs,
                     const TW* __restrict__ w, const float* __restrict__ rstd,
-                    T* __restrict__ dx, int64_t dxs, float* __restrict__ partials,
+                    T* dx, int64_t dxs, float* __restrict__ partials,
                     float* __restrict__ partials_lo, float* __restrict__ zero_row, int64_t rows,
-                    int hidden, float eps) {
+                    int hidden, float eps, const T* aux, int64_t as) {
   __shared__ float red[4][32];
   // Each thread only ever touches the partial columns c = threadIdx.x + k * blockDim.x of
   // this CTA's partial rows, so no barrier is needed around the accumulation. The sums
@@ -493,7 +536,9 @@ rmsnorm_bwd_generic(const T* __restrict__ dy, int64_t dys, const T* __restrict__
     for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
       const float fx = to_float(xr[c]);
       const float fg = to_float(gr[c]);
-      dr[c] = from_float<T>(inv * (fg * to_float(w[c]) - fx * cc));
+      float d = inv * (fg * to_float(w[c]) - fx * cc);
+      if (aux != nullptr) d += to_float(aux[row * as + c]);  // may alias dr[c]: read first
+      dr[c] = from_float<T>(d);
       const float pxy = __fmul_rn(fg, fx);
       const float t = __fmul_rn(pxy, inv);
       // Low-order parts: the rounding of p * inv, p * inv_lo and (fp32 inputs) of dy * x.
@@ -626,13 +671,13 @@ template <typename T, bool kBwd> constexpr int vpt_quarter() {
 // with them, and a ring of as many slots as fit in the forward or backward budget (at
 // least kMinStages, a multiple of the reducer count). ok=false when the row needs the
 // generic path.
-template <typename T, bool kBwd>
+template <typename T, bool kBwd, bool kAdd = false>
 FastPlan plan_fast(int64_t hidden) {
   FastPlan plan;
   constexpr int V = Vec16<T>::N;
   if (hidden <= 0 || hidden % V != 0) return plan;
   const int64_t nvec = hidden / V;
-  const int64_t slot_bytes = nvec * 16 * (kBwd ? 2 : 1);
+  const int64_t slot_bytes = nvec * 16 * ((kBwd ? 2 : 1) + (kAdd ? 1 : 0));
   if (slot_bytes > kMaxSlotBytes) return plan;
   const int vmax = vpt_max<T, kBwd>();
   const int64_t consumers = (nvec + 32 * vmax - 1) / (32 * vmax);
@@ -652,7 +697,8 @@ FastPlan plan_fast(int64_t hidden) {
   // stages must be a multiple of the reducer count: then each slot is served by exactly
   // one reducer, which visits it in row order, so no waiter can reach a slot's barrier two
   // phases early (try_wait.parity cannot tell use k from use k - 2).
-  int stages = (int)std::min<int64_t>(kMaxStages, (kBwd ? kSmemBwd : kSmemFwd) / slot_bytes);
+  const int64_t budget = (int64_t)(kBwd ? kSmemBwd : kSmemFwd) * (kAdd ? 3 : 2) / 2;
+  int stages = (int)std::min<int64_t>(kMaxStages, budget / slot_bytes);
   stages = std::max(stages, kMinStages);
   stages = std::max(kReducers, stages / kReducers * kReducers);
   plan.stages = stages;
@@ -670,13 +716,13 @@ bool rows_aligned(const void* p, int64_t stride) {
 // Kernel instance for a plan: CTAs of up to kSmallConsumers consumer warps (rows of up to
 // 4 * 32 * kElemsPerThread elements) use any of the three vectors-per-thread shapes under
 // a 5-warp launch bound; bigger CTAs use the full shape under a 17-warp bound.
-#define PT_WS(VPT_, MAXW_) rmsnorm_ws<T, TW, VPT_, kBwd, kHasRstd, MAXW_>
+#define PT_WS(VPT_, MAXW_) rmsnorm_ws<T, TW, VPT_, kBwd, kHasRstd, kAdd, MAXW_>
 template <bool kBwd> constexpr int small_warps() { return kSmallConsumers(kBwd) + kReducers + 1; }
 constexpr int kBigWarps = kMaxConsumers + kReducers + 1;
 inline int ws_threads(const FastPlan& plan) {
   return (plan.consumers + plan.reducers + 1) * 32;
 }
-template <typename T, typename TW, bool kBwd, bool kHasRstd>
+template <typename T, typename TW, bool kBwd, bool kHasRstd, bool kAdd = false>
 const void* ws_kernel(const FastPlan& plan) {
   constexpr int SW = small_warps<kBwd>();
   if (plan.consumers > kSmallConsumers(kBwd))
@@ -686,17 +732,18 @@ const void* ws_kernel(const FastPlan& plan) {
   return (const void*)PT_WS((vpt_quarter<T, kBwd>()), SW);
 }
 
-template <typename T, typename TW, bool kBwd, bool kHasRstd>
+template <typename T, typename TW, bool kBwd, bool kHasRstd, bool kAdd = false>
 void ws_launch(const FastPlan& plan, int grid, cudaStream_t stream, const T* x, int64_t xs,
                const T* dy, int64_t dys, const TW* w, const float* rstd_in, T* out, int64_t os,
                float* rstd_out, float* partials, float* partials_lo, float* zero_row,
-               int64_t rows, int hidden, float eps) {
+               int64_t rows, int hidden, float eps, const T* aux = nullptr, int64_t as = 0,
+               T* h_out = nullptr, int64_t hs = 0) {
   constexpr int SW = small_warps<kBwd>();
   const int threads = ws_threads(plan);
   const float hf = (float)hidden;
 #define PT_WS_ARGS                                                                         \
-  x, xs, dy, dys, w, rstd_in, out, os, rstd_out, partials, partials_lo, zero_row, rows,    \
-      plan.nvec, hidden, plan.stages, plan.consumers, plan.reducers, hf, eps
+  x, xs, dy, dys, w, rstd_in, out, os, rstd_out, partials, partials_lo, zero_row, aux, as,  \
+      h_out, hs, rows, plan.nvec, hidden, plan.stages, plan.consumers, plan.reducers, hf, eps
   if (plan.consumers > kSmallConsumers(kBwd))
     PT_WS((vpt_max<T, kBwd>()), kBigWarps)<<<grid, threads, plan.smem, stream>>>(PT_WS_ARGS);
   else if (plan.vpt == vpt_max<T, kBwd>())
@@ -709,45 +756,52 @@ void ws_launch(const FastPlan& plan, int grid, cudaStream_t stream, const T* x, 
 }
 #undef PT_WS
 
-template <typename T, typename TW>
+// kAdd: fused residual add (aux = the branch output, h_out = x + aux); see rmsnorm_ws.
+template <typename T, typename TW, bool kAdd = false>
 int fwd_impl(const void* x_, int64_t xs, const void* w_, void* y_, int64_t ys, float* rstd,
-             int64_t rows, int64_t hidden, float eps, cudaStream_t stream) {
+             int64_t rows, int64_t hidden, float eps, cudaStream_t stream,
+             const void* aux_ = nullptr, int64_t as = 0, void* h_out_ = nullptr, int64_t hs = 0) {
   const T* x = static_cast<const T*>(x_);
   const TW* w = static_cast<const TW*>(w_);
   T* y = static_cast<T*>(y_);
+  const T* aux = static_cast<const T*>(aux_);
+  T* h_out = static_cast<T*>(h_out_);
   int dev = 0, sms = 0;
   if (int st = current_device_info(&dev, &sms)) return st;
-  FastPlan plan = plan_fast<T, false>(hidden);
+  FastPlan plan = plan_fast<T, false, kAdd>(hidden);
   bool fast = plan.ok && rows_aligned<T>(x, xs) && rows_aligned<T>(y, ys) && aligned16(w);
+  if (kAdd) fast = fast && rows_aligned<T>(aux, as) && rows_aligned<T>(h_out, hs);
   int occ = 0;
   if (fast) {
-    occ = blocks_per_sm(ws_kernel<T, TW, false, false>(plan), ws_threads(plan),
+    occ = blocks_per_sm(ws_kernel<T, TW, false, false, kAdd>(plan), ws_threads(plan),
                         plan.smem);
     fast = occ > 0;
   }
+  const char* what = kAdd ? "pt_add_rmsnorm_fwd" : "pt_rmsnorm_fwd";
   if (fast) {
     const int64_t resident = (int64_t)sms * occ;
     const int grid = (int)(rows < resident ? rows : resident);
-    ws_launch<T, TW, false, false>(plan, grid, stream, x, xs, nullptr, 0, w, nullptr, y, ys, rstd,
-                                   nullptr, nullptr, nullptr, rows, (int)hidden, eps);
+    ws_launch<T, TW, false, false, kAdd>(plan, grid, stream, x, xs, nullptr, 0, w, nullptr, y,
+                                         ys, rstd, nullptr, nullptr, nullptr, rows, (int)hidden,
+                                         eps, aux, as, h_out, hs);
   } else {
     const void* fn = (const void*)rmsnorm_fwd_generic<T, TW>;
     const int64_t resident = (int64_t)sms * std::max(1, blocks_per_sm(fn, kGenericThreads, 0));
     const int grid = (int)(rows < resident ? rows : resident);
-    rmsnorm_fwd_generic<T, TW><<<grid, kGenericThreads, 0, stream>>>(x, xs, w, y, ys, rstd, rows,
-                                                                     (int)hidden, eps);
+    rmsnorm_fwd_generic<T, TW><<<grid, kGenericThreads, 0, stream>>>(
+        x, xs, w, y, ys, rstd, rows, (int)hidden, eps, aux, as, h_out, hs);
   }
-  return check_launch("pt_rmsnorm_fwd");
+  return check_launch(what);
 }
 
-template <typename T, typename TW>
+template <typename T, typename TW, bool kAdd = false>
 int num_partials_impl(int64_t rows, int64_t hidden, int* out) {
   int dev = 0, sms = 0;
   if (int st = current_device_info(&dev, &sms)) return st;
-  FastPlan plan = plan_fast<T, true>(hidden);
+  FastPlan plan = plan_fast<T, true, kAdd>(hidden);
   int occ = 0;
   if (plan.ok)
-    occ = blocks_per_sm(ws_kernel<T, TW, true, false>(plan), ws_threads(plan),
+    occ = blocks_per_sm(ws_kernel<T, TW, true, false, kAdd>(plan), ws_threads(plan),
                         plan.smem);
   int64_t n;
   if (occ > 0) {
@@ -778,39 +832,43 @@ PartialLayout partial_layout(float* partials, int num_partials, int64_t hidden) 
           (num_partials & 1) ? partials + (int64_t)2 * g * hidden : nullptr};
 }
 
-template <typename T, typename TW>
+// kAdd: dx also receives aux (the gradient reaching h through the residual stream).
+template <typename T, typename TW, bool kAdd = false>
 int bwd_impl(const void* dy_, int64_t dys, const void* x_, int64_t xs, const void* w_,
              const float* rstd, void* dx_, int64_t dxs, float* partials, int num_partials,
-             int64_t rows, int64_t hidden, float eps, cudaStream_t stream) {
+             int64_t rows, int64_t hidden, float eps, cudaStream_t stream,
+             const void* aux_ = nullptr, int64_t as = 0) {
   const T* dy = static_cast<const T*>(dy_);
   const T* x = static_cast<const T*>(x_);
   const TW* w = static_cast<const TW*>(w_);
   T* dx = static_cast<T*>(dx_);
-  FastPlan plan = plan_fast<T, true>(hidden);
+  const T* aux = static_cast<const T*>(aux_);
+  FastPlan plan = plan_fast<T, true, kAdd>(hidden);
   bool fast = plan.ok && rows_aligned<T>(x, xs) && rows_aligned<T>(dy, dys) &&
               rows_aligned<T>(dx, dxs) && aligned16(w) && aligned16(partials);
+  if (kAdd) fast = fast && rows_aligned<T>(aux, as);
   const bool hr = rstd != nullptr;
   if (fast) {
-    const void* fn = hr ? ws_kernel<T, TW, true, true>(plan)
-                        : ws_kernel<T, TW, true, false>(plan);
+    const void* fn = hr ? ws_kernel<T, TW, true, true, kAdd>(plan)
+                        : ws_kernel<T, TW, true, false, kAdd>(plan);
     fast = blocks_per_sm(fn, ws_threads(plan), plan.smem) > 0;
   }
   const PartialLayout lay = partial_layout(partials, num_partials, hidden);
   if (fast) {
     if (hr)
-      ws_launch<T, TW, true, true>(plan, lay.grid, stream, x, xs, dy, dys, w, rstd, dx, dxs,
-                                   nullptr, partials, lay.lo, lay.zero_row, rows, (int)hidden,
-                                   eps);
+      ws_launch<T, TW, true, true, kAdd>(plan, lay.grid, stream, x, xs, dy, dys, w, rstd, dx,
+                                         dxs, nullptr, partials, lay.lo, lay.zero_row, rows,
+                                         (int)hidden, eps, aux, as);
     else
-      ws_launch<T, TW, true, false>(plan, lay.grid, stream, x, xs, dy, dys, w, nullptr, dx, dxs,
-                                    nullptr, partials, lay.lo, lay.zero_row, rows, (int)hidden,
-                                    eps);
+      ws_launch<T, TW, true, false, kAdd>(plan, lay.grid, stream, x, xs, dy, dys, w, nullptr, dx,
+                                          dxs, nullptr, partials, lay.lo, lay.zero_row, rows,
+                                          (int)hidden, eps, aux, as);
   } else {
     rmsnorm_bwd_generic<T, TW><<<lay.grid, kGenericThreads, 0, stream>>>(
         dy, dys, x, xs, w, rstd, dx, dxs, partials, lay.lo, lay.zero_row, rows, (int)hidden,
-        eps);
+        eps, aux, as);
   }
-  return check_launch("pt_rmsnorm_bwd");
+  return check_launch(kAdd ? "pt_add_rmsnorm_bwd" : "pt_rmsnorm_bwd");
 }
 
 // Dispatch on the (x, w) dtype pair. Returns PT_ERR_UNSUPPORTED_DTYPE for pairs that
@@ -908,6 +966,87 @@ int pt_rmsnorm_bwd(const void* dy, int64_t dy_row_stride, const void* x, int64_t
     using TW = std::remove_pointer_t<decltype(tw)>;
     return bwd_impl<T, TW>(dy, dy_row_stride, x, x_row_stride, weight, rstd, dx, dx_row_stride,
                            dw_partials, num_partials, rows, hidden, eps, as_stream(stream));
+  });
+}
+
+int pt_add_rmsnorm_fwd(const void* residual, int64_t residual_row_stride, const void* branch,
+                       int64_t branch_row_stride, const void* weight, void* h_out,
+                       int64_t h_row_stride, void* y, int64_t y_row_stride, float* rstd,
+                       int64_t rows, int64_t hidden, int x_dtype, int w_dtype, float eps,
+                       void* stream) {
+  if (int st = check_shape(rows, hidden)) return st;
+  if (!(eps >= 0.0f)) return set_error(PT_ERR_INVALID_ARGUMENT, "eps must be >= 0");
+  if (rows == 0) return ok();
+  if (int st = check_row_stride(residual_row_stride, hidden, "residual_row_stride")) return st;
+  if (int st = check_row_stride(branch_row_stride, hidden, "branch_row_stride")) return st;
+  if (int st = check_row_stride(h_row_stride, hidden, "h_row_stride")) return st;
+  if (int st = check_row_stride(y_row_stride, hidden, "y_row_stride")) return st;
+  if (int st = check_device_ptr(residual, "residual")) return st;
+  if (int st = check_device_ptr(branch, "branch")) return st;
+  if (int st = check_device_ptr(weight, "weight")) return st;
+  if (int st = check_device_ptr(h_out, "h_out")) return st;
+  if (int st = check_device_ptr(y, "y")) return st;
+  if (rstd)
+    if (int st = check_device_ptr(rstd, "rstd")) return st;
+  if (h_out == branch || y == residual || y == branch || y == h_out)
+    return set_error(PT_ERR_INVALID_ARGUMENT,
+                     "h_out may alias residual only; y must not alias any other buffer");
+  return dispatch_xw(x_dtype, w_dtype, [&](auto* tx, auto* tw) {
+    using T = std::remove_pointer_t<decltype(tx)>;
+    using TW = std::remove_pointer_t<decltype(tw)>;
+    return fwd_impl<T, TW, true>(residual, residual_row_stride, weight, y, y_row_stride, rstd,
+                                 rows, hidden, eps, as_stream(stream), branch, branch_row_stride,
+                                 h_out, h_row_stride);
+  });
+}
+
+int pt_add_rmsnorm_bwd_num_partials(int64_t rows, int64_t hidden, int x_dtype, int w_dtype,
+                                    int* num_partials) {
+  if (num_partials == nullptr)
+    return set_error(PT_ERR_INVALID_ARGUMENT, "num_partials is NULL");
+  if (int st = check_shape(rows, hidden)) return st;
+  return dispatch_xw(x_dtype, w_dtype, [&](auto* tx, auto* tw) {
+    using T = std::remove_pointer_t<decltype(tx)>;
+    using TW = std::remove_pointer_t<decltype(tw)>;
+    return num_partials_impl<T, TW, true>(rows, hidden, num_partials);
+  });
+}
+
+int pt_add_rmsnorm_bwd(const void* dy, int64_t dy_row_stride, const void* dh,
+                       int64_t dh_row_stride, const void* h, int64_t h_row_stride,
+                       const void* weight, const float* rstd, void* dx, int64_t dx_row_stride,
+                       float* dw_partials, int num_partials, int64_t rows, int64_t hidden,
+                       int x_dtype, int w_dtype, float eps, void* stream) {
+  if (dh == nullptr)
+    return pt_rmsnorm_bwd(dy, dy_row_stride, h, h_row_stride, weight, rstd, dx, dx_row_stride,
+                          dw_partials, num_partials, rows, hidden, x_dtype, w_dtype, eps,
+                          stream);
+  if (int st = check_shape(rows, hidden)) return st;
+  if (!(eps >= 0.0f)) return set_error(PT_ERR_INVALID_ARGUMENT, "eps must be >= 0");
+  if (num_partials < 1)
+    return set_error(PT_ERR_INVALID_ARGUMENT, "num_partials must be >= 1 (got %d)", num_partials);
+  if (int st = check_device_ptr(dw_partials, "dw_partials")) return st;
+  if (int st = check_device_ptr(weight, "weight")) return st;
+  if (rows > 0) {
+    if (int st = check_row_stride(dy_row_stride, hidden, "dy_row_stride")) return st;
+    if (int st = check_row_stride(dh_row_stride, hidden, "dh_row_stride")) return st;
+    if (int st = check_row_stride(h_row_stride, hidden, "h_row_stride")) return st;
+    if (int st = check_row_stride(dx_row_stride, hidden, "dx_row_stride")) return st;
+    if (int st = check_device_ptr(dy, "dy")) return st;
+    if (int st = check_device_ptr(dh, "dh")) return st;
+    if (int st = check_device_ptr(h, "h")) return st;
+    if (int st = check_device_ptr(dx, "dx")) return st;
+    if (rstd)
+      if (int st = check_device_ptr(rstd, "rstd")) return st;
+    if (dx == dy || dx == h)
+      return set_error(PT_ERR_INVALID_ARGUMENT, "dx may alias dh only");
+  }
+  return dispatch_xw(x_dtype, w_dtype, [&](auto* tx, auto* tw) {
+    using T = std::remove_pointer_t<decltype(tx)>;
+    using TW = std::remove_pointer_t<decltype(tw)>;
+    return bwd_impl<T, TW, true>(dy, dy_row_stride, h, h_row_stride, weight, rstd, dx,
+                                 dx_row_stride, dw_partials, num_partials, rows, hidden, eps,
+                                 as_stream(stream), dh, dh_row_stride);
   });
 }
 

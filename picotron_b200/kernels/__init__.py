@@ -1,8 +1,8 @@
 """Drop-in replacement of ``picotron.nn.triton_kernels`` for the hot path.
 
 Same public names as the reference package (src/picotron/nn/triton_kernels/__init__.py)
-for RMSNorm, SwiGLU and RoPE, backed by the sm_100a CUDA library instead of Triton. The
-reference's attention, cross-entropy and AdamW kernels are not part of this package.
+for RMSNorm, SwiGLU and RoPE, backed by the sm_100a CUDA library instead of Triton, plus
+``fused_add_rms_norm`` (the decoder block's residual add fused into the following norm).
 """
 
 from picotron_b200.errors import (
@@ -10,12 +10,17 @@ from picotron_b200.errors import (
     TritonRoPEUnavailable,
     TritonSwiGLUUnavailable,
 )
-from picotron_b200.kernels.rmsnorm import rms_norm_with_pytorch_forward, triton_rms_norm
+from picotron_b200.kernels.rmsnorm import (
+    fused_add_rms_norm,
+    rms_norm_with_pytorch_forward,
+    triton_rms_norm,
+)
 from picotron_b200.kernels.rope import triton_apply_rotary_embedding
 from picotron_b200.kernels.swiglu import swiglu_with_pytorch_forward, triton_swiglu
 
 __all__ = [
     "TritonRMSNormUnavailable",
+    "fused_add_rms_norm",
     "TritonRoPEUnavailable",
     "TritonSwiGLUUnavailable",
     "triton_apply_rotary_embedding",

@@ -73,3 +73,20 @@ def rms_norm_with_pytorch_forward(hidden_states: Tensor, weight: Tensor, eps: fl
     """
 
     return _EagerRMSNorm.apply(hidden_states, weight, eps)
+
+
+def fused_add_rms_norm(residual: Tensor, branch: Tensor, weight: Tensor,
+                       eps: float) -> tuple[Tensor, Tensor]:
+    """``h = residual + branch`` and ``y = RMSNorm(h) * weight`` in one sm_100a kernel.
+
+    Replaces the residual add followed by the next norm in the reference decoder block
+    (src/picotron/models/picotron_decoder.py:116-123): returns ``(h, y)`` with the values
+    ``h = residual + branch; y = RMSNorm(h)`` would give (h rounded to the input dtype, as
+    PyTorch stores it), with autograd. residual and branch must share shape and dtype.
+    Raises :class:`TritonRMSNormUnavailable` when the inputs cannot run on this path.
+    """
+
+    _validate(residual, weight)
+    if not isinstance(branch, Tensor) or not branch.is_cuda:
+        raise TritonRMSNormUnavailable("sm_100a fused add + RMSNorm requires CUDA tensors.")
+    return torch.ops.picotron_b200.add_rms_norm(residual, branch, weight, float(eps))

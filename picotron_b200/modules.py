@@ -61,6 +61,22 @@ class RMSNorm(nn.Module):
         normalized = hidden_states * torch.rsqrt(variance + self.eps)
         return normalized * self.weight
 
+    def forward_with_residual(self, residual: Tensor, branch: Tensor) -> tuple[Tensor, Tensor]:
+        """``h = residual + branch`` and ``self(h)``, returned as ``(h, self(h))``.
+
+        The decoder block's residual add followed by this norm
+        (picotron_decoder.py:116-123) as one fused kernel when the kernel path is enabled,
+        the inputs are CUDA tensors and residual and branch share dtype; otherwise the two
+        eager steps.
+        """
+
+        if (self.use_triton_rmsnorm and residual.is_cuda and branch.is_cuda
+                and residual.dtype == branch.dtype and residual.shape == branch.shape):
+            return torch.ops.picotron_b200.add_rms_norm(residual, branch, self.weight,
+                                                        float(self.eps))
+        hidden_states = residual + branch
+        return hidden_states, self(hidden_states)
+
 
 class SwiGLU(nn.Module):
     """Llama-style gated feed-forward network."""

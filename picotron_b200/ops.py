@@ -6,6 +6,9 @@ backward op:
 
 * ``rms_norm(x, weight, eps) -> y``                  (reference rmsnorm.py:87-160)
 * ``rms_norm_backward(dy, x, weight, eps) -> (dx, dweight)``
+* ``add_rms_norm(residual, branch, weight, eps) -> (h, y)``  (reference
+  picotron_decoder.py:116-123: ``h = residual + branch`` then RMSNorm of h, fused)
+* ``add_rms_norm_backward(dy, dh, h, weight, eps) -> (dx, dweight)``
 * ``swiglu(gate, up) -> out``                        (reference swiglu.py:56-101)
 * ``swiglu_backward(dout, gate, up) -> (dgate, dup)``
 * ``rope(x, cosine, sine, layout) -> out``           (reference nn/rope.py:35-51)
@@ -205,6 +208,100 @@ def _rms_backward(ctx, grad: Tensor):
 
 
 rms_norm.register_autograd(_rms_backward, setup_context=_rms_setup)
+
+
+def _validate_add_rms(residual: Tensor, branch: Tensor, weight: Tensor) -> int:
+    hidden = _validate_rms(residual, weight)
+    if branch.device != residual.device:
+        raise TritonRMSNormUnavailable("residual and branch must be on the same device.")
+    if branch.shape != residual.shape or branch.dtype != residual.dtype:
+        raise TritonRMSNormUnavailable(
+            "fused add + RMSNorm requires residual and branch of the same shape and dtype.")
+    return hidden
+
+
+@torch.library.custom_op("picotron_b200::add_rms_norm", mutates_args=())
+def add_rms_norm(residual: Tensor, branch: Tensor, weight: Tensor,
+                 eps: float) -> tuple[Tensor, Tensor]:
+    hidden = _validate_add_rms(residual, branch, weight)
+    w = _rms_weight(residual, weight)
+    h = torch.empty(residual.shape, dtype=residual.dtype, device=residual.device)
+    y = torch.empty(residual.shape, dtype=residual.dtype, device=residual.device)
+    if residual.numel() == 0:
+        return h, y
+    rr, br = _as_rows(residual, hidden), _as_rows(branch, hidden)
+    hr, yr = h.view(-1, hidden), y.view(-1, hidden)
+    with _OnDevice(residual.device):
+        _capi.add_rmsnorm_fwd(
+            rr.data_ptr(), rr.stride(0), br.data_ptr(), br.stride(0), w.data_ptr(),
+            hr.data_ptr(), hr.stride(0), yr.data_ptr(), yr.stride(0), None, rr.size(0), hidden,
+            DTYPE_CODES[residual.dtype], DTYPE_CODES[w.dtype], float(eps),
+            _stream(residual.device), TritonRMSNormUnavailable,
+        )
+    return h, y
+
+
+@add_rms_norm.register_fake
+def _add_rms_norm_fake(residual: Tensor, branch: Tensor, weight: Tensor, eps: float):
+    return (torch.empty(residual.shape, dtype=residual.dtype, device=residual.device),
+            torch.empty(residual.shape, dtype=residual.dtype, device=residual.device))
+
+
+@torch.library.custom_op("picotron_b200::add_rms_norm_backward", mutates_args=())
+def add_rms_norm_backward(dy: Tensor, dh: Tensor | None, h: Tensor, weight: Tensor,
+                          eps: float) -> tuple[Tensor, Tensor]:
+    hidden = _validate_rms(h, weight)
+    if dy.shape != h.shape or (dh is not None and dh.shape != h.shape):
+        raise TritonRMSNormUnavailable("fused add + RMSNorm gradients must have h's shape.")
+    if dy.dtype != h.dtype:
+        dy = dy.to(h.dtype)
+    if dh is not None and dh.dtype != h.dtype:
+        dh = dh.to(h.dtype)
+    w = _rms_weight(h, weight)
+    dx = torch.empty(h.shape, dtype=h.dtype, device=h.device)
+    dw = torch.empty(weight.shape, dtype=weight.dtype, device=h.device)
+    hr, dyr, dxr = _as_rows(h, hidden), _as_rows(dy, hidden), dx.view(-1, hidden)
+    dhr = _as_rows(dh, hidden) if dh is not None else None
+    rows = hr.size(0)
+    x_code, w_code = DTYPE_CODES[h.dtype], DTYPE_CODES[w.dtype]
+    with _OnDevice(h.device):
+        stream = _stream(h.device)
+        num_partials = _capi.add_rmsnorm_bwd_num_partials(rows, hidden, x_code, w_code,
+                                                          TritonRMSNormUnavailable)
+        partials = torch.empty((num_partials, hidden), dtype=torch.float32, device=h.device)
+        _capi.add_rmsnorm_bwd(
+            dyr.data_ptr(), dyr.stride(0), dhr.data_ptr() if dhr is not None else None,
+            dhr.stride(0) if dhr is not None else 0, hr.data_ptr(), hr.stride(0), w.data_ptr(),
+            None, dxr.data_ptr(), dxr.stride(0), partials.data_ptr(), num_partials, rows,
+            hidden, x_code, w_code, float(eps), stream, TritonRMSNormUnavailable,
+        )
+        _capi.rmsnorm_dw_reduce(partials.data_ptr(), num_partials, hidden, dw.data_ptr(),
+                                DTYPE_CODES[dw.dtype], stream, TritonRMSNormUnavailable)
+    return dx, dw
+
+
+@add_rms_norm_backward.register_fake
+def _add_rms_norm_backward_fake(dy, dh, h, weight, eps):
+    return (torch.empty(h.shape, dtype=h.dtype, device=h.device),
+            torch.empty(weight.shape, dtype=weight.dtype, device=h.device))
+
+
+def _add_rms_setup(ctx, inputs, output) -> None:
+    _, _, weight, eps = inputs
+    h, _ = output
+    ctx.save_for_backward(h, weight)
+    ctx.eps = eps
+
+
+def _add_rms_backward(ctx, grad_h, grad_y):
+    h, weight = ctx.saved_tensors
+    if grad_y is None:
+        grad_y = torch.zeros_like(h)
+    dx, dw = torch.ops.picotron_b200.add_rms_norm_backward(grad_y, grad_h, h, weight, ctx.eps)
+    return dx, dx, dw, None
+
+
+add_rms_norm.register_autograd(_add_rms_backward, setup_context=_add_rms_setup)
 
 
 # ---------------------------------------------------------------------------- SwiGLU --

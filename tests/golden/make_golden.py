@@ -44,6 +44,21 @@ def _rms(ref, x, w, dy, eps):
     return {"y": y.detach(), "dx": xg.grad, "dw": wg.grad}
 
 
+def _add_rms(ref, residual, branch, w, dy, dh, eps):
+    """The decoder block's residual add followed by the norm (picotron_decoder.py:116-123),
+    with the reference's RMSNorm autograd function; dh is the gradient reaching h through
+    its other use (the residual stream)."""
+
+    rg = residual.clone().requires_grad_(True)
+    bg = branch.clone().requires_grad_(True)
+    wg = w.clone().requires_grad_(True)
+    h = rg + bg
+    y = ref.rms_norm_with_pytorch_forward(h, wg, eps)
+    torch.autograd.backward([y, h], [dy, dh])
+    return {"h": h.detach(), "y": y.detach(), "dresidual": rg.grad, "dbranch": bg.grad,
+            "dw": wg.grad}
+
+
 def _swiglu(ref, g, u, dy):
     gg = g.clone().requires_grad_(True)
     ug = u.clone().requires_grad_(True)
@@ -126,6 +141,19 @@ def main() -> None:
     res = _rms(rms_ref, x, wf, dy, 1e-5)
     written.append(golden_io.save("rmsnorm_bf16_wf32", {"x": x, "w": wf, "dy": dy, **res},
                                   {"eps": 1e-5, "seed": 0}))
+
+    # Fused residual add + RMSNorm (the next-step row of the hot path), config 2 family,
+    # bf16: residual, branch, dy, dh [8, 4096] ~ N(0,1), gamma = 1 + 0.02 N(0,1) in fp32.
+    g = _gen(3)
+    residual = torch.randn(8, 4096, generator=g).to(torch.bfloat16)
+    branch = torch.randn(8, 4096, generator=g).to(torch.bfloat16)
+    wf = 1 + 0.02 * torch.randn(4096, generator=g)
+    dy = torch.randn(8, 4096, generator=g).to(torch.bfloat16)
+    dh = torch.randn(8, 4096, generator=g).to(torch.bfloat16)
+    res = _add_rms(rms_ref, residual, branch, wf, dy, dh, 1e-5)
+    written.append(golden_io.save("add_rmsnorm_bf16", {"residual": residual, "branch": branch,
+                                                       "w": wf, "dy": dy, "dh": dh, **res},
+                                  {"eps": 1e-5, "seed": 3}))
 
     # BASELINE config 3 family, bf16: gate, up ~ N(0,1) * 2, dy ~ N(0,1), [16, 1024].
     g = _gen(0)

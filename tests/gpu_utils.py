@@ -90,3 +90,33 @@ def rope(direction: str, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                cos.data_ptr(), sin.data_ptr(), cos.stride(0), code[layout],
                DTYPE_CODES[x.dtype], DTYPE_CODES[cos.dtype], stream())
     return out
+
+
+def add_rmsnorm_fwd(res2d, br2d, w, eps, h_out=None):
+    rows, hidden = res2d.shape
+    h = torch.empty_like(res2d) if h_out is None else h_out
+    y = torch.empty_like(res2d)
+    _capi.add_rmsnorm_fwd(res2d.data_ptr(), res2d.stride(0), br2d.data_ptr(), br2d.stride(0),
+                          w.data_ptr(), h.data_ptr(), h.stride(0), y.data_ptr(), y.stride(0),
+                          None, rows, hidden, DTYPE_CODES[res2d.dtype], DTYPE_CODES[w.dtype],
+                          eps, stream())
+    return h, y
+
+
+def add_rmsnorm_bwd(dy2d, dh2d, h2d, w, eps, num_partials=None, dx_out=None):
+    rows, hidden = h2d.shape
+    xc, wc = DTYPE_CODES[h2d.dtype], DTYPE_CODES[w.dtype]
+    if num_partials is None:
+        num_partials = _capi.add_rmsnorm_bwd_num_partials(rows, hidden, xc, wc)
+    dx = torch.empty_like(h2d) if dx_out is None else dx_out
+    partials = torch.full((num_partials, hidden), float("nan"), dtype=torch.float32,
+                          device=h2d.device)
+    dw = torch.empty(hidden, dtype=w.dtype, device=h2d.device)
+    _capi.add_rmsnorm_bwd(dy2d.data_ptr(), dy2d.stride(0),
+                          dh2d.data_ptr() if dh2d is not None else None,
+                          dh2d.stride(0) if dh2d is not None else 0, h2d.data_ptr(),
+                          h2d.stride(0), w.data_ptr(), None, dx.data_ptr(), dx.stride(0),
+                          partials.data_ptr(), num_partials, rows, hidden, xc, wc, eps, stream())
+    _capi.rmsnorm_dw_reduce(partials.data_ptr(), num_partials, hidden, dw.data_ptr(), wc,
+                            stream())
+    return dx, dw

@@ -63,6 +63,33 @@ def test_rms_norm_fp32_residual_stream():
     assert not norm._triton_fallback_warned
 
 
+def test_fused_add_rms_norm_autograd_matches_two_step_eager():
+    # forward_with_residual == (h = residual + branch, norm(h)) with gradients through both
+    # outputs, as in the decoder block (the residual stream h is used again downstream).
+    shape = (2, 50, 4096)
+    res = gu.randn(shape, 71, torch.bfloat16).requires_grad_(True)
+    br = gu.randn(shape, 72, torch.bfloat16).requires_grad_(True)
+    norm = RMSNorm(4096, eps=1e-5, use_triton_rmsnorm=True).to(gu.DEV)
+    with torch.no_grad():
+        norm.weight.copy_(gu.randn(4096, 73, torch.float32, 0.02, 1.0))
+    h, y = norm.forward_with_residual(res, br)
+    dy = gu.randn(shape, 74, torch.bfloat16)
+    dh = gu.randn(shape, 75, torch.bfloat16)
+    dres, dbr, dw = torch.autograd.grad((y, h), (res, br, norm.weight), (dy, dh))
+    assert torch.equal(h, res.detach() + br.detach())
+    ye, _ = po.rms_norm_forward(h.detach(), norm.weight.detach(), 1e-5, "exact")
+    dxe, dwe = po.add_rms_norm_backward(h.detach(), norm.weight.detach(), dy, dh, 1e-5, "exact")
+    tolerance.assert_close(y, ye, "y")
+    tolerance.assert_close(dres, dxe, "dresidual")
+    tolerance.assert_close(dbr, dxe, "dbranch")
+    tolerance.assert_close(dw, dwe, "dw")
+    # Only y used downstream: the norm gradient alone.
+    h2, y2 = pb.fused_add_rms_norm(res, br, norm.weight, 1e-5)
+    (dres2,) = torch.autograd.grad(y2, (res,), dy)
+    dxe2, _ = po.rms_norm_backward(h2.detach(), norm.weight.detach(), dy, 1e-5, "exact")
+    tolerance.assert_close(dres2, dxe2, "dresidual (y only)")
+
+
 def test_swiglu_op_autograd_and_module():
     mlp = SwiGLU(256, 512, use_triton_swiglu=True).to(gu.DEV).to(torch.bfloat16)
     gate = gu.randn((3, 17, 512), 6, torch.bfloat16, 2.0).requires_grad_(True)

@@ -29,6 +29,7 @@ def test_all_golden_cases_present():
     assert set(golden_io.cases()) == {
         "cfg1_rmsnorm_f32", "cfg1_swiglu_f32", "reftest_rmsnorm_f32", "reftest_swiglu_f64",
         "rmsnorm_bf16", "rmsnorm_bf16_wf32", "swiglu_bf16", "rope_bf16", "rope_f32",
+        "add_rmsnorm_bf16",
     }
 
 
@@ -47,6 +48,25 @@ def test_rmsnorm_oracle_matches_reference(case):
     tolerance.assert_close(t["y"], ye, f"{case} y")
     tolerance.assert_close(t["dx"], dxe, f"{case} dx")
     tolerance.assert_close(t["dw"], dwe, f"{case} dw")
+
+
+def test_add_rmsnorm_oracle_matches_reference():
+    t, meta = golden_io.load("add_rmsnorm_bf16")
+    eps = float(meta["eps"])
+    h, y, _ = po.add_rms_norm_forward(t["residual"], t["branch"], t["w"], eps, "eager")
+    dx, dw = po.add_rms_norm_backward(h, t["w"], t["dy"], t["dh"], eps, "eager")
+    assert torch.equal(h, t["h"]) and torch.equal(y, t["y"])
+    assert torch.equal(dx, t["dresidual"]) and torch.equal(dx, t["dbranch"])
+    assert torch.equal(dw, t["dw"])
+    he, ye, _ = po.add_rms_norm_forward(t["residual"], t["branch"], t["w"], eps, "exact")
+    dxe, dwe = po.add_rms_norm_backward(he, t["w"], t["dy"], t["dh"], eps, "exact")
+    assert torch.equal(he, t["h"])  # h is stored in bf16 by the reference in both modes
+    tolerance.assert_close(t["y"], ye, "add_rmsnorm y")
+    tolerance.assert_close(t["dw"], dwe, "add_rmsnorm dw")
+    # The reference rounds the norm's dx to bf16 before adding dh (two roundings), so near
+    # cancellations it is off by up to a bf16 ulp of the operands: reported, bounded loosely.
+    stats = tolerance.compare(t["dresidual"], dxe)
+    assert stats.max_abs <= 2.0 ** -7 * float(dxe.abs().max())
 
 
 @pytest.mark.parametrize("case", ["cfg1_swiglu_f32", "reftest_swiglu_f64", "swiglu_bf16"])
