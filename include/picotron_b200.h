@@ -216,6 +216,24 @@ PT_API int pt_swiglu_fwd(const void* gate, const void* up, void* out, int64_t n,
 PT_API int pt_swiglu_bwd(const void* dout, const void* gate, const void* up,
                   void* dgate, void* dup, int64_t n, int dtype, void* stream);
 
+/* ------------------------------------------ SwiGLU fused into the gate/up GEMM -- */
+
+/* gate = x @ w_gate^T and up = x @ w_up^T on the tcgen05 tensor cores (fp32 accumulation),
+ * each rounded to `dtype`, and act = gate * sigmoid(gate) * up (fp32 math on the rounded
+ * values, one rounding) written straight from the accumulators: x [m, k], w_gate and w_up
+ * [n, k] (nn.Linear weight layout), act [m, n]; gate_out and up_out [m, n] (row stride
+ * pre_row_stride) receive gate and up for the backward, or are both NULL. All matrices are
+ * row-major with unit column stride and 16-byte-aligned rows: n, k and every row stride must
+ * be multiples of 8. dtype is PT_BFLOAT16 or PT_FLOAT16. Replaces gate_projection,
+ * up_projection and the activation of SwiGLU.forward (src/picotron/nn/feedforward.py:27-43;
+ * activation at :29-42) up to the down projection. */
+PT_API int pt_swiglu_gemm_fwd(const void* x, int64_t x_row_stride,
+                              const void* w_gate, const void* w_up, int64_t w_row_stride,
+                              void* act, int64_t act_row_stride,
+                              void* gate_out, void* up_out, int64_t pre_row_stride,
+                              int64_t m, int64_t n, int64_t k, int dtype,
+                              void* stream);
+
 /* ------------------------------------------------------------------- RoPE -------- */
 
 /* Rotary embedding of a 4-D tensor with logical shape sizes = [B, H, S, D] (the

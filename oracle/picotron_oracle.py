@@ -121,6 +121,22 @@ def swiglu_forward(gate: Tensor, up: Tensor, mode: str = "eager") -> Tensor:
     return F.silu(gate) * up
 
 
+def gate_up_forward(x: Tensor, w_gate: Tensor, w_up: Tensor, mode: str = "eager"):
+    """Returns (gate, up, activated) of SwiGLU.forward up to the down projection (picotron
+    src/picotron/nn/feedforward.py:27-42): gate = gate_projection(x) = x @ w_gate^T,
+    up = up_projection(x) = x @ w_up^T (nn.Linear without bias, in the input dtype),
+    activated = F.silu(gate) * up (swiglu_forward above).
+    exact: the two products and the activation in float64, unrounded."""
+
+    _check_mode(mode)
+    if mode == "exact":
+        xd = x.double()
+        g, u = xd @ w_gate.double().t(), xd @ w_up.double().t()
+        return g, u, swiglu_forward(g, u, "exact")
+    g, u = F.linear(x, w_gate), F.linear(x, w_up)
+    return g, u, swiglu_forward(g, u, "eager")
+
+
 def swiglu_backward(gate: Tensor, up: Tensor, dout: Tensor, mode: str = "eager"):
     """Returns (dgate, dup).
 

@@ -64,6 +64,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                 _c_ptr, _c_int, _c_i64, _c_i64, _c_int, _c_int, _c_float,
                                 _c_ptr]),
     "pt_rmsnorm_dw_reduce": (_c_int, [_c_ptr, _c_int, _c_i64, _c_ptr, _c_int, _c_ptr]),
+    "pt_swiglu_gemm_fwd": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64, _c_ptr, _c_i64,
+                                    _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_int,
+                                    _c_ptr]),
     "pt_add_rmsnorm_fwd": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64,
                                     _c_ptr, _c_i64, _c_ptr, _c_i64, _c_i64, _c_int, _c_int,
                                     _c_float, _c_ptr]),
@@ -256,6 +259,18 @@ def add_rmsnorm_bwd(dy: int, dy_row_stride: int, dh: int | None, dh_row_stride: 
                                           dw_partials, num_partials, rows, hidden, x_dtype,
                                           w_dtype, eps, stream)
     _check("pt_add_rmsnorm_bwd", status, error_type)
+
+
+def swiglu_gemm_fwd(x: int, x_row_stride: int, w_gate: int, w_up: int, w_row_stride: int,
+                    act: int, act_row_stride: int, gate_out: int | None, up_out: int | None,
+                    pre_row_stride: int, m: int, n: int, k: int, dtype: int, stream: int,
+                    error_type: type[Exception] | None = None) -> None:
+    """Fused gate/up GEMM + SwiGLU activation on the tensor cores (pt_swiglu_gemm_fwd)."""
+
+    status = library().pt_swiglu_gemm_fwd(x, x_row_stride, w_gate, w_up, w_row_stride, act,
+                                          act_row_stride, gate_out, up_out, pre_row_stride, m,
+                                          n, k, dtype, stream)
+    _check("pt_swiglu_gemm_fwd", status, error_type)
 
 
 def take_device_error() -> int:

@@ -43,6 +43,9 @@
 
 namespace pt {
 
+// Reads and clears the fused SwiGLU GEMM's device error word (swiglu_gemm.cu).
+int take_gemm_device_error(int* code);
+
 // Device-side error word of this library on each device (0 = none). Kernels that give up
 // on a bounded wait record kDeviceErrWaitTimeout here; pt_take_device_error reads it.
 __device__ int g_device_error = 0;
@@ -1162,7 +1165,9 @@ int pt_take_device_error(int* code) {
                        cudaGetErrorString(e));
     }
   }
-  *code = value;
+  int gemm_value = 0;
+  if (int st = take_gemm_device_error(&gemm_value)) return st;
+  *code = value != 0 ? value : gemm_value;
   return ok();
 }
 

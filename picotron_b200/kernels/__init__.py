@@ -2,7 +2,8 @@
 
 Same public names as the reference package (src/picotron/nn/triton_kernels/__init__.py)
 for RMSNorm, SwiGLU and RoPE, backed by the sm_100a CUDA library instead of Triton, plus
-``fused_add_rms_norm`` (the decoder block's residual add fused into the following norm).
+``fused_add_rms_norm`` (the decoder block's residual add fused into the following norm) and
+``swiglu_gate_up`` (the MLP's gate/up projections with the activation as one tcgen05 GEMM).
 """
 
 from picotron_b200.errors import (
@@ -16,11 +17,16 @@ from picotron_b200.kernels.rmsnorm import (
     triton_rms_norm,
 )
 from picotron_b200.kernels.rope import triton_apply_rotary_embedding
-from picotron_b200.kernels.swiglu import swiglu_with_pytorch_forward, triton_swiglu
+from picotron_b200.kernels.swiglu import (
+    swiglu_gate_up,
+    swiglu_with_pytorch_forward,
+    triton_swiglu,
+)
 
 __all__ = [
     "TritonRMSNormUnavailable",
     "fused_add_rms_norm",
+    "swiglu_gate_up",
     "TritonRoPEUnavailable",
     "TritonSwiGLUUnavailable",
     "triton_apply_rotary_embedding",

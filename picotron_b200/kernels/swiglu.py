@@ -60,3 +60,26 @@ def swiglu_with_pytorch_forward(gate: Tensor, up: Tensor) -> Tensor:
     """
 
     return _EagerSwiGLU.apply(gate, up)
+
+
+def swiglu_gate_up(hidden_states: Tensor, w_gate: Tensor, w_up: Tensor) -> Tensor:
+    """``silu(hidden_states @ w_gate^T) * (hidden_states @ w_up^T)`` as one tensor-core GEMM.
+
+    The gate and up projections of the reference's SwiGLU.forward
+    (src/picotron/nn/feedforward.py:27-42) and the activation, fused: a tcgen05 GEMM whose
+    epilogue applies the activation to the fp32 accumulators (rounded to the input dtype
+    first, as the unfused path stores gate and up). Weights in another dtype are cast to the
+    input's (what autocast does for the reference's nn.Linear). Autograd: the activation
+    backward runs on the sm_100a kernel and the projections' backward on library GEMMs.
+    Raises :class:`TritonSwiGLUUnavailable` when the inputs cannot run on this path.
+    """
+
+    if not hidden_states.is_cuda or not w_gate.is_cuda or not w_up.is_cuda:
+        raise TritonSwiGLUUnavailable("the fused gate/up GEMM requires CUDA tensors.")
+    ops.check_device(hidden_states.device, TritonSwiGLUUnavailable)
+    if w_gate.dtype != hidden_states.dtype:
+        w_gate = w_gate.to(hidden_states.dtype)
+    if w_up.dtype != hidden_states.dtype:
+        w_up = w_up.to(hidden_states.dtype)
+    act, _, _ = torch.ops.picotron_b200.swiglu_gate_up(hidden_states, w_gate, w_up)
+    return act

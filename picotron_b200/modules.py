@@ -89,6 +89,11 @@ class SwiGLU(nn.Module):
         self.up_projection = nn.Linear(hidden_size, intermediate_size, bias=False)
         self.down_projection = nn.Linear(intermediate_size, hidden_size, bias=False)
         self.use_triton_swiglu = use_triton_swiglu
+        # Not in the reference (so not a constructor argument; set it on the module): run
+        # gate_projection, up_projection and the activation as one tcgen05 GEMM with a
+        # SwiGLU epilogue (bf16/fp16 CUDA inputs; otherwise the three-step path below).
+        # Same parameters, so checkpoints are unaffected.
+        self.fuse_gate_up = False
         self._triton_fallback_warned = False
 
     def activation(self, gate: Tensor, up: Tensor) -> Tensor:
@@ -101,9 +106,24 @@ class SwiGLU(nn.Module):
         return F.silu(gate) * up
 
     def forward(self, hidden_states: Tensor) -> Tensor:
+        if (self.fuse_gate_up and hidden_states.is_cuda
+                and self._compute_dtype(hidden_states) in (torch.bfloat16, torch.float16)):
+            dtype = self._compute_dtype(hidden_states)
+            activated = torch.ops.picotron_b200.swiglu_gate_up(
+                hidden_states.to(dtype), self.gate_projection.weight.to(dtype),
+                self.up_projection.weight.to(dtype))[0]
+            return self.down_projection(activated)
         gate = self.gate_projection(hidden_states)
         up = self.up_projection(hidden_states)
         return self.down_projection(self.activation(gate, up))
+
+    @staticmethod
+    def _compute_dtype(hidden_states: Tensor) -> torch.dtype:
+        """The dtype nn.Linear would compute in: the autocast dtype when autocast is on."""
+
+        if torch.is_autocast_enabled("cuda"):
+            return torch.get_autocast_dtype("cuda")
+        return hidden_states.dtype
 
 
 def rotary_cos_sin(

@@ -11,6 +11,8 @@ backward op:
 * ``add_rms_norm_backward(dy, dh, h, weight, eps) -> (dx, dweight)``
 * ``swiglu(gate, up) -> out``                        (reference swiglu.py:56-101)
 * ``swiglu_backward(dout, gate, up) -> (dgate, dup)``
+* ``swiglu_gate_up(x, w_gate, w_up) -> (act, gate, up)``  (reference feedforward.py:27-42:
+  the gate and up projections and the activation as one tcgen05 GEMM with a SwiGLU epilogue)
 * ``rope(x, cosine, sine, layout) -> out``           (reference nn/rope.py:35-51)
 * ``rope_backward(dy, cosine, sine, layout) -> dx``
 
@@ -371,6 +373,77 @@ def _swiglu_bwd(ctx, grad: Tensor):
 
 
 swiglu.register_autograd(_swiglu_bwd, setup_context=_swiglu_setup)
+
+
+def _validate_gate_up(x: Tensor, w_gate: Tensor, w_up: Tensor) -> tuple[int, int]:
+    check_device(x.device, TritonSwiGLUUnavailable)
+    if w_gate.device != x.device or w_up.device != x.device:
+        raise TritonSwiGLUUnavailable("x, w_gate and w_up must be on the same device.")
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        raise TritonSwiGLUUnavailable(
+            f"the fused gate/up GEMM takes bfloat16 or float16 inputs, not {x.dtype}")
+    if w_gate.dtype != x.dtype or w_up.dtype != x.dtype:
+        raise TritonSwiGLUUnavailable("w_gate and w_up must have the dtype of x.")
+    if (x.dim() < 1 or w_gate.dim() != 2 or w_gate.shape != w_up.shape
+            or w_gate.size(1) != x.size(-1)):
+        raise TritonSwiGLUUnavailable("expected x [..., k] and w_gate, w_up [n, k].")
+    return w_gate.size(0), x.size(-1)
+
+
+@torch.library.custom_op("picotron_b200::swiglu_gate_up", mutates_args=())
+def swiglu_gate_up(x: Tensor, w_gate: Tensor, w_up: Tensor) -> tuple[Tensor, Tensor, Tensor]:
+    n, k = _validate_gate_up(x, w_gate, w_up)
+    out_shape = (*x.shape[:-1], n)
+    act = torch.empty(out_shape, dtype=x.dtype, device=x.device)
+    gate = torch.empty(out_shape, dtype=x.dtype, device=x.device)
+    up = torch.empty(out_shape, dtype=x.dtype, device=x.device)
+    if act.numel() == 0:
+        return act, gate, up
+    x2 = _as_rows(x, k)
+    if x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    wg, wu = w_gate.contiguous(), w_up.contiguous()
+    with _OnDevice(x.device):
+        _capi.swiglu_gemm_fwd(
+            x2.data_ptr(), x2.stride(0), wg.data_ptr(), wu.data_ptr(), k, act.data_ptr(), n,
+            gate.data_ptr(), up.data_ptr(), n, x2.size(0), n, k, DTYPE_CODES[x.dtype],
+            _stream(x.device), TritonSwiGLUUnavailable,
+        )
+    return act, gate, up
+
+
+@swiglu_gate_up.register_fake
+def _swiglu_gate_up_fake(x: Tensor, w_gate: Tensor, w_up: Tensor):
+    shape = (*x.shape[:-1], w_gate.size(0))
+    return tuple(torch.empty(shape, dtype=x.dtype, device=x.device) for _ in range(3))
+
+
+def _gate_up_setup(ctx, inputs, output) -> None:
+    x, w_gate, w_up = inputs
+    _, gate, up = output
+    ctx.save_for_backward(x, w_gate, w_up, gate, up)
+    ctx.set_materialize_grads(False)
+
+
+def _gate_up_backward(ctx, d_act, d_gate, d_up):
+    # dgate, dup from the fused activation backward, then the projections' backward as
+    # plain library GEMMs (reference: autograd of the two nn.Linear, feedforward.py:27-28).
+    x, w_gate, w_up, gate, up = ctx.saved_tensors
+    n, k = w_gate.shape
+    if d_act is not None:
+        dg, du = torch.ops.picotron_b200.swiglu_backward(d_act, gate, up)
+    else:
+        dg, du = torch.zeros_like(gate), torch.zeros_like(up)
+    if d_gate is not None:
+        dg = dg + d_gate
+    if d_up is not None:
+        du = du + d_up
+    x2, dg2, du2 = x.reshape(-1, k), dg.reshape(-1, n), du.reshape(-1, n)
+    dx = (dg2 @ w_gate).addmm_(du2, w_up).reshape(x.shape)
+    return dx, dg2.t() @ x2, du2.t() @ x2
+
+
+swiglu_gate_up.register_autograd(_gate_up_backward, setup_context=_gate_up_setup)
 
 
 # ------------------------------------------------------------------------------ RoPE --

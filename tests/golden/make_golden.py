@@ -59,6 +59,18 @@ def _add_rms(ref, residual, branch, w, dy, dh, eps):
             "dw": wg.grad}
 
 
+def _gate_up(ffn_mod, x, hidden, inter, seed):
+    """The reference's SwiGLU module (feedforward.py:13-43) up to its down projection."""
+
+    torch.manual_seed(seed)
+    mlp = ffn_mod.SwiGLU(hidden, inter).to(x.dtype)
+    gate = mlp.gate_projection(x)
+    up = mlp.up_projection(x)
+    activated = torch.nn.functional.silu(gate) * up  # feedforward.py:42
+    return {"w_gate": mlp.gate_projection.weight.detach(), "w_up": mlp.up_projection.weight.detach(),
+            "gate": gate.detach(), "up": up.detach(), "act": activated.detach()}
+
+
 def _swiglu(ref, g, u, dy):
     gg = g.clone().requires_grad_(True)
     ug = u.clone().requires_grad_(True)
@@ -86,6 +98,7 @@ def main() -> None:
     args = parser.parse_args()
     sys.path.insert(0, args.reference_src)
     torch.set_num_threads(1)
+    from picotron.nn import feedforward as ffn_mod
     from picotron.nn import rope as rope_mod
     from picotron.nn.triton_kernels import rmsnorm as rms_ref
     from picotron.nn.triton_kernels import swiglu as swiglu_ref
@@ -154,6 +167,13 @@ def main() -> None:
     written.append(golden_io.save("add_rmsnorm_bf16", {"residual": residual, "branch": branch,
                                                        "w": wf, "dy": dy, "dh": dh, **res},
                                   {"eps": 1e-5, "seed": 3}))
+
+    # SwiGLU MLP up to the down projection (the next-step row: gate/up GEMMs + activation),
+    # bf16, hidden 64, intermediate 128, x [32, 64] ~ N(0,1), the module's own weight init.
+    g = _gen(4)
+    x = torch.randn(32, 64, generator=g).to(torch.bfloat16)
+    res = _gate_up(ffn_mod, x, 64, 128, 4)
+    written.append(golden_io.save("gate_up_bf16", {"x": x, **res}, {"seed": 4}))
 
     # BASELINE config 3 family, bf16: gate, up ~ N(0,1) * 2, dy ~ N(0,1), [16, 1024].
     g = _gen(0)

@@ -120,3 +120,17 @@ def add_rmsnorm_bwd(dy2d, dh2d, h2d, w, eps, num_partials=None, dx_out=None):
     _capi.rmsnorm_dw_reduce(partials.data_ptr(), num_partials, hidden, dw.data_ptr(), wc,
                             stream())
     return dx, dw
+
+
+def swiglu_gemm(x2d, wg, wu, save_preact=True):
+    m, k = x2d.shape
+    n = wg.size(0)
+    act = torch.empty((m, n), dtype=x2d.dtype, device=x2d.device)
+    g = torch.empty_like(act) if save_preact else None
+    u = torch.empty_like(act) if save_preact else None
+    _capi.swiglu_gemm_fwd(x2d.data_ptr(), x2d.stride(0), wg.data_ptr(), wu.data_ptr(),
+                          wg.stride(0), act.data_ptr(), act.stride(0),
+                          g.data_ptr() if save_preact else None,
+                          u.data_ptr() if save_preact else None, n, m, n, k,
+                          DTYPE_CODES[x2d.dtype], stream())
+    return act, g, u

@@ -90,6 +90,31 @@ def test_fused_add_rms_norm_autograd_matches_two_step_eager():
     tolerance.assert_close(dres2, dxe2, "dresidual (y only)")
 
 
+def test_fused_gate_up_module_matches_three_step_path():
+    # SwiGLU with fuse_gate_up (tcgen05 GEMM + activation epilogue) against the same module
+    # run as gate/up Linear + the SwiGLU kernel, forward and backward, under bf16 autocast
+    # with fp32 parameters (the reference's training setup).
+    torch.manual_seed(0)
+    mlp = SwiGLU(512, 1024, use_triton_swiglu=True).to(gu.DEV)
+    x = gu.randn((4, 96, 512), 91, torch.float32).requires_grad_(True)
+    dy = gu.randn((4, 96, 512), 92, torch.bfloat16)
+    grads = []
+    outs = []
+    for fused in (False, True):
+        mlp.fuse_gate_up = fused
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y = mlp(x)
+        outs.append(y.float())
+        grads.append(torch.autograd.grad(y, (x, mlp.gate_projection.weight,
+                                             mlp.up_projection.weight,
+                                             mlp.down_projection.weight), dy))
+    # Same math; only the GEMMs' fp32 summation order differs: compare normwise.
+    for a, b, name in zip((outs[1], *grads[1]), (outs[0], *grads[0]),
+                          ("y", "dx", "dw_gate", "dw_up", "dw_down")):
+        err = (a.float() - b.float()).abs().max().item()
+        assert err <= 2 ** -6 * b.float().abs().max().item(), (name, err)
+
+
 def test_swiglu_op_autograd_and_module():
     mlp = SwiGLU(256, 512, use_triton_swiglu=True).to(gu.DEV).to(torch.bfloat16)
     gate = gu.randn((3, 17, 512), 6, torch.bfloat16, 2.0).requires_grad_(True)

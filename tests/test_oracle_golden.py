@@ -29,7 +29,7 @@ def test_all_golden_cases_present():
     assert set(golden_io.cases()) == {
         "cfg1_rmsnorm_f32", "cfg1_swiglu_f32", "reftest_rmsnorm_f32", "reftest_swiglu_f64",
         "rmsnorm_bf16", "rmsnorm_bf16_wf32", "swiglu_bf16", "rope_bf16", "rope_f32",
-        "add_rmsnorm_bf16",
+        "add_rmsnorm_bf16", "gate_up_bf16",
     }
 
 
@@ -67,6 +67,15 @@ def test_add_rmsnorm_oracle_matches_reference():
     # cancellations it is off by up to a bf16 ulp of the operands: reported, bounded loosely.
     stats = tolerance.compare(t["dresidual"], dxe)
     assert stats.max_abs <= 2.0 ** -7 * float(dxe.abs().max())
+
+
+def test_gate_up_oracle_matches_reference():
+    t, _ = golden_io.load("gate_up_bf16")
+    g, u, act = po.gate_up_forward(t["x"], t["w_gate"], t["w_up"], "eager")
+    assert torch.equal(g, t["gate"]) and torch.equal(u, t["up"]) and torch.equal(act, t["act"])
+    ge, ue, _ = po.gate_up_forward(t["x"], t["w_gate"], t["w_up"], "exact")
+    tolerance.assert_close(t["gate"], ge, "gate_up gate")
+    tolerance.assert_close(t["up"], ue, "gate_up up")
 
 
 @pytest.mark.parametrize("case", ["cfg1_swiglu_f32", "reftest_swiglu_f64", "swiglu_bf16"])
