@@ -46,13 +46,42 @@ BF16 = 2
 # --------------------------------------------------------------------------- helpers --
 
 
-def measured_peaks() -> tuple[float, str]:
+def measured_peaks(key: str = "hbm_gbs") -> tuple[float, str]:
+    """A peak from MEASURED_PEAKS.json (``hbm_gbs`` or ``bf16_tflops``), else the pool's
+    fallback figure."""
+
     path = ROOT / "MEASURED_PEAKS.json"
     try:
         data = json.loads(path.read_text())
-        return float(data["hbm_gbs"]), "measured"
+        return float(data[key]), "measured"
     except Exception:
-        return 6650.0, "fallback"
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}[key], "fallback"
+
+
+def time_library_mlpup(work, stream: int, steps: int) -> float:
+    """ms per step of the unfused path the fused GEMM replaces: two cuBLAS GEMMs (torch
+    matmul) for gate and up, then this library's SwiGLU forward kernel."""
+
+    c = work.capi
+    n = work.tokens * INTER
+
+    def step(i: int) -> None:
+        x = work.x[i % 2]
+        torch.matmul(x, work.wg.t(), out=work.g)
+        torch.matmul(x, work.wu.t(), out=work.u)
+        c.swiglu_fwd(work.g.data_ptr(), work.u.data_ptr(), work.act.data_ptr(), n,
+                     c.PT_BFLOAT16, stream)
+
+    for i in range(3):
+        step(i)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(steps):
+        step(i)
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
 
 
 def dram_traffic_per_launch(kernel: str, tokens: int) -> float | None:
@@ -353,6 +382,20 @@ class OpWorkload:
             self.bytes = 8 * tokens * HIDDEN * BF16
             self.launches_per_step = 3
             self.dominant = ("rmsnorm_ws (fused add, backward)", 4 * tokens * HIDDEN * BF16)
+        elif op == "mlpup":
+            # SwiGLU fused into the gate/up GEMM (the next-step row): x [tokens, 4096] bf16,
+            # w_gate, w_up [14336, 4096] bf16; act, gate and up written (the training forward).
+            k = HIDDEN
+            self.x = [torch.randn((tokens, k), generator=gen, device=device, dtype=bf)
+                      for _ in range(2)]
+            self.wg = torch.randn((INTER, k), generator=gen, device=device, dtype=bf) * 2 * k ** -0.5
+            self.wu = torch.randn((INTER, k), generator=gen, device=device, dtype=bf) * 2 * k ** -0.5
+            self.act = torch.empty((tokens, INTER), device=device, dtype=bf)
+            self.g, self.u = torch.empty_like(self.act), torch.empty_like(self.act)
+            self.flops = 2 * 2 * tokens * INTER * k
+            self.bytes = (tokens * k + 2 * INTER * k + 3 * tokens * INTER) * BF16
+            self.launches_per_step = 1
+            self.dominant = ("swiglu_gemm_kernel", self.flops)
         elif op == "swiglu":
             mk = lambda scale: [torch.randn((tokens, INTER), generator=gen, device=device, dtype=bf) * scale
                                 for _ in range(sets)]
@@ -382,7 +425,7 @@ class OpWorkload:
         self.i = 0
         self.events_per_step = 1
         self.traffic_key = {"rmsnorm": "rmsnorm_bwd", "swiglu": "swiglu_bwd", "rope": "rope_fwd",
-                            "addnorm": "add_rmsnorm_bwd"}[op]
+                            "addnorm": "add_rmsnorm_bwd", "mlpup": "swiglu_gemm"}[op]
 
     def bytes_per_step(self) -> int:
         return self.bytes
@@ -422,6 +465,13 @@ class OpWorkload:
             if ev: ev[1].record()
             self._check(lib.pt_rmsnorm_dw_reduce(self.part.data_ptr(), self.P, HIDDEN,
                                                  self.dw.data_ptr(), c.PT_FLOAT32, stream), "red")
+        elif self.op == "mlpup":
+            if ev: ev[0].record()
+            x = self.x[i % 2]
+            c.swiglu_gemm_fwd(x.data_ptr(), HIDDEN, self.wg.data_ptr(), self.wu.data_ptr(), HIDDEN,
+                              self.act.data_ptr(), INTER, self.g.data_ptr(), self.u.data_ptr(),
+                              INTER, T, INTER, HIDDEN, c.PT_BFLOAT16, stream)
+            if ev: ev[1].record()
         elif self.op == "swiglu":
             n = T * INTER
             self._check(lib.pt_swiglu_fwd(self.g[i].data_ptr(), self.u[i].data_ptr(),
@@ -523,11 +573,12 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tokens", type=int, default=2048)
-    ap.add_argument("--workload", choices=["stack", "rmsnorm", "swiglu", "rope", "addnorm"],
+    ap.add_argument("--workload", choices=["stack", "rmsnorm", "swiglu", "rope", "addnorm", "mlpup"],
                     default="stack",
                     help="stack = BASELINE config 5 (the headline); rmsnorm, swiglu, rope are "
                          "configs 2, 3 and 4, one op forward+backward per step, for per-kernel "
-                         "measurement; addnorm = fused residual add + RMSNorm at config 2 shapes")
+                         "measurement; addnorm = fused residual add + RMSNorm at config 2 shapes; "
+                         "mlpup = the gate/up GEMMs with the SwiGLU epilogue (tcgen05)")
     args = ap.parse_args()
     if args.workload != "stack":
         args.no_e2e = True
@@ -540,7 +591,8 @@ def main() -> None:
              "rmsnorm": "RMSNorm fwd+bwd bf16 h4096 (BASELINE config 2)",
              "swiglu": "SwiGLU fwd+bwd bf16 i14336 (BASELINE config 3)",
              "rope": "RoPE q+k fwd+bwd bf16 (BASELINE config 4)",
-             "addnorm": "fused residual add + RMSNorm fwd+bwd bf16 h4096 (config 2 shapes)"}
+             "addnorm": "fused residual add + RMSNorm fwd+bwd bf16 h4096 (config 2 shapes)",
+             "mlpup": "gate/up GEMMs + SwiGLU epilogue fwd bf16 4096->14336 (config 3/5 shapes)"}
     config = {
         "workload": names[args.workload],
         "layers": args.layers,
@@ -625,6 +677,13 @@ def main() -> None:
     dom_name, dom_bytes = work.dominant
     achieved = dom_bytes / (dom_ms / 1e3) / 1e9
     traffic = dram_traffic_per_launch(work.traffic_key, work.tokens)
+    tensor_bound = args.workload == "mlpup"
+    library_ms = None
+    if tensor_bound:
+        # A tensor-core contraction: FLOPs per launch over the cuBLAS bf16 burst peak.
+        achieved = dom_bytes / (dom_ms / 1e3) / 1e12
+        tpeak, tpeak_kind = measured_peaks("bf16_tflops")
+        library_ms = time_library_mlpup(work, stream, args.steps)
 
     e2e = None
     if not args.no_e2e:
@@ -663,6 +722,23 @@ def main() -> None:
                 "traffic": traffic,
                 "algorithmic_bytes_per_launch": dom_bytes,
                 "mean_launch_us": dom_ms * 1e3,
+            } if not tensor_bound else {
+                "kernel": dom_name,
+                "bound": "tensor",
+                "achieved": achieved,
+                "peak": tpeak,
+                "peak_source": f"{tpeak_kind} bf16_tflops, burst (MEASURED_PEAKS.json)",
+                "unit": "TFLOP/s",
+                "frac": achieved / tpeak,
+                "traffic": traffic,
+                "algorithmic_flops_per_launch": dom_bytes,
+                "mean_launch_us": dom_ms * 1e3,
+            },
+            "library_baseline": None if library_ms is None else {
+                "what": "cuBLAS gate and up GEMMs (torch.matmul) + this library's SwiGLU kernel",
+                "ms_per_step": library_ms,
+                "value": world * work.tokens / (library_ms / 1e3),
+                "unit": "tokens/s",
             },
             "cpu_baseline": cpu,
             "e2e": e2e,

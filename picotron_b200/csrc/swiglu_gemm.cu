@@ -24,6 +24,8 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <set>
+#include <utility>
 
 #include "common.cuh"
 
@@ -33,32 +35,48 @@ __device__ int g_gemm_error = 0;
 
 namespace {
 
-constexpr int kBM = 128;             // tile rows = tensor-memory lanes
+constexpr int kBM = 128;             // rows per CTA = tensor-memory lanes
 constexpr int kBN = 128;             // output columns per tile (gate and up each)
 constexpr int kBK = 64;              // K per stage: one 128-byte swizzle row of 16-bit values
 constexpr int kUmmaK = 16;           // K of one tcgen05.mma for 16-bit inputs
-constexpr int kStages = 4;
-constexpr int kATileBytes = kBM * kBK * 2;          // 16 KB
-constexpr int kBTileBytes = 2 * kBN * kBK * 2;      // 32 KB: gate rows, then up rows
-constexpr int kStageBytes = kATileBytes + kBTileBytes;
+constexpr int kATileBytes = kBM * kBK * 2;          // 16 KB: this CTA's rows of x
+constexpr int kWTileBytes = kBN * kBK * 2;          // 16 KB: one weight tile (gate or up)
 constexpr int kAccCols = 2 * kBN;    // fp32 columns of one accumulator buffer (gate | up)
 constexpr int kTmemCols = 2 * kAccCols;  // double-buffered: 512 columns (all of them)
 constexpr int kThreads = 256;        // warp 0 TMA, 1 MMA, 2 TMEM owner, 3 idle, 4-7 epilogue
 constexpr int kEpiWarp0 = 4;
+constexpr int kEpiWarps = kThreads / 32 - kEpiWarp0;
 constexpr int kGroupM = 16;          // m-tiles per raster group (L2 reuse of the weights)
+constexpr int kMaxStages = 6;
 constexpr long long kWaitCycles = 2000000000LL;  // about one second of SM clock
 
+// Two shapes of the same pipeline:
+//  * single CTA (kPair = false): a 128 x 128 tile per CTA; each stage holds the x tile and
+//    both weight tiles (48 KB), 4 stages; tcgen05.mma cta_group::1 with M = 128, N = 256.
+//  * CTA pair (kPair = true, a cluster of two CTAs on two SMs): a 256 x 128 tile per pair;
+//    each CTA stages its own 128 rows of x and one weight tile (the even CTA the gate rows,
+//    the odd CTA the up rows: 32 KB), 6 stages; the even CTA issues tcgen05.mma cta_group::2
+//    with M = 256, N = 256, which reads both CTAs' shared memory and leaves each CTA's 128
+//    rows of both accumulators in its own tensor memory. Per SM this halves the weight bytes
+//    moved per FLOP, so twice the bytes per SM can be in flight.
+template <bool kPair> struct Shape {
+  static constexpr int kStages = kPair ? 6 : 4;
+  static constexpr int kStageBytes = kATileBytes + (kPair ? 1 : 2) * kWTileBytes;
+  static constexpr int kTileM = kPair ? 2 * kBM : kBM;
+  static constexpr int kCtas = kPair ? 2 : 1;
+  static constexpr int kSmemBytes = 1024 /* alignment slack */ + kStages * kStageBytes + 256;
+};
+static_assert(Shape<false>::kStages <= kMaxStages && Shape<true>::kStages <= kMaxStages, "");
+
 struct GemmBarriers {
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
   uint64_t drain;
   uint32_t tmem_base;
 };
-
-constexpr int kSmemBytes = 1024 /* alignment slack */ + kStages * kStageBytes +
-                           (int)((sizeof(GemmBarriers) + 15) / 16 * 16);
+static_assert(sizeof(GemmBarriers) <= 256, "barrier block must fit its reserved space");
 
 __device__ __forceinline__ void record_gemm_error() {
   atomicExch(&g_gemm_error, kDeviceErrWaitTimeout);
@@ -73,16 +91,53 @@ __device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity) {
   return true;
 }
 
-// 2-D tiled TMA load (no multicast) of box {kBK, rows} at (x = column, y = row) into smem,
-// completing on `bar` with the box's byte count.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Shared::cluster address of the same shared variable in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_addr(p)), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+
+// Arrive (release, cluster scope) on an mbarrier given by its shared::cluster address.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];"
+               :
+               : "r"(cluster_addr)
+               : "memory");
+}
+
+// 2-D tiled TMA load of box {kBK, rows} at (x = column, y = row) into this CTA's shared
+// memory, completing on the mbarrier at shared::cluster address `bar`. kPair: the
+// cta_group::2 form, whose completion may be signalled on the pair's even CTA. No multicast.
+template <bool kPair>
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];"
-      :
-      : "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
-      : "memory");
+                                            uint32_t bar) {
+  if constexpr (kPair) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];"
+        :
+        : "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+  } else {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];"
+        :
+        : "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+  }
 }
 
 // Shared-memory matrix descriptor of a K-major operand tile stored as TMA wrote it with
@@ -104,22 +159,87 @@ template <typename T> constexpr uint32_t instr_desc(int m, int n) {
          ((uint32_t)(m >> 4) << 24);
 }
 
+template <bool kPair>
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                          uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
-      :
-      : "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
+  if constexpr (kPair) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+        :
+        : "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+        :
+        : "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  }
 }
 
-// Arrive once on `bar` when every tcgen05.mma this thread issued before has completed.
+// Arrive once on `bar` (in this CTA, and for kPair also at the same offset in the peer CTA)
+// when every tcgen05.mma this thread issued before has completed.
+template <bool kPair>
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-               :
-               : "r"(smem_addr(bar))
-               : "memory");
+  if constexpr (kPair) {
+    const uint16_t both = 0x3;
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+        " [%0], %1;"
+        :
+        : "r"(smem_addr(bar)), "h"(both)
+        : "memory");
+  } else {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :
+                 : "r"(smem_addr(bar))
+                 : "memory");
+  }
+}
+
+// Commit to this CTA's barrier only (the drain before tensor memory is freed).
+template <bool kPair>
+__device__ __forceinline__ void umma_commit_local(uint64_t* bar) {
+  if constexpr (kPair) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :
+                 : "r"(smem_addr(bar))
+                 : "memory");
+  } else {
+    umma_commit<false>(bar);
+  }
+}
+
+template <bool kPair> __device__ __forceinline__ void tmem_alloc(uint32_t* dst) {
+  if constexpr (kPair) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :
+                 : "r"(smem_addr(dst)), "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  } else {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :
+                 : "r"(smem_addr(dst)), "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+}
+
+template <bool kPair> __device__ __forceinline__ void tmem_dealloc(uint32_t base) {
+  if constexpr (kPair) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;"
+                 :
+                 : "r"(base), "r"(kTmemCols)
+                 : "memory");
+  } else {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
+                 :
+                 : "r"(base), "r"(kTmemCols)
+                 : "memory");
+  }
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -175,87 +295,96 @@ struct TileGrid {
   }
 };
 
-template <typename T>
-__global__ void __launch_bounds__(kThreads, 1)
-swiglu_gemm_kernel(const __grid_constant__ CUtensorMap map_x,
-                   const __grid_constant__ CUtensorMap map_wg,
-                   const __grid_constant__ CUtensorMap map_wu, T* __restrict__ act,
-                   int64_t act_stride, T* __restrict__ gate_out, T* __restrict__ up_out,
-                   int64_t pre_stride, int m, int n, int k) {
+template <typename T, bool kPair>
+__device__ __forceinline__ void swiglu_gemm_body(const CUtensorMap* map_x,
+                                                 const CUtensorMap* map_wg,
+                                                 const CUtensorMap* map_wu, T* act,
+                                                 int64_t act_stride, T* gate_out, T* up_out,
+                                                 int64_t pre_stride, int m, int n, int k) {
+  using S = Shape<kPair>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   const uint32_t pad = ((raw + 1023u) & ~1023u) - raw;
   unsigned char* tiles = smem_raw + pad;
-  GemmBarriers* bars = reinterpret_cast<GemmBarriers*>(tiles + kStages * kStageBytes);
+  GemmBarriers* bars = reinterpret_cast<GemmBarriers*>(tiles + S::kStages * S::kStageBytes);
   const uint32_t tiles_addr = raw + pad;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const TileGrid grid{(m + kBM - 1) / kBM, (n + kBN - 1) / kBN};
+  const uint32_t rank = kPair ? cluster_rank() : 0u;
+  const bool leader = rank == 0;
+  const int unit = blockIdx.x / S::kCtas, units = gridDim.x / S::kCtas;
+  const TileGrid grid{(m + S::kTileM - 1) / S::kTileM, (n + kBN - 1) / kBN};
   const int kblocks = (k + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < S::kStages; ++s) {
       mbar_init(&bars->full[s], 1);
       mbar_init(&bars->empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->tmem_full[b], 1);
-      mbar_init(&bars->tmem_empty[b], kThreads / 32 - kEpiWarp0);
+      mbar_init(&bars->tmem_empty[b], kEpiWarps * S::kCtas);
     }
     mbar_init(&bars->drain, 1);
     fence_mbar_init();
   }
-  if (warp == 2) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                 :
-                 : "r"(smem_addr(&bars->tmem_base)), "r"(kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
+  if (warp == 2) tmem_alloc<kPair>(&bars->tmem_base);
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kPair) cluster_sync(); else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer --
+    // Both CTAs of a pair load their own halves; the copies complete on the even CTA's
+    // `full` barrier, whose expected byte count covers both halves.
     if (lane == 0) {
       RingPos pos;
       uint32_t issued_mask = 0, issued_phase = 0;  // per slot: ever issued, parity of last
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < grid.count(); t += gridDim.x) {
+      for (int t = unit; ok && t < grid.count(); t += units) {
         int mb, nb;
         grid.coords(t, mb, nb);
+        const int row0 = mb * S::kTileM + (int)rank * kBM;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!wait_bounded(&bars->empty[pos.slot], pos.phase ^ 1u)) {
             ok = false;
             break;
           }
           uint64_t* full = &bars->full[pos.slot];
-          mbar_arrive_expect_tx(full, kStageBytes);
-          const uint32_t sa = tiles_addr + pos.slot * kStageBytes;
-          tma_load_2d(sa, &map_x, kb * kBK, mb * kBM, full);
-          tma_load_2d(sa + kATileBytes, &map_wg, kb * kBK, nb * kBN, full);
-          tma_load_2d(sa + kATileBytes + kBTileBytes / 2, &map_wu, kb * kBK, nb * kBN, full);
+          if (leader) mbar_arrive_expect_tx(full, S::kCtas * S::kStageBytes);
+          const uint32_t full_addr = kPair ? peer_addr(full, 0) : smem_addr(full);
+          const uint32_t sa = tiles_addr + pos.slot * S::kStageBytes;
+          tma_load_2d<kPair>(sa, map_x, kb * kBK, row0, full_addr);
+          if constexpr (kPair) {
+            tma_load_2d<true>(sa + kATileBytes, leader ? map_wg : map_wu, kb * kBK, nb * kBN,
+                              full_addr);
+          } else {
+            tma_load_2d<false>(sa + kATileBytes, map_wg, kb * kBK, nb * kBN, full_addr);
+            tma_load_2d<false>(sa + kATileBytes + kWTileBytes, map_wu, kb * kBK, nb * kBN,
+                               full_addr);
+          }
           issued_mask |= 1u << pos.slot;
           issued_phase = (issued_phase & ~(1u << pos.slot)) | (pos.phase << pos.slot);
-          pos.advance(1, kStages);
+          pos.advance(1, S::kStages);
         }
       }
       if (!ok) record_gemm_error();
-      // Every copy this CTA issued must have landed before it may exit.
-      for (int s = 0; s < kStages; ++s)
-        if (issued_mask >> s & 1u) wait_bounded(&bars->full[s], issued_phase >> s & 1u);
+      // Every copy this CTA issued must have landed before it may exit (the even CTA's
+      // barriers also count the odd CTA's bytes).
+      if (leader)
+        for (int s = 0; s < S::kStages; ++s)
+          if (issued_mask >> s & 1u) wait_bounded(&bars->full[s], issued_phase >> s & 1u);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA issuer --
-    if (lane == 0) {
-      constexpr uint32_t idesc = instr_desc<T>(kBM, 2 * kBN);
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = instr_desc<T>(S::kTileM, 2 * kBN);
       RingPos pos;
       bool ok = true;
       int i = 0;
-      for (int t = blockIdx.x; ok && t < grid.count(); t += gridDim.x, ++i) {
+      for (int t = unit; ok && t < grid.count(); t += units, ++i) {
         const int b = i & 1;
         if (!wait_bounded(&bars->tmem_empty[b], ((i >> 1) & 1) ^ 1)) {
           ok = false;
@@ -269,7 +398,7 @@ swiglu_gemm_kernel(const __grid_constant__ CUtensorMap map_x,
             break;
           }
           tc_fence_after();
-          const uint32_t sa = tiles_addr + pos.slot * kStageBytes;
+          const uint32_t sa = tiles_addr + pos.slot * S::kStageBytes;
           const uint64_t adesc = smem_desc_sw128(sa);
           const uint64_t bdesc = smem_desc_sw128(sa + kATileBytes);
 #pragma unroll
@@ -277,25 +406,27 @@ swiglu_gemm_kernel(const __grid_constant__ CUtensorMap map_x,
             // Advancing the start address by 32 bytes selects the next 16 K-elements inside
             // the swizzled 128-byte rows (the swizzle is a function of the address bits).
             const uint64_t step = (uint64_t)((kk * kUmmaK * 2) >> 4);
-            umma_f16(d, adesc + step, bdesc + step, idesc, (kb | kk) != 0);
+            umma_f16<kPair>(d, adesc + step, bdesc + step, idesc, (kb | kk) != 0);
           }
-          umma_commit(&bars->empty[pos.slot]);  // frees the stage once these MMAs finish
-          pos.advance(1, kStages);
+          umma_commit<kPair>(&bars->empty[pos.slot]);  // frees the stage in both CTAs
+          pos.advance(1, S::kStages);
         }
         if (!ok) break;
-        umma_commit(&bars->tmem_full[b]);
+        umma_commit<kPair>(&bars->tmem_full[b]);
       }
       if (!ok) record_gemm_error();
       // All MMAs this thread issued must be complete before the tensor memory is freed.
-      umma_commit(&bars->drain);
+      umma_commit_local<kPair>(&bars->drain);
       wait_bounded(&bars->drain, 0);
     }
     __syncwarp();
   } else if (warp >= kEpiWarp0) {
     // ---------------------------------------------------------------- epilogue --
     const int q = warp & 3;  // this warp may read tensor-memory lanes [32q, 32q + 32)
+    const uint32_t empty_addr0 = kPair ? peer_addr(&bars->tmem_empty[0], 0)
+                                       : smem_addr(&bars->tmem_empty[0]);
     int i = 0;
-    for (int t = blockIdx.x; t < grid.count(); t += gridDim.x, ++i) {
+    for (int t = unit; t < grid.count(); t += units, ++i) {
       const int b = i & 1;
       if (!wait_bounded(&bars->tmem_full[b], (i >> 1) & 1)) {
         record_gemm_error();
@@ -304,7 +435,7 @@ swiglu_gemm_kernel(const __grid_constant__ CUtensorMap map_x,
       tc_fence_after();
       int mb, nb;
       grid.coords(t, mb, nb);
-      const int row = mb * kBM + q * 32 + lane;
+      const int row = mb * S::kTileM + (int)rank * kBM + q * 32 + lane;
       const uint32_t tg = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * kAccCols);
 #pragma unroll 1
       for (int c = 0; c < kBN / 32; ++c) {
@@ -346,19 +477,37 @@ swiglu_gemm_kernel(const __grid_constant__ CUtensorMap map_x,
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->tmem_empty[b]);
+      // Release this buffer to the MMA issuer (on the even CTA of a pair).
+      if (lane == 0) mbar_arrive_cluster(empty_addr0 + (uint32_t)(b * sizeof(uint64_t)));
     }
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kPair) cluster_sync(); else __syncthreads();
   tc_fence_after();
-  if (warp == 2) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
-                 :
-                 : "r"(tmem_base), "r"(kTmemCols)
-                 : "memory");
-  }
+  if (warp == 2) tmem_dealloc<kPair>(tmem_base);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+swiglu_gemm_kernel(const __grid_constant__ CUtensorMap map_x,
+                   const __grid_constant__ CUtensorMap map_wg,
+                   const __grid_constant__ CUtensorMap map_wu, T* __restrict__ act,
+                   int64_t act_stride, T* __restrict__ gate_out, T* __restrict__ up_out,
+                   int64_t pre_stride, int m, int n, int k) {
+  swiglu_gemm_body<T, false>(&map_x, &map_wg, &map_wu, act, act_stride, gate_out, up_out,
+                             pre_stride, m, n, k);
+}
+
+template <typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+swiglu_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
+                        const __grid_constant__ CUtensorMap map_wg,
+                        const __grid_constant__ CUtensorMap map_wu, T* __restrict__ act,
+                        int64_t act_stride, T* __restrict__ gate_out, T* __restrict__ up_out,
+                        int64_t pre_stride, int m, int n, int k) {
+  swiglu_gemm_body<T, true>(&map_x, &map_wg, &map_wu, act, act_stride, gate_out, up_out,
+                            pre_stride, m, n, k);
 }
 
 // ------------------------------------------------------------------------ host ------
@@ -397,6 +546,21 @@ int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int6
   return PT_OK;
 }
 
+// Raises a kernel's dynamic shared memory limit once per device.
+bool allow_smem(const void* fn, int bytes, int dev) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({fn, dev})) return true;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  done.insert({fn, dev});
+  return true;
+}
+
 template <typename T>
 int gemm_impl(const void* x, int64_t xs, const void* wg, const void* wu, int64_t ws, void* act,
               int64_t as, void* gate_out, void* up_out, int64_t ps, int64_t m, int64_t n,
@@ -410,16 +574,30 @@ int gemm_impl(const void* x, int64_t xs, const void* wg, const void* wu, int64_t
   if (int st = make_map(&mu, wu, n, k, ws, kBN, type, "w_up")) return st;
   int dev = 0, sms = 0;
   if (int st = current_device_info(&dev, &sms)) return st;
-  static std::once_flag attr_once[2];
-  std::call_once(attr_once[std::is_same<T, __nv_bfloat16>::value ? 1 : 0], [] {
-    cudaFuncSetAttribute(swiglu_gemm_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         kSmemBytes);
-  });
-  const int64_t tiles = ((m + kBM - 1) / kBM) * ((n + kBN - 1) / kBN);
-  const int grid = (int)std::min<int64_t>(tiles, sms);
-  swiglu_gemm_kernel<T><<<grid, kThreads, kSmemBytes, stream>>>(
-      mx, mg, mu, static_cast<T*>(act), as, static_cast<T*>(gate_out), static_cast<T*>(up_out),
-      ps, (int)m, (int)n, (int)k);
+  T* a = static_cast<T*>(act);
+  T* g = static_cast<T*>(gate_out);
+  T* u = static_cast<T*>(up_out);
+  const int64_t tiles_n = (n + kBN - 1) / kBN;
+  // CTA pairs whenever there are at least two row blocks to pair up.
+  if (m > kBM && sms >= 2) {
+    using S = Shape<true>;
+    const void* fn = (const void*)swiglu_gemm_pair_kernel<T>;
+    if (!allow_smem(fn, S::kSmemBytes, dev))
+      return set_error(PT_ERR_CUDA, "cannot raise the shared memory limit of the GEMM kernel");
+    const int64_t tiles = ((m + S::kTileM - 1) / S::kTileM) * tiles_n;
+    const int pairs = (int)std::min<int64_t>(tiles, sms / 2);
+    swiglu_gemm_pair_kernel<T><<<2 * pairs, kThreads, S::kSmemBytes, stream>>>(
+        mx, mg, mu, a, as, g, u, ps, (int)m, (int)n, (int)k);
+  } else {
+    using S = Shape<false>;
+    const void* fn = (const void*)swiglu_gemm_kernel<T>;
+    if (!allow_smem(fn, S::kSmemBytes, dev))
+      return set_error(PT_ERR_CUDA, "cannot raise the shared memory limit of the GEMM kernel");
+    const int64_t tiles = ((m + S::kTileM - 1) / S::kTileM) * tiles_n;
+    const int grid = (int)std::min<int64_t>(tiles, sms);
+    swiglu_gemm_kernel<T><<<grid, kThreads, S::kSmemBytes, stream>>>(mx, mg, mu, a, as, g, u, ps,
+                                                                       (int)m, (int)n, (int)k);
+  }
   return check_launch("pt_swiglu_gemm_fwd");
 }
 
