@@ -58,6 +58,29 @@ def measured_peaks(key: str = "hbm_gbs") -> tuple[float, str]:
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}[key], "fallback"
 
 
+def time_library_ce(work, steps: int) -> float:
+    """ms per step of PyTorch's own cross-entropy forward + backward on the same logits."""
+
+    import torch.nn.functional as F
+
+    def step(i: int) -> None:
+        x = work.logits[i % 2].float().requires_grad_(True)
+        loss = F.cross_entropy(x, work.targets)
+        loss.backward()
+        work.dlogits.copy_(x.grad)
+
+    for i in range(2):
+        step(i)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(steps):
+        step(i)
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
+
+
 def time_library_mlpup(work, stream: int, steps: int) -> float:
     """ms per step of the unfused path the fused GEMM replaces: two cuBLAS GEMMs (torch
     matmul) for gate and up, then this library's SwiGLU forward kernel."""
@@ -396,6 +419,20 @@ class OpWorkload:
             self.bytes = (tokens * k + 2 * INTER * k + 3 * tokens * INTER) * BF16
             self.launches_per_step = 1
             self.dominant = ("swiglu_gemm_kernel", self.flops)
+        elif op == "ce":
+            # Cross-entropy forward + backward over a Llama-3 vocabulary (the next-step row):
+            # logits [tokens, 128256] bf16 ~ N(0, 2^2), uniform targets.
+            self.vocab = 128256
+            self.logits = [torch.randn((tokens, self.vocab), generator=gen, device=device,
+                                       dtype=bf) * 2 for _ in range(2)]
+            self.targets = torch.randint(0, self.vocab, (tokens,), generator=gen, device=device)
+            self.row_loss = torch.empty(tokens, device=device)
+            self.row_lse = torch.empty(tokens, device=device)
+            self.mean = torch.empty(2, device=device)
+            self.dlogits = torch.empty_like(self.logits[0])
+            self.bytes = 3 * tokens * self.vocab * BF16
+            self.launches_per_step = 3
+            self.dominant = ("ce_bwd_kernel", 2 * tokens * self.vocab * BF16)
         elif op == "swiglu":
             mk = lambda scale: [torch.randn((tokens, INTER), generator=gen, device=device, dtype=bf) * scale
                                 for _ in range(sets)]
@@ -425,7 +462,8 @@ class OpWorkload:
         self.i = 0
         self.events_per_step = 1
         self.traffic_key = {"rmsnorm": "rmsnorm_bwd", "swiglu": "swiglu_bwd", "rope": "rope_fwd",
-                            "addnorm": "add_rmsnorm_bwd", "mlpup": "swiglu_gemm"}[op]
+                            "addnorm": "add_rmsnorm_bwd", "mlpup": "swiglu_gemm",
+                            "ce": "ce_bwd"}[op]
 
     def bytes_per_step(self) -> int:
         return self.bytes
@@ -471,6 +509,18 @@ class OpWorkload:
             c.swiglu_gemm_fwd(x.data_ptr(), HIDDEN, self.wg.data_ptr(), self.wu.data_ptr(), HIDDEN,
                               self.act.data_ptr(), INTER, self.g.data_ptr(), self.u.data_ptr(),
                               INTER, T, INTER, HIDDEN, c.PT_BFLOAT16, stream)
+            if ev: ev[1].record()
+        elif self.op == "ce":
+            lg = self.logits[i % 2]
+            c.cross_entropy_fwd(lg.data_ptr(), self.vocab, T, 1, (self.vocab, 0),
+                                self.targets.data_ptr(), (1, 0), -100, self.row_loss.data_ptr(),
+                                self.row_lse.data_ptr(), self.mean.data_ptr(), c.PT_BFLOAT16,
+                                stream)
+            if ev: ev[0].record()
+            c.cross_entropy_bwd(lg.data_ptr(), self.vocab, T, 1, (self.vocab, 0),
+                                self.targets.data_ptr(), (1, 0), -100, self.row_lse.data_ptr(),
+                                self.mean.data_ptr(), None, self.dlogits.data_ptr(),
+                                (self.vocab, 0), c.PT_BFLOAT16, stream)
             if ev: ev[1].record()
         elif self.op == "swiglu":
             n = T * INTER
@@ -573,12 +623,14 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tokens", type=int, default=2048)
-    ap.add_argument("--workload", choices=["stack", "rmsnorm", "swiglu", "rope", "addnorm", "mlpup"],
+    ap.add_argument("--workload", choices=["stack", "rmsnorm", "swiglu", "rope", "addnorm", "mlpup",
+                                           "ce"],
                     default="stack",
                     help="stack = BASELINE config 5 (the headline); rmsnorm, swiglu, rope are "
                          "configs 2, 3 and 4, one op forward+backward per step, for per-kernel "
                          "measurement; addnorm = fused residual add + RMSNorm at config 2 shapes; "
-                         "mlpup = the gate/up GEMMs with the SwiGLU epilogue (tcgen05)")
+                         "mlpup = the gate/up GEMMs with the SwiGLU epilogue (tcgen05); "
+                         "ce = cross-entropy forward + backward over a 128256 vocabulary")
     args = ap.parse_args()
     if args.workload != "stack":
         args.no_e2e = True
@@ -592,7 +644,8 @@ def main() -> None:
              "swiglu": "SwiGLU fwd+bwd bf16 i14336 (BASELINE config 3)",
              "rope": "RoPE q+k fwd+bwd bf16 (BASELINE config 4)",
              "addnorm": "fused residual add + RMSNorm fwd+bwd bf16 h4096 (config 2 shapes)",
-             "mlpup": "gate/up GEMMs + SwiGLU epilogue fwd bf16 4096->14336 (config 3/5 shapes)"}
+             "mlpup": "gate/up GEMMs + SwiGLU epilogue fwd bf16 4096->14336 (config 3/5 shapes)",
+             "ce": "cross-entropy fwd+bwd bf16, vocab 128256 (Llama-3 head)"}
     config = {
         "workload": names[args.workload],
         "layers": args.layers,
@@ -679,11 +732,17 @@ def main() -> None:
     traffic = dram_traffic_per_launch(work.traffic_key, work.tokens)
     tensor_bound = args.workload == "mlpup"
     library_ms = None
+    library_what = None
+    if args.workload == "ce":
+        library_ms = time_library_ce(work, args.steps)
+        library_what = ("PyTorch F.cross_entropy forward + backward on the bf16 logits "
+                        "upcast to fp32 (what CUDA autocast runs)")
     if tensor_bound:
         # A tensor-core contraction: FLOPs per launch over the cuBLAS bf16 burst peak.
         achieved = dom_bytes / (dom_ms / 1e3) / 1e12
         tpeak, tpeak_kind = measured_peaks("bf16_tflops")
         library_ms = time_library_mlpup(work, stream, args.steps)
+        library_what = "cuBLAS gate and up GEMMs (torch.matmul) + this library's SwiGLU kernel"
 
     e2e = None
     if not args.no_e2e:
@@ -735,7 +794,7 @@ def main() -> None:
                 "mean_launch_us": dom_ms * 1e3,
             },
             "library_baseline": None if library_ms is None else {
-                "what": "cuBLAS gate and up GEMMs (torch.matmul) + this library's SwiGLU kernel",
+                "what": library_what,
                 "ms_per_step": library_ms,
                 "value": world * work.tokens / (library_ms / 1e3),
                 "unit": "tokens/s",

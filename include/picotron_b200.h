@@ -197,8 +197,10 @@ PT_API int pt_add_rmsnorm_bwd(const void* dy, int64_t dy_row_stride,
 
 /* Reads and clears this library's device-side error word of the current device
  * (synchronous: waits for the device). *code = 0 means no kernel reported a problem;
- * 1 means a kernel gave up waiting for one of its own TMA copies (after about a second)
- * and skipped the rest of its rows, so outputs of the affected call are incomplete.
+ * 1 means a kernel gave up waiting for one of its own TMA copies or MMAs (after about a
+ * second) and skipped the rest of its work, so outputs of the affected call are incomplete;
+ * 2 means pt_cross_entropy_fwd met a target outside [0, vocab) that is not ignore_index
+ * (its row loss, and so the mean, is NaN).
  * No reference counterpart: the reference has no device-side waits. */
 PT_API int pt_take_device_error(int* code);
 
@@ -233,6 +235,42 @@ PT_API int pt_swiglu_gemm_fwd(const void* x, int64_t x_row_stride,
                               void* gate_out, void* up_out, int64_t pre_row_stride,
                               int64_t m, int64_t n, int64_t k, int dtype,
                               void* stream);
+
+/* ---------------------------------------------------------- cross-entropy ------- */
+
+/* Mean cross-entropy over rows of `vocab` logits (class stride 1). Rows form an
+ * [outer, inner] grid: row (o, i) starts at logits + o * logits_outer_stride +
+ * i * logits_inner_stride and its target is targets[o * targets_outer_stride +
+ * i * targets_inner_stride] (int64); strides are in elements. So the training call
+ * F.cross_entropy(logits[:, :-1, :].transpose(1, 2), input_ids[:, 1:]) reads [B, S, V] logits
+ * in place with outer = B, inner = S - 1, strides (S * V, V) and targets (S, 1) from
+ * input_ids + 1. Writes row_loss[r] = lse_r - x_r[target] (0 for ignore_index rows) and
+ * row_lse[r] = log(sum(exp(x_r))) (fp32, dense [rows]), then mean_out[0] = the mean of
+ * row_loss over the rows whose target is not ignore_index and mean_out[1] = 1 / their count
+ * (NaN for both when there are none), deterministically. fp32 math from f32/f16/bf16 logits.
+ * Replaces the loss of src/picotron/training/train_loop.py:95-97,141-145 (F.cross_entropy,
+ * mean reduction) and the forward-only Triton kernel of
+ * src/picotron/nn/triton_kernels/cross_entropy.py:28-87. */
+PT_API int pt_cross_entropy_fwd(const void* logits, int64_t vocab, int64_t outer,
+                                int64_t inner, int64_t logits_outer_stride,
+                                int64_t logits_inner_stride, const int64_t* targets,
+                                int64_t targets_outer_stride, int64_t targets_inner_stride,
+                                int64_t ignore_index, float* row_loss, float* row_lse,
+                                float* mean_out, int dtype, void* stream);
+
+/* Gradient of pt_cross_entropy_fwd's mean loss: dlogits = (softmax(x_r) - onehot(target_r))
+ * * grad_loss * mean_out[1] (grad_loss: one fp32 value in device memory, or NULL for 1),
+ * zeros for ignored rows, written in the logits dtype at dlogits with its own two row
+ * strides (class stride 1). Recomputes softmax from row_lse. Replaces the autograd
+ * backward of F.cross_entropy at train_loop.py:141-145. */
+PT_API int pt_cross_entropy_bwd(const void* logits, int64_t vocab, int64_t outer,
+                                int64_t inner, int64_t logits_outer_stride,
+                                int64_t logits_inner_stride, const int64_t* targets,
+                                int64_t targets_outer_stride, int64_t targets_inner_stride,
+                                int64_t ignore_index, const float* row_lse,
+                                const float* mean_out, const float* grad_loss, void* dlogits,
+                                int64_t dlogits_outer_stride, int64_t dlogits_inner_stride,
+                                int dtype, void* stream);
 
 /* ------------------------------------------------------------------- RoPE -------- */
 

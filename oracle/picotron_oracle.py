@@ -154,6 +154,60 @@ def swiglu_backward(gate: Tensor, up: Tensor, dout: Tensor, mode: str = "eager")
     return dout * up * silu_derivative, dout * silu_gate
 
 
+# --------------------------------------------------------------------- cross-entropy --
+
+
+def _ce_rows(logits: Tensor, targets: Tensor):
+    # [N, V] / [N] or [B, V, S] / [B, S] (class dimension 1) as [rows, V] / [rows].
+    if logits.dim() == 3:
+        return logits.movedim(1, -1).reshape(-1, logits.size(1)), targets.reshape(-1)
+    return logits, targets
+
+
+def cross_entropy_forward(logits: Tensor, targets: Tensor, ignore_index: int = -100,
+                          mode: str = "eager") -> Tensor:
+    """Mean cross-entropy as the training loop computes it (picotron
+    src/picotron/training/train_loop.py:141-145: F.cross_entropy(logits[:, :-1, :]
+    .transpose(1, 2), input_ids[:, 1:]) through CrossEntropyWithFallback,
+    nn/triton_kernels/cross_entropy.py:102-112; mean over the targets != ignore_index).
+    eager: F.cross_entropy on the logits upcast to fp32 (what CUDA autocast does for
+    cross_entropy; a no-op for the reference's fp32 CPU path), fp32 result.
+    exact: log-sum-exp and the mean in float64."""
+
+    _check_mode(mode)
+    if mode == "eager":
+        return F.cross_entropy(logits.float(), targets, ignore_index=ignore_index)
+    x, t = _ce_rows(logits.double(), targets)
+    keep = t != ignore_index
+    lse = torch.logsumexp(x, dim=1)
+    picked = x.gather(1, t.clamp(0, x.size(1) - 1).unsqueeze(1)).squeeze(1)
+    return ((lse - picked) * keep).sum() / keep.sum()
+
+
+def cross_entropy_backward(logits: Tensor, targets: Tensor, grad: float = 1.0,
+                           ignore_index: int = -100, mode: str = "eager") -> Tensor:
+    """Gradient of cross_entropy_forward with respect to the logits, in the logits' layout.
+    eager: PyTorch autograd of the eager form, cast to the logits dtype (the gradient
+    flowing back through autocast's fp32 cast). exact: (softmax - onehot) * grad / count in
+    float64, zero for ignored rows."""
+
+    _check_mode(mode)
+    if mode == "eager":
+        x = logits.detach().float().requires_grad_(True)
+        loss = F.cross_entropy(x, targets, ignore_index=ignore_index)
+        (dx,) = torch.autograd.grad(loss, (x,), torch.tensor(grad, dtype=torch.float32))
+        return dx.to(logits.dtype)
+    x = logits.double()
+    rows, t = _ce_rows(x, targets)
+    keep = (t != ignore_index).double()
+    p = torch.softmax(rows, dim=1)
+    onehot = torch.zeros_like(p).scatter_(1, t.clamp(0, rows.size(1) - 1).unsqueeze(1), 1.0)
+    d = (p - onehot) * (keep * grad / keep.sum()).unsqueeze(1)
+    if logits.dim() == 3:
+        d = d.reshape(logits.size(0), logits.size(2), logits.size(1)).movedim(-1, 1)
+    return d
+
+
 # ------------------------------------------------------------------------------ RoPE --
 
 

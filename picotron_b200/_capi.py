@@ -67,6 +67,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pt_swiglu_gemm_fwd": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64, _c_ptr, _c_i64,
                                     _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_int,
                                     _c_ptr]),
+    "pt_cross_entropy_fwd": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_ptr,
+                                      _c_i64, _c_i64, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_int,
+                                      _c_ptr]),
+    "pt_cross_entropy_bwd": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_ptr,
+                                      _c_i64, _c_i64, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
+                                      _c_i64, _c_i64, _c_int, _c_ptr]),
     "pt_add_rmsnorm_fwd": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64,
                                     _c_ptr, _c_i64, _c_ptr, _c_i64, _c_i64, _c_int, _c_int,
                                     _c_float, _c_ptr]),
@@ -271,6 +277,34 @@ def swiglu_gemm_fwd(x: int, x_row_stride: int, w_gate: int, w_up: int, w_row_str
                                           act_row_stride, gate_out, up_out, pre_row_stride, m,
                                           n, k, dtype, stream)
     _check("pt_swiglu_gemm_fwd", status, error_type)
+
+
+def cross_entropy_fwd(logits: int, vocab: int, outer: int, inner: int, logits_strides,
+                      targets: int, targets_strides, ignore_index: int, row_loss: int,
+                      row_lse: int, mean_out: int, dtype: int, stream: int,
+                      error_type: type[Exception] | None = None) -> None:
+    """Per-row loss / lse and the mean cross-entropy (see pt_cross_entropy_fwd)."""
+
+    status = library().pt_cross_entropy_fwd(logits, vocab, outer, inner, logits_strides[0],
+                                            logits_strides[1], targets, targets_strides[0],
+                                            targets_strides[1], ignore_index, row_loss, row_lse,
+                                            mean_out, dtype, stream)
+    _check("pt_cross_entropy_fwd", status, error_type)
+
+
+def cross_entropy_bwd(logits: int, vocab: int, outer: int, inner: int, logits_strides,
+                      targets: int, targets_strides, ignore_index: int, row_lse: int,
+                      mean_out: int, grad_loss: int | None, dlogits: int, dlogits_strides,
+                      dtype: int, stream: int,
+                      error_type: type[Exception] | None = None) -> None:
+    """Logits gradient of the mean cross-entropy (see pt_cross_entropy_bwd)."""
+
+    status = library().pt_cross_entropy_bwd(logits, vocab, outer, inner, logits_strides[0],
+                                            logits_strides[1], targets, targets_strides[0],
+                                            targets_strides[1], ignore_index, row_lse, mean_out,
+                                            grad_loss, dlogits, dlogits_strides[0],
+                                            dlogits_strides[1], dtype, stream)
+    _check("pt_cross_entropy_bwd", status, error_type)
 
 
 def take_device_error() -> int:

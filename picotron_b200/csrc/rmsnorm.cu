@@ -43,8 +43,10 @@
 
 namespace pt {
 
-// Reads and clears the fused SwiGLU GEMM's device error word (swiglu_gemm.cu).
+// Read and clear the device error words of the fused SwiGLU GEMM (swiglu_gemm.cu) and of
+// the cross-entropy kernels (cross_entropy.cu).
 int take_gemm_device_error(int* code);
+int take_ce_device_error(int* code);
 
 // Device-side error word of this library on each device (0 = none). Kernels that give up
 // on a bounded wait record kDeviceErrWaitTimeout here; pt_take_device_error reads it.
@@ -236,10 +238,10 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
           unpack2<T>(lds128(sx + row_elems + v * V), fg);
           float2 wv[V / 2];
 #pragma unroll
-          for (int q = 0; q < kPlanes; ++q) {
-            const float4 t = wsm[q * nvec + v];
-            wv[2 * q] = make_float2(t.x, t.y);
-            wv[2 * q + 1] = make_float2(t.z, t.w);
+          for (int pl = 0; pl < kPlanes; ++pl) {
+            const float4 t = wsm[pl * nvec + v];
+            wv[2 * pl] = make_float2(t.x, t.y);
+            wv[2 * pl + 1] = make_float2(t.z, t.w);
           }
 #pragma unroll
           for (int e = 0; e < V / 2; ++e) {
@@ -1165,9 +1167,10 @@ int pt_take_device_error(int* code) {
                        cudaGetErrorString(e));
     }
   }
-  int gemm_value = 0;
+  int gemm_value = 0, ce_value = 0;
   if (int st = take_gemm_device_error(&gemm_value)) return st;
-  *code = value != 0 ? value : gemm_value;
+  if (int st = take_ce_device_error(&ce_value)) return st;
+  *code = value != 0 ? value : gemm_value != 0 ? gemm_value : ce_value;
   return ok();
 }
 

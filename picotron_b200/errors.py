@@ -20,3 +20,8 @@ class TritonSwiGLUUnavailable(RuntimeError):
 
 class TritonRoPEUnavailable(RuntimeError):
     """The sm_100a RoPE path cannot run these inputs."""
+
+
+class TritonCrossEntropyUnavailable(RuntimeError):
+    """The sm_100a cross-entropy path cannot run these inputs (reference
+    triton_kernels/cross_entropy.py:22)."""

@@ -3,13 +3,20 @@
 Same public names as the reference package (src/picotron/nn/triton_kernels/__init__.py)
 for RMSNorm, SwiGLU and RoPE, backed by the sm_100a CUDA library instead of Triton, plus
 ``fused_add_rms_norm`` (the decoder block's residual add fused into the following norm) and
-``swiglu_gate_up`` (the MLP's gate/up projections with the activation as one tcgen05 GEMM).
+``swiglu_gate_up`` (the MLP's gate/up projections with the activation as one tcgen05 GEMM),
+and the loss: ``triton_cross_entropy`` / ``CrossEntropyWithFallback`` (forward and backward).
 """
 
 from picotron_b200.errors import (
+    TritonCrossEntropyUnavailable,
     TritonRMSNormUnavailable,
     TritonRoPEUnavailable,
     TritonSwiGLUUnavailable,
+)
+from picotron_b200.kernels.cross_entropy import (
+    CrossEntropyWithFallback,
+    cross_entropy,
+    triton_cross_entropy,
 )
 from picotron_b200.kernels.rmsnorm import (
     fused_add_rms_norm,
@@ -24,6 +31,10 @@ from picotron_b200.kernels.swiglu import (
 )
 
 __all__ = [
+    "CrossEntropyWithFallback",
+    "TritonCrossEntropyUnavailable",
+    "cross_entropy",
+    "triton_cross_entropy",
     "TritonRMSNormUnavailable",
     "fused_add_rms_norm",
     "swiglu_gate_up",

@@ -13,6 +13,9 @@ backward op:
 * ``swiglu_backward(dout, gate, up) -> (dgate, dup)``
 * ``swiglu_gate_up(x, w_gate, w_up) -> (act, gate, up)``  (reference feedforward.py:27-42:
   the gate and up projections and the activation as one tcgen05 GEMM with a SwiGLU epilogue)
+* ``cross_entropy(logits, targets, ignore_index) -> (loss, row_lse, mean_out)``
+  (reference train_loop.py:95-97,141-145: F.cross_entropy, mean over non-ignored rows)
+* ``cross_entropy_backward(grad, logits, targets, row_lse, mean_out, ignore_index) -> dlogits``
 * ``rope(x, cosine, sine, layout) -> out``           (reference nn/rope.py:35-51)
 * ``rope_backward(dy, cosine, sine, layout) -> dx``
 
@@ -28,6 +31,7 @@ from torch import Tensor
 
 from picotron_b200 import _capi
 from picotron_b200.errors import (
+    TritonCrossEntropyUnavailable,
     TritonRMSNormUnavailable,
     TritonRoPEUnavailable,
     TritonSwiGLUUnavailable,
@@ -444,6 +448,116 @@ def _gate_up_backward(ctx, d_act, d_gate, d_up):
 
 
 swiglu_gate_up.register_autograd(_gate_up_backward, setup_context=_gate_up_setup)
+
+
+# --------------------------------------------------------------------- cross-entropy --
+
+
+def _ce_geometry(logits: Tensor, targets: Tensor):
+    """(outer, inner, logits strides, targets strides) of F.cross_entropy's layouts:
+    logits [N, V] with targets [N], or logits [B, V, S] with targets [B, S] (class dim 1,
+    which must have unit stride)."""
+
+    if logits.dim() == 2 and targets.dim() == 1 and targets.size(0) == logits.size(0):
+        return logits.size(0), 1, (logits.stride(0), 0), (targets.stride(0), 0)
+    if (logits.dim() == 3 and targets.dim() == 2 and targets.size(0) == logits.size(0)
+            and targets.size(1) == logits.size(2)):
+        return (logits.size(0), logits.size(2), (logits.stride(0), logits.stride(2)),
+                (targets.stride(0), targets.stride(1)))
+    raise TritonCrossEntropyUnavailable(
+        "cross-entropy expects logits [N, V] with targets [N], or [B, V, S] with targets [B, S]")
+
+
+def _ce_inputs(logits: Tensor, targets: Tensor) -> tuple[Tensor, Tensor]:
+    check_device(logits.device, TritonCrossEntropyUnavailable)
+    if targets.device != logits.device:
+        raise TritonCrossEntropyUnavailable("logits and targets must be on the same device.")
+    if targets.dtype != torch.long:
+        raise TritonCrossEntropyUnavailable("cross-entropy targets must be int64 class indices.")
+    _dtype_code(logits, TritonCrossEntropyUnavailable)
+    if logits.dim() not in (2, 3) or logits.stride(1) != 1:
+        # The class dimension must be contiguous: move it last (one copy).
+        if logits.dim() in (2, 3):
+            logits = logits.movedim(1, -1).contiguous().movedim(-1, 1)
+    return logits, targets
+
+
+@torch.library.custom_op("picotron_b200::cross_entropy", mutates_args=())
+def cross_entropy(logits: Tensor, targets: Tensor,
+                  ignore_index: int) -> tuple[Tensor, Tensor, Tensor]:
+    logits, targets = _ce_inputs(logits, targets)
+    outer, inner, lstr, tstr = _ce_geometry(logits, targets)
+    rows = outer * inner
+    row_loss = torch.empty(rows, dtype=torch.float32, device=logits.device)
+    row_lse = torch.empty(rows, dtype=torch.float32, device=logits.device)
+    mean_out = torch.empty(2, dtype=torch.float32, device=logits.device)
+    with _OnDevice(logits.device):
+        _capi.cross_entropy_fwd(
+            logits.data_ptr(), logits.size(1), outer, inner, lstr, targets.data_ptr(), tstr,
+            int(ignore_index), row_loss.data_ptr(), row_lse.data_ptr(), mean_out.data_ptr(),
+            DTYPE_CODES[logits.dtype], _stream(logits.device), TritonCrossEntropyUnavailable,
+        )
+    return mean_out[0].clone(), row_lse, mean_out
+
+
+@cross_entropy.register_fake
+def _cross_entropy_fake(logits: Tensor, targets: Tensor, ignore_index: int):
+    rows = targets.numel()
+    return (torch.empty((), dtype=torch.float32, device=logits.device),
+            torch.empty(rows, dtype=torch.float32, device=logits.device),
+            torch.empty(2, dtype=torch.float32, device=logits.device))
+
+
+@torch.library.custom_op("picotron_b200::cross_entropy_backward", mutates_args=())
+def cross_entropy_backward(grad: Tensor, logits: Tensor, targets: Tensor, row_lse: Tensor,
+                           mean_out: Tensor, ignore_index: int) -> Tensor:
+    logits_c, targets = _ce_inputs(logits, targets)
+    outer, inner, lstr, tstr = _ce_geometry(logits_c, targets)
+    vocab = logits_c.size(1)
+    # Class dimension innermost in memory: [N, V], or [B, S, V] seen as [B, V, S].
+    if logits.dim() == 2:
+        dlogits = torch.empty((outer, vocab), dtype=logits.dtype, device=logits.device)
+        dstr = (dlogits.stride(0), 0)
+    else:
+        buf = torch.empty((outer, inner, vocab), dtype=logits.dtype, device=logits.device)
+        dlogits = buf.transpose(1, 2)
+        dstr = (buf.stride(0), buf.stride(1))
+    if outer * inner == 0:
+        return dlogits
+    g = grad.to(torch.float32).contiguous()
+    with _OnDevice(logits.device):
+        _capi.cross_entropy_bwd(
+            logits_c.data_ptr(), vocab, outer, inner, lstr, targets.data_ptr(), tstr,
+            int(ignore_index), row_lse.data_ptr(), mean_out.data_ptr(), g.data_ptr(),
+            dlogits.data_ptr(), dstr, DTYPE_CODES[logits.dtype], _stream(logits.device),
+            TritonCrossEntropyUnavailable,
+        )
+    return dlogits
+
+
+@cross_entropy_backward.register_fake
+def _cross_entropy_backward_fake(grad, logits, targets, row_lse, mean_out, ignore_index):
+    return torch.empty_like(logits)
+
+
+def _ce_setup(ctx, inputs, output) -> None:
+    logits, targets, ignore_index = inputs
+    _, row_lse, mean_out = output
+    ctx.save_for_backward(logits, targets, row_lse, mean_out)
+    ctx.ignore_index = ignore_index
+    ctx.set_materialize_grads(False)
+
+
+def _ce_backward(ctx, grad, _grad_lse, _grad_mean):
+    logits, targets, row_lse, mean_out = ctx.saved_tensors
+    if grad is None:
+        return None, None, None
+    dlogits = torch.ops.picotron_b200.cross_entropy_backward(grad, logits, targets, row_lse,
+                                                             mean_out, ctx.ignore_index)
+    return dlogits, None, None
+
+
+cross_entropy.register_autograd(_ce_backward, setup_context=_ce_setup)
 
 
 # ------------------------------------------------------------------------------ RoPE --

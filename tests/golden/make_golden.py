@@ -71,6 +71,18 @@ def _gate_up(ffn_mod, x, hidden, inter, seed):
             "gate": gate.detach(), "up": up.detach(), "act": activated.detach()}
 
 
+def _ce(ce_mod, logits, input_ids, upcast):
+    """The training loop's loss call (train_loop.py:95-97,141-145) on [B, S, V] logits, with
+    the reference's CrossEntropyWithFallback; `upcast` applies CUDA autocast's fp32 cast."""
+
+    lg = logits.clone().requires_grad_(True)
+    x = lg.float() if upcast else lg
+    loss = ce_mod.CrossEntropyWithFallback(use_triton=False)(
+        x[:, :-1, :].transpose(1, 2), input_ids[:, 1:])
+    loss.backward()
+    return {"loss": loss.detach(), "dlogits": lg.grad}
+
+
 def _swiglu(ref, g, u, dy):
     gg = g.clone().requires_grad_(True)
     ug = u.clone().requires_grad_(True)
@@ -99,6 +111,7 @@ def main() -> None:
     sys.path.insert(0, args.reference_src)
     torch.set_num_threads(1)
     from picotron.nn import feedforward as ffn_mod
+    from picotron.nn.triton_kernels import cross_entropy as ce_mod
     from picotron.nn import rope as rope_mod
     from picotron.nn.triton_kernels import rmsnorm as rms_ref
     from picotron.nn.triton_kernels import swiglu as swiglu_ref
@@ -174,6 +187,22 @@ def main() -> None:
     x = torch.randn(32, 64, generator=g).to(torch.bfloat16)
     res = _gate_up(ffn_mod, x, 64, 128, 4)
     written.append(golden_io.save("gate_up_bf16", {"x": x, **res}, {"seed": 4}))
+
+    # Cross-entropy as the training loop calls it: logits [B=2, S=9, V=1000] ~ N(0,1) * 3,
+    # input_ids uniform in [0, V) with two positions set to -100 (ignored); fp32 logits (the
+    # reference's CPU training dtype) and bf16 logits under autocast's fp32 cast.
+    g = _gen(5)
+    logits = torch.randn(2, 9, 1000, generator=g) * 3
+    ids = torch.randint(0, 1000, (2, 9), generator=g)
+    ids[0, 4] = -100
+    ids[1, 8] = -100
+    res = _ce(ce_mod, logits, ids, upcast=False)
+    written.append(golden_io.save("ce_f32", {"logits": logits, "input_ids": ids, **res},
+                                  {"seed": 5}))
+    lb = logits.to(torch.bfloat16)
+    res = _ce(ce_mod, lb, ids, upcast=True)
+    written.append(golden_io.save("ce_bf16", {"logits": lb, "input_ids": ids, **res},
+                                  {"seed": 5}))
 
     # BASELINE config 3 family, bf16: gate, up ~ N(0,1) * 2, dy ~ N(0,1), [16, 1024].
     g = _gen(0)

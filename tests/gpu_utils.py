@@ -134,3 +134,41 @@ def swiglu_gemm(x2d, wg, wu, save_preact=True):
                           u.data_ptr() if save_preact else None, n, m, n, k,
                           DTYPE_CODES[x2d.dtype], stream())
     return act, g, u
+
+
+def cross_entropy(logits, targets, ignore_index=-100, grad=None, want_grad=True):
+    """C-ABI forward (+ backward) on [N, V] / [N] or [B, V, S] / [B, S] (class stride 1).
+    Returns (mean loss, row_loss, dlogits or None); dlogits is dense [N, V] / [B, S, V]
+    seen in the logits' layout."""
+
+    if logits.dim() == 2:
+        outer, inner = logits.size(0), 1
+        ls, ts = (logits.stride(0), 0), (targets.stride(0), 0)
+    else:
+        outer, inner = logits.size(0), logits.size(2)
+        ls, ts = (logits.stride(0), logits.stride(2)), (targets.stride(0), targets.stride(1))
+    vocab = logits.size(1)
+    rows = outer * inner
+    row_loss = torch.empty(rows, dtype=torch.float32, device=logits.device)
+    row_lse = torch.empty_like(row_loss)
+    mean = torch.empty(2, dtype=torch.float32, device=logits.device)
+    code = DTYPE_CODES[logits.dtype]
+    _capi.cross_entropy_fwd(logits.data_ptr(), vocab, outer, inner, ls, targets.data_ptr(), ts,
+                            ignore_index, row_loss.data_ptr(), row_lse.data_ptr(),
+                            mean.data_ptr(), code, stream())
+    if not want_grad:
+        return mean[0], row_loss, None
+    if logits.dim() == 2:
+        d = torch.empty((outer, vocab), dtype=logits.dtype, device=logits.device)
+        ds = (d.stride(0), 0)
+        dview = d
+    else:
+        d = torch.empty((outer, inner, vocab), dtype=logits.dtype, device=logits.device)
+        ds = (d.stride(0), d.stride(1))
+        dview = d.transpose(1, 2)
+    g = None if grad is None else torch.tensor([grad], dtype=torch.float32, device=logits.device)
+    _capi.cross_entropy_bwd(logits.data_ptr(), vocab, outer, inner, ls, targets.data_ptr(), ts,
+                            ignore_index, row_lse.data_ptr(), mean.data_ptr(),
+                            g.data_ptr() if g is not None else None, d.data_ptr(), ds, code,
+                            stream())
+    return mean[0], row_loss, dview

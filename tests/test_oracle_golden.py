@@ -29,7 +29,7 @@ def test_all_golden_cases_present():
     assert set(golden_io.cases()) == {
         "cfg1_rmsnorm_f32", "cfg1_swiglu_f32", "reftest_rmsnorm_f32", "reftest_swiglu_f64",
         "rmsnorm_bf16", "rmsnorm_bf16_wf32", "swiglu_bf16", "rope_bf16", "rope_f32",
-        "add_rmsnorm_bf16", "gate_up_bf16",
+        "add_rmsnorm_bf16", "gate_up_bf16", "ce_f32", "ce_bf16",
     }
 
 
@@ -76,6 +76,25 @@ def test_gate_up_oracle_matches_reference():
     ge, ue, _ = po.gate_up_forward(t["x"], t["w_gate"], t["w_up"], "exact")
     tolerance.assert_close(t["gate"], ge, "gate_up gate")
     tolerance.assert_close(t["up"], ue, "gate_up up")
+
+
+@pytest.mark.parametrize("case", ["ce_f32", "ce_bf16"])
+def test_cross_entropy_oracle_matches_reference(case):
+    t, _ = golden_io.load(case)
+    logits, ids = t["logits"], t["input_ids"]
+    view, targets = logits[:, :-1, :].transpose(1, 2), ids[:, 1:]
+    loss = po.cross_entropy_forward(view, targets, mode="eager")
+    d = po.cross_entropy_backward(view, targets, mode="eager")
+    full = torch.zeros_like(logits)
+    full[:, :-1, :] = d.transpose(1, 2)
+    assert torch.equal(loss, t["loss"])
+    assert torch.equal(full, t["dlogits"])
+    tolerance.assert_close(t["loss"], po.cross_entropy_forward(view, targets, mode="exact"),
+                           f"{case} loss", torch.float32)
+    de = po.cross_entropy_backward(view, targets, mode="exact")
+    fe = torch.zeros(logits.shape, dtype=torch.float64)
+    fe[:, :-1, :] = de.transpose(1, 2)
+    tolerance.assert_close(t["dlogits"], fe, f"{case} dlogits")
 
 
 @pytest.mark.parametrize("case", ["cfg1_swiglu_f32", "reftest_swiglu_f64", "swiglu_bf16"])
