@@ -58,6 +58,28 @@ def measured_peaks(key: str = "hbm_gbs") -> tuple[float, str]:
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}[key], "fallback"
 
 
+def time_library_adamw(work, steps: int) -> float:
+    """ms per step of torch.optim.AdamW.step() on copies of the same parameters."""
+
+    params = [torch.nn.Parameter(p.clone()) for p in work.params]
+    for p, g in zip(params, work.grads):
+        p.grad = g
+    opt = torch.optim.AdamW(params, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    for _ in range(2):
+        opt.step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        opt.step()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    del opt, params
+    torch.cuda.empty_cache()
+    return ms
+
+
 def time_library_ce(work, steps: int) -> float:
     """ms per step of PyTorch's own cross-entropy forward + backward on the same logits."""
 
@@ -433,6 +455,22 @@ class OpWorkload:
             self.bytes = 3 * tokens * self.vocab * BF16
             self.launches_per_step = 3
             self.dominant = ("ce_bwd_kernel", 2 * tokens * self.vocab * BF16)
+        elif op == "adamw":
+            # One fused AdamW step over the fp32 parameters of 4 Llama-3-8B decoder layers
+            # (q, k, v, o, gate, up, down projections and the two norm weights per layer:
+            # 218 M parameters a layer), lr 3e-4, betas (0.9, 0.95), eps 1e-8, wd 0.1.
+            shapes = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096),
+                      (14336, 4096), (4096, 14336), (4096,), (4096,)] * 4
+            self.params = [torch.randn(s_, generator=gen, device=device) for s_ in shapes]
+            self.grads = [torch.randn(s_, generator=gen, device=device) for s_ in shapes]
+            self.m = [torch.zeros(s_, device=device) for s_ in shapes]
+            self.v = [torch.zeros(s_, device=device) for s_ in shapes]
+            self.nparams = sum(p_.numel() for p_ in self.params)
+            self.step_count = 0
+            self.bytes = 28 * self.nparams
+            self.launches_per_step = 1
+            self.units, self.unit = self.nparams, "params/s"
+            self.dominant = ("adamw_kernel", 28 * self.nparams)
         elif op == "swiglu":
             mk = lambda scale: [torch.randn((tokens, INTER), generator=gen, device=device, dtype=bf) * scale
                                 for _ in range(sets)]
@@ -461,9 +499,11 @@ class OpWorkload:
             raise SystemExit(f"unknown workload {op}")
         self.i = 0
         self.events_per_step = 1
+        if not hasattr(self, "units"):
+            self.units, self.unit = self.tokens, "tokens/s"
         self.traffic_key = {"rmsnorm": "rmsnorm_bwd", "swiglu": "swiglu_bwd", "rope": "rope_fwd",
                             "addnorm": "add_rmsnorm_bwd", "mlpup": "swiglu_gemm",
-                            "ce": "ce_bwd"}[op]
+                            "ce": "ce_bwd", "adamw": "adamw"}[op]
 
     def bytes_per_step(self) -> int:
         return self.bytes
@@ -521,6 +561,16 @@ class OpWorkload:
                                 self.targets.data_ptr(), (1, 0), -100, self.row_lse.data_ptr(),
                                 self.mean.data_ptr(), None, self.dlogits.data_ptr(),
                                 (self.vocab, 0), c.PT_BFLOAT16, stream)
+            if ev: ev[1].record()
+        elif self.op == "adamw":
+            self.step_count += 1
+            n = len(self.params)
+            if ev: ev[0].record()
+            c.adamw_step([p_.data_ptr() for p_ in self.params],
+                         [g_.data_ptr() for g_ in self.grads],
+                         [m_.data_ptr() for m_ in self.m], [v_.data_ptr() for v_ in self.v],
+                         [p_.numel() for p_ in self.params], [self.step_count] * n, [3e-4] * n,
+                         [0.1] * n, 0.9, 0.95, 1e-8, False, stream)
             if ev: ev[1].record()
         elif self.op == "swiglu":
             n = T * INTER
@@ -624,13 +674,14 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--workload", choices=["stack", "rmsnorm", "swiglu", "rope", "addnorm", "mlpup",
-                                           "ce"],
+                                           "ce", "adamw"],
                     default="stack",
                     help="stack = BASELINE config 5 (the headline); rmsnorm, swiglu, rope are "
                          "configs 2, 3 and 4, one op forward+backward per step, for per-kernel "
                          "measurement; addnorm = fused residual add + RMSNorm at config 2 shapes; "
                          "mlpup = the gate/up GEMMs with the SwiGLU epilogue (tcgen05); "
-                         "ce = cross-entropy forward + backward over a 128256 vocabulary")
+                         "ce = cross-entropy forward + backward over a 128256 vocabulary; "
+                         "adamw = one fused AdamW step over 4 Llama-3-8B layers of parameters")
     args = ap.parse_args()
     if args.workload != "stack":
         args.no_e2e = True
@@ -645,7 +696,8 @@ def main() -> None:
              "rope": "RoPE q+k fwd+bwd bf16 (BASELINE config 4)",
              "addnorm": "fused residual add + RMSNorm fwd+bwd bf16 h4096 (config 2 shapes)",
              "mlpup": "gate/up GEMMs + SwiGLU epilogue fwd bf16 4096->14336 (config 3/5 shapes)",
-             "ce": "cross-entropy fwd+bwd bf16, vocab 128256 (Llama-3 head)"}
+             "ce": "cross-entropy fwd+bwd bf16, vocab 128256 (Llama-3 head)",
+             "adamw": "AdamW step, fp32 params of 4 Llama-3-8B decoder layers (873 M)"}
     config = {
         "workload": names[args.workload],
         "layers": args.layers,
@@ -733,6 +785,10 @@ def main() -> None:
     tensor_bound = args.workload == "mlpup"
     library_ms = None
     library_what = None
+    if args.workload == "adamw":
+        library_ms = time_library_adamw(work, args.steps)
+        library_what = ("torch.optim.AdamW.step() (its default CUDA multi-tensor path, what "
+                        "the reference runs) on the same parameters")
     if args.workload == "ce":
         library_ms = time_library_ce(work, args.steps)
         library_what = ("PyTorch F.cross_entropy forward + backward on the bf16 logits "
@@ -756,8 +812,8 @@ def main() -> None:
     if rank == 0:
         line = {
             "metric": METRIC,
-            "value": world * work.tokens / (ms / 1e3),
-            "unit": "tokens/s",
+            "value": world * work.units / (ms / 1e3),
+            "unit": work.unit,
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
@@ -796,8 +852,8 @@ def main() -> None:
             "library_baseline": None if library_ms is None else {
                 "what": library_what,
                 "ms_per_step": library_ms,
-                "value": world * work.tokens / (library_ms / 1e3),
-                "unit": "tokens/s",
+                "value": world * work.units / (library_ms / 1e3),
+                "unit": work.unit,
             },
             "cpu_baseline": cpu,
             "e2e": e2e,

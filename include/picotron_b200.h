@@ -272,6 +272,24 @@ PT_API int pt_cross_entropy_bwd(const void* logits, int64_t vocab, int64_t outer
                                 int64_t dlogits_outer_stride, int64_t dlogits_inner_stride,
                                 int dtype, void* stream);
 
+/* ------------------------------------------------------------------ AdamW -------- */
+
+/* One fused AdamW step over num_tensors fp32 parameters (device pointers in host arrays):
+ * for tensor i, numels[i] elements of params[i], grads[i], exp_avgs[i] and exp_avg_sqs[i]
+ * (same layout, dense), at step steps[i] (the count after this step's increment, >= 1), with
+ * learning rate lrs[i] and weight decay weight_decays[i] (its parameter group's values).
+ * Computes torch.optim.AdamW's update (decoupled weight decay, amsgrad off, maximize as
+ * given) with the same fp32 operations and roundings as its CUDA multi-tensor path, so the
+ * results are bit-identical to it, in one read and one write of each array. Replaces the
+ * reserved fused-AdamW extension point of src/picotron/nn/triton_kernels/adamw.py:14-24
+ * (called from src/picotron/training/train_loop.py:98-100,168), whose fallback is that
+ * torch.optim.AdamW (train_loop.py:302-325). */
+PT_API int pt_adamw_step(float* const* params, const float* const* grads,
+                         float* const* exp_avgs, float* const* exp_avg_sqs,
+                         const int64_t* numels, const int64_t* steps, const double* lrs,
+                         const double* weight_decays, int num_tensors, double beta1,
+                         double beta2, double eps, int maximize, void* stream);
+
 /* ------------------------------------------------------------------- RoPE -------- */
 
 /* Rotary embedding of a 4-D tensor with logical shape sizes = [B, H, S, D] (the

@@ -208,6 +208,46 @@ def cross_entropy_backward(logits: Tensor, targets: Tensor, grad: float = 1.0,
     return d
 
 
+# --------------------------------------------------------------------------- AdamW --
+
+
+def adamw_step(param: Tensor, grad: Tensor, exp_avg: Tensor, exp_avg_sq: Tensor, step: int,
+               lr: float, betas: tuple[float, float], eps: float, weight_decay: float,
+               maximize: bool = False, mode: str = "eager"):
+    """One AdamW step of one parameter; returns (param, exp_avg, exp_avg_sq), new tensors.
+
+    The reference's optimizer step is torch.optim.AdamW built by the training loop
+    (src/picotron/training/train_loop.py:302-325; its fused extension point,
+    nn/triton_kernels/adamw.py:14-24, always falls back to it). eager: that optimizer's
+    update op for op in fp32 (torch/optim/adam.py, decoupled weight decay): param *= 1 - lr*wd;
+    exp_avg.lerp_(grad, 1 - beta1); exp_avg_sq = exp_avg_sq * beta2 + (1 - beta2) * grad^2;
+    denom = sqrt(exp_avg_sq) / sqrt(1 - beta2^step) + eps;
+    param += -(lr / (1 - beta1^step)) * exp_avg / denom; `step` is the count after this step.
+    exact: the same formula in float64 from the same inputs."""
+
+    _check_mode(mode)
+    beta1, beta2 = betas
+    if maximize:
+        grad = -grad
+    bc1 = 1 - beta1 ** step
+    bc2 = 1 - beta2 ** step
+    if mode == "exact":
+        p, g, m, v = param.double(), grad.double(), exp_avg.double(), exp_avg_sq.double()
+        p = p * (1 - lr * weight_decay)
+        m = m + (1 - beta1) * (g - m)
+        v = v * beta2 + (1 - beta2) * g * g
+        denom = v.sqrt() / bc2 ** 0.5 + eps
+        return p - (lr / bc1) * m / denom, m, v
+    p, m, v = param.clone(), exp_avg.clone(), exp_avg_sq.clone()
+    if weight_decay != 0:
+        p.mul_(1 - lr * weight_decay)
+    m.lerp_(grad, 1 - beta1)
+    v.mul_(beta2).addcmul_(grad, grad, value=1 - beta2)
+    denom = (v.sqrt() / bc2 ** 0.5).add_(eps)
+    p.addcdiv_(m, denom, value=-(lr / bc1))
+    return p, m, v
+
+
 # ------------------------------------------------------------------------------ RoPE --
 
 

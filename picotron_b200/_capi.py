@@ -73,6 +73,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pt_cross_entropy_bwd": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_ptr,
                                       _c_i64, _c_i64, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
                                       _c_i64, _c_i64, _c_int, _c_ptr]),
+    "pt_adamw_step": (_c_int, [ctypes.POINTER(_c_ptr), ctypes.POINTER(_c_ptr),
+                               ctypes.POINTER(_c_ptr), ctypes.POINTER(_c_ptr),
+                               ctypes.POINTER(_c_i64), ctypes.POINTER(_c_i64),
+                               ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
+                               _c_int, ctypes.c_double, ctypes.c_double, ctypes.c_double, _c_int,
+                               _c_ptr]),
     "pt_add_rmsnorm_fwd": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64,
                                     _c_ptr, _c_i64, _c_ptr, _c_i64, _c_i64, _c_int, _c_int,
                                     _c_float, _c_ptr]),
@@ -305,6 +311,22 @@ def cross_entropy_bwd(logits: int, vocab: int, outer: int, inner: int, logits_st
                                             grad_loss, dlogits, dlogits_strides[0],
                                             dlogits_strides[1], dtype, stream)
     _check("pt_cross_entropy_bwd", status, error_type)
+
+
+def adamw_step(params, grads, exp_avgs, exp_avg_sqs, numels, steps, lrs, weight_decays,
+               beta1: float, beta2: float, eps: float, maximize: bool, stream: int,
+               error_type: type[Exception] | None = None) -> None:
+    """One fused AdamW step over lists of device addresses (see pt_adamw_step)."""
+
+    n = len(params)
+    ptrs = lambda xs: (_c_ptr * n)(*[int(x) for x in xs])  # noqa: E731
+    status = library().pt_adamw_step(
+        ptrs(params), ptrs(grads), ptrs(exp_avgs), ptrs(exp_avg_sqs),
+        (_c_i64 * n)(*[int(x) for x in numels]), (_c_i64 * n)(*[int(x) for x in steps]),
+        (ctypes.c_double * n)(*[float(x) for x in lrs]),
+        (ctypes.c_double * n)(*[float(x) for x in weight_decays]), n, float(beta1),
+        float(beta2), float(eps), int(bool(maximize)), stream)
+    _check("pt_adamw_step", status, error_type)
 
 
 def take_device_error() -> int:

@@ -2,10 +2,11 @@
 
 Mirrors ``TritonKernelsConfig`` (src/picotron/config/config.py:72-92): six strict boolean
 opt-ins, all False by default. ``rmsnorm``, ``swiglu``, ``rope`` and ``cross_entropy``
-select the sm_100a kernels of this package (``cross_entropy`` through
-``kernels.CrossEntropyWithFallback(use_triton=...)``, as the reference's training loop
-builds its loss, train_loop.py:95-97); ``attention`` and ``adamw`` are accepted for config
-compatibility and select nothing here. ``module_kwargs`` maps the switches onto the
+select the sm_100a kernels of this package (``cross_entropy`` and ``adamw`` through
+``kernels.CrossEntropyWithFallback(use_triton=...)`` and
+``kernels.AdamWStepWithFallback(use_triton=...)``, as the reference's training loop builds
+them, train_loop.py:95-100); ``attention`` is accepted for config compatibility and selects
+nothing here. ``module_kwargs`` maps the switches onto the
 module constructor keywords (``use_triton_rmsnorm`` and friends) that the reference's
 decoder passes (picotron_decoder.py:78-101, nn/attention.py).
 """

@@ -1,0 +1,185 @@
+// Fused multi-tensor AdamW step on sm_100a: one pass over every parameter, reading param,
+// grad, exp_avg and exp_avg_sq once and writing param, exp_avg and exp_avg_sq once (28
+// bytes per fp32 element), for a whole list of tensors per launch.
+//
+// Replaces the reserved extension point of picotron (src/picotron/nn/triton_kernels/
+// adamw.py:14-24, AdamWStepWithFallback at :27-45, used by the training loop at
+// src/picotron/training/train_loop.py:98-100,168), whose fallback is torch.optim.AdamW as the
+// loop builds it (train_loop.py:302-325). On CUDA that optimizer runs its multi-tensor
+// ("foreach") implementation, a sequence of eight elementwise passes; this kernel performs
+// the same fp32 operations in the same order with the same roundings, so parameters and
+// optimizer state come out bit-identical:
+//
+//   p  = p * (1 - lr * wd)                 (scalar rounded to fp32 once, as torch does)
+//   m  = lerp(m, g, 1 - beta1)             (m + w * (g - m), fused multiply-add)
+//   v  = v * beta2;  v = v + (1 - beta2) * (g * g)      (product rounded, then fma)
+//   d  = sqrt(v) / sqrt(1 - beta2^t) + eps (correctly rounded sqrt and division)
+//   p  = p + (-lr / (1 - beta1^t)) * (m / d)            (quotient rounded, then fma)
+//
+// The per-tensor scalars are computed on the host in double precision exactly as the
+// reference's Python does and rounded to fp32 once.
+
+#include <cmath>
+
+#include "common.cuh"
+
+namespace pt {
+namespace {
+
+constexpr int kAdamThreads = 256;
+constexpr int kAdamBatch = 64;          // tensors per launch (kernel parameter block)
+constexpr int64_t kChunk = 65536;       // elements per work item
+
+struct AdamBatch {
+  float* param[kAdamBatch];
+  const float* grad[kAdamBatch];
+  float* exp_avg[kAdamBatch];
+  float* exp_avg_sq[kAdamBatch];
+  int64_t numel[kAdamBatch];
+  int64_t chunk_begin[kAdamBatch + 1];  // prefix sum of chunks per tensor
+  float step_size[kAdamBatch];          // -lr / (1 - beta1^t)
+  float bc2_sqrt[kAdamBatch];           // sqrt(1 - beta2^t)
+  float decay[kAdamBatch];              // 1 - lr * weight_decay
+  int count;
+};
+
+struct AdamScalars {
+  float w1;        // 1 - beta1 (lerp weight)
+  float beta2;
+  float c2;        // 1 - beta2
+  float eps;
+  int maximize;
+};
+
+__device__ __forceinline__ float lerp_ref(float self, float end, float w) {
+  // m + w * (g - m) for small weights, g - (g - m) * (1 - w) otherwise (the two branches
+  // of the reference's lerp, each contracted to one fma).
+  return fabsf(w) < 0.5f ? __fmaf_rn(w, __fsub_rn(end, self), self)
+                         : __fmaf_rn(-__fsub_rn(end, self), __fsub_rn(1.0f, w), end);
+}
+
+__device__ __forceinline__ void adam_elem(float& p, float g, float& m, float& v,
+                                          const AdamScalars& s, float decay, float step_size,
+                                          float bc2s) {
+  if (s.maximize) g = -g;
+  p = __fmul_rn(p, decay);
+  m = lerp_ref(m, g, s.w1);
+  v = __fmul_rn(v, s.beta2);
+  v = __fmaf_rn(s.c2, __fmul_rn(g, g), v);
+  const float d = __fadd_rn(__fdiv_rn(__fsqrt_rn(v), bc2s), s.eps);
+  p = __fmaf_rn(step_size, __fdiv_rn(m, d), p);
+}
+
+__global__ void __launch_bounds__(kAdamThreads)
+adamw_kernel(const __grid_constant__ AdamBatch batch, AdamScalars s) {
+  const int64_t total = batch.chunk_begin[batch.count];
+  int t = 0;
+  for (int64_t c = blockIdx.x; c < total; c += gridDim.x) {
+    while (c >= batch.chunk_begin[t + 1]) ++t;  // chunks are visited in increasing order
+    const int64_t begin = (c - batch.chunk_begin[t]) * kChunk;
+    const int64_t end = min(begin + kChunk, batch.numel[t]);
+    float* P = batch.param[t];
+    const float* G = batch.grad[t];
+    float* M = batch.exp_avg[t];
+    float* V = batch.exp_avg_sq[t];
+    const float decay = batch.decay[t], ss = batch.step_size[t], b2s = batch.bc2_sqrt[t];
+    const bool vec = ((reinterpret_cast<uintptr_t>(P) | reinterpret_cast<uintptr_t>(G) |
+                       reinterpret_cast<uintptr_t>(M) | reinterpret_cast<uintptr_t>(V)) &
+                      15u) == 0;
+    int64_t scalar_from = begin;
+    if (vec) {
+      const int64_t vec_end = begin + (end - begin) / 4 * 4;
+      for (int64_t i = begin + threadIdx.x * 4; i < vec_end; i += kAdamThreads * 4) {
+        float4 p = *reinterpret_cast<const float4*>(P + i);
+        const float4 g = __ldcs(reinterpret_cast<const float4*>(G + i));
+        float4 m = *reinterpret_cast<const float4*>(M + i);
+        float4 v = *reinterpret_cast<const float4*>(V + i);
+        adam_elem(p.x, g.x, m.x, v.x, s, decay, ss, b2s);
+        adam_elem(p.y, g.y, m.y, v.y, s, decay, ss, b2s);
+        adam_elem(p.z, g.z, m.z, v.z, s, decay, ss, b2s);
+        adam_elem(p.w, g.w, m.w, v.w, s, decay, ss, b2s);
+        *reinterpret_cast<float4*>(P + i) = p;
+        *reinterpret_cast<float4*>(M + i) = m;
+        *reinterpret_cast<float4*>(V + i) = v;
+      }
+      scalar_from = vec_end;
+    }
+    // The chunk's tail (or all of it when a pointer is not 16-byte aligned), one element
+    // per thread.
+    for (int64_t j = scalar_from + threadIdx.x; j < end; j += kAdamThreads) {
+      float p = P[j], m = M[j], v = V[j];
+      adam_elem(p, G[j], m, v, s, decay, ss, b2s);
+      P[j] = p;
+      M[j] = m;
+      V[j] = v;
+    }
+  }
+}
+
+}  // namespace
+}  // namespace pt
+
+using namespace pt;
+
+extern "C" {
+
+int pt_adamw_step(float* const* params, const float* const* grads, float* const* exp_avgs,
+                  float* const* exp_avg_sqs, const int64_t* numels, const int64_t* steps,
+                  const double* lrs, const double* weight_decays, int num_tensors, double beta1,
+                  double beta2, double eps, int maximize, void* stream) {
+  if (num_tensors < 0) return set_error(PT_ERR_INVALID_ARGUMENT, "num_tensors must be >= 0");
+  if (num_tensors == 0) return ok();
+  if (!params || !grads || !exp_avgs || !exp_avg_sqs || !numels || !steps || !lrs ||
+      !weight_decays)
+    return set_error(PT_ERR_INVALID_ARGUMENT, "a tensor list pointer is NULL");
+  if (!(beta1 >= 0.0 && beta1 < 1.0) || !(beta2 >= 0.0 && beta2 < 1.0) || !(eps >= 0.0))
+    return set_error(PT_ERR_INVALID_ARGUMENT, "betas must be in [0, 1) and eps >= 0");
+  int dev = 0, sms = 0;
+  if (int st = current_device_info(&dev, &sms)) return st;
+  AdamScalars sc;
+  sc.w1 = (float)(1.0 - beta1);
+  sc.beta2 = (float)beta2;
+  sc.c2 = (float)(1.0 - beta2);
+  sc.eps = (float)eps;
+  sc.maximize = maximize != 0;
+  cudaStream_t s = as_stream(stream);
+  int t = 0;
+  while (t < num_tensors) {
+    AdamBatch b;
+    b.count = 0;
+    b.chunk_begin[0] = 0;
+    for (; t < num_tensors && b.count < kAdamBatch; ++t) {
+      if (numels[t] < 0) return set_error(PT_ERR_SHAPE, "tensor %d has a negative numel", t);
+      if (steps[t] < 1) return set_error(PT_ERR_INVALID_ARGUMENT, "tensor %d: step must be >= 1", t);
+      if (numels[t] == 0) continue;
+      const char* what[4] = {"param", "grad", "exp_avg", "exp_avg_sq"};
+      const void* ptr[4] = {params[t], grads[t], exp_avgs[t], exp_avg_sqs[t]};
+      for (int k = 0; k < 4; ++k)
+        if (int st = check_device_ptr(ptr[k], what[k])) return st;
+      const int i = b.count++;
+      b.param[i] = params[t];
+      b.grad[i] = grads[t];
+      b.exp_avg[i] = exp_avgs[t];
+      b.exp_avg_sq[i] = exp_avg_sqs[t];
+      b.numel[i] = numels[t];
+      b.chunk_begin[i + 1] = b.chunk_begin[i] + (numels[t] + kChunk - 1) / kChunk;
+      // The reference's host arithmetic (torch.optim.AdamW, foreach path), in double:
+      // bias_correction1 = 1 - beta1 ** step; step_size = (lr / bias_correction1) * -1;
+      // bias_correction2_sqrt = (1 - beta2 ** step) ** 0.5; param scale 1 - lr * wd.
+      const double st = (double)steps[t];
+      const double bc1 = 1.0 - std::pow(beta1, st);
+      const double bc2 = 1.0 - std::pow(beta2, st);
+      b.step_size[i] = (float)((lrs[t] / bc1) * -1.0);
+      b.bc2_sqrt[i] = (float)std::pow(bc2, 0.5);
+      b.decay[i] = (float)(1.0 - lrs[t] * weight_decays[t]);
+    }
+    if (b.count == 0) continue;
+    const int64_t chunks = b.chunk_begin[b.count];
+    const int grid = (int)std::min<int64_t>(chunks, (int64_t)sms * 8);
+    adamw_kernel<<<grid, kAdamThreads, 0, s>>>(b, sc);
+    if (int st = check_launch("pt_adamw_step")) return st;
+  }
+  return ok();
+}
+
+}  // extern "C"

@@ -25,3 +25,7 @@ class TritonRoPEUnavailable(RuntimeError):
 class TritonCrossEntropyUnavailable(RuntimeError):
     """The sm_100a cross-entropy path cannot run these inputs (reference
     triton_kernels/cross_entropy.py:22)."""
+
+
+class TritonAdamWUnavailable(RuntimeError):
+    """The fused AdamW step cannot run this optimizer (reference triton_kernels/adamw.py:10)."""

@@ -4,15 +4,18 @@ Same public names as the reference package (src/picotron/nn/triton_kernels/__ini
 for RMSNorm, SwiGLU and RoPE, backed by the sm_100a CUDA library instead of Triton, plus
 ``fused_add_rms_norm`` (the decoder block's residual add fused into the following norm) and
 ``swiglu_gate_up`` (the MLP's gate/up projections with the activation as one tcgen05 GEMM),
-and the loss: ``triton_cross_entropy`` / ``CrossEntropyWithFallback`` (forward and backward).
+the loss: ``triton_cross_entropy`` / ``CrossEntropyWithFallback`` (forward and backward), and
+the optimizer step: ``triton_adamw_step`` / ``AdamWStepWithFallback``.
 """
 
 from picotron_b200.errors import (
+    TritonAdamWUnavailable,
     TritonCrossEntropyUnavailable,
     TritonRMSNormUnavailable,
     TritonRoPEUnavailable,
     TritonSwiGLUUnavailable,
 )
+from picotron_b200.kernels.adamw import AdamWStepWithFallback, triton_adamw_step
 from picotron_b200.kernels.cross_entropy import (
     CrossEntropyWithFallback,
     cross_entropy,
@@ -31,6 +34,9 @@ from picotron_b200.kernels.swiglu import (
 )
 
 __all__ = [
+    "AdamWStepWithFallback",
+    "TritonAdamWUnavailable",
+    "triton_adamw_step",
     "CrossEntropyWithFallback",
     "TritonCrossEntropyUnavailable",
     "cross_entropy",

@@ -83,6 +83,32 @@ def _ce(ce_mod, logits, input_ids, upcast):
     return {"loss": loss.detach(), "dlogits": lg.grad}
 
 
+def _adamw(adamw_mod, shapes, steps, seed):
+    """AdamW as the training loop builds it (train_loop.py:302-325: lr, betas, eps,
+    weight_decay), stepped through the reference's AdamWStepWithFallback with its fused
+    switch on (which falls back to optimizer.step(), adamw.py:27-45)."""
+
+    g = _gen(seed)
+    params = [torch.nn.Parameter(torch.randn(s, generator=g)) for s in shapes]
+    init = [p.detach().clone() for p in params]
+    opt = torch.optim.AdamW(params, lr=3e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    stepper = adamw_mod.AdamWStepWithFallback(use_triton=True)
+    out = {f"p{i}_init": t for i, t in enumerate(init)}
+    import warnings
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore", RuntimeWarning)
+        for k in range(steps):
+            for i, p in enumerate(params):
+                p.grad = torch.randn(p.shape, generator=g) * (0.5 + k)
+                out[f"g{i}_s{k}"] = p.grad.clone()
+            stepper.step(opt)
+    for i, p in enumerate(params):
+        out[f"p{i}"] = p.detach().clone()
+        out[f"m{i}"] = opt.state[p]["exp_avg"].clone()
+        out[f"v{i}"] = opt.state[p]["exp_avg_sq"].clone()
+    return out
+
+
 def _swiglu(ref, g, u, dy):
     gg = g.clone().requires_grad_(True)
     ug = u.clone().requires_grad_(True)
@@ -111,6 +137,7 @@ def main() -> None:
     sys.path.insert(0, args.reference_src)
     torch.set_num_threads(1)
     from picotron.nn import feedforward as ffn_mod
+    from picotron.nn.triton_kernels import adamw as adamw_mod
     from picotron.nn.triton_kernels import cross_entropy as ce_mod
     from picotron.nn import rope as rope_mod
     from picotron.nn.triton_kernels import rmsnorm as rms_ref
@@ -203,6 +230,13 @@ def main() -> None:
     res = _ce(ce_mod, lb, ids, upcast=True)
     written.append(golden_io.save("ce_bf16", {"logits": lb, "input_ids": ids, **res},
                                   {"seed": 5}))
+
+    # AdamW through the reference's optimizer-step object: three fp32 parameters, 4 steps,
+    # lr 3e-3, betas (0.9, 0.95), eps 1e-8, weight decay 0.1.
+    res = _adamw(adamw_mod, [(64, 32), (100,), (7, 13)], 4, 6)
+    written.append(golden_io.save("adamw_f32", res,
+                                  {"seed": 6, "steps": 4, "lr": 3e-3, "beta1": 0.9,
+                                   "beta2": 0.95, "eps": 1e-8, "weight_decay": 0.1}))
 
     # BASELINE config 3 family, bf16: gate, up ~ N(0,1) * 2, dy ~ N(0,1), [16, 1024].
     g = _gen(0)

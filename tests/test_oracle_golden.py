@@ -29,7 +29,7 @@ def test_all_golden_cases_present():
     assert set(golden_io.cases()) == {
         "cfg1_rmsnorm_f32", "cfg1_swiglu_f32", "reftest_rmsnorm_f32", "reftest_swiglu_f64",
         "rmsnorm_bf16", "rmsnorm_bf16_wf32", "swiglu_bf16", "rope_bf16", "rope_f32",
-        "add_rmsnorm_bf16", "gate_up_bf16", "ce_f32", "ce_bf16",
+        "add_rmsnorm_bf16", "gate_up_bf16", "ce_f32", "ce_bf16", "adamw_f32",
     }
 
 
@@ -95,6 +95,32 @@ def test_cross_entropy_oracle_matches_reference(case):
     fe = torch.zeros(logits.shape, dtype=torch.float64)
     fe[:, :-1, :] = de.transpose(1, 2)
     tolerance.assert_close(t["dlogits"], fe, f"{case} dlogits")
+
+
+def _replay_adamw(t, meta, mode):
+    out = []
+    for i in range(3):
+        p = t[f"p{i}_init"]
+        m, v = torch.zeros_like(p), torch.zeros_like(p)
+        if mode == "exact":
+            p, m, v = p.double(), m.double(), v.double()
+        for k in range(int(meta["steps"])):
+            p, m, v = po.adamw_step(p, t[f"g{i}_s{k}"], m, v, k + 1, float(meta["lr"]),
+                                    (float(meta["beta1"]), float(meta["beta2"])),
+                                    float(meta["eps"]), float(meta["weight_decay"]), mode=mode)
+        out.append((p, m, v))
+    return out
+
+
+def test_adamw_oracle_matches_reference():
+    t, meta = golden_io.load("adamw_f32")
+    for i, (p, m, v) in enumerate(_replay_adamw(t, meta, "eager")):
+        assert torch.equal(p, t[f"p{i}"]) and torch.equal(m, t[f"m{i}"])
+        assert torch.equal(v, t[f"v{i}"])
+    for i, (p, m, v) in enumerate(_replay_adamw(t, meta, "exact")):
+        tolerance.assert_close(t[f"p{i}"], p, f"adamw p{i}")
+        tolerance.assert_close(t[f"m{i}"], m, f"adamw m{i}")
+        tolerance.assert_close(t[f"v{i}"], v, f"adamw v{i}")
 
 
 @pytest.mark.parametrize("case", ["cfg1_swiglu_f32", "reftest_swiglu_f64", "swiglu_bf16"])
