@@ -812,8 +812,8 @@ def main() -> None:
     if rank == 0:
         line = {
             "metric": METRIC,
-            "value": world * work.units / (ms / 1e3),
-            "unit": work.unit,
+            "value": world * getattr(work, "units", work.tokens) / (ms / 1e3),
+            "unit": getattr(work, "unit", "tokens/s"),
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
@@ -852,8 +852,8 @@ def main() -> None:
             "library_baseline": None if library_ms is None else {
                 "what": library_what,
                 "ms_per_step": library_ms,
-                "value": world * work.units / (library_ms / 1e3),
-                "unit": work.unit,
+                "value": world * getattr(work, "units", work.tokens) / (library_ms / 1e3),
+                "unit": getattr(work, "unit", "tokens/s"),
             },
             "cpu_baseline": cpu,
             "e2e": e2e,
