@@ -119,6 +119,26 @@ template <typename T> __device__ __forceinline__ void unpack2(const uint4& v, fl
 __device__ __forceinline__ float2 neg2(float2 a) { return make_float2(-a.x, -a.y); }
 __device__ __forceinline__ float2 splat2(float a) { return make_float2(a, a); }
 
+// Division of 32-bit unsigned values by a runtime divisor d >= 1 with a multiply-high and
+// shifts (Granlund and Montgomery, "Division by invariant integers using multiplication",
+// 1994, the round-up method): with l = ceil(log2 d) and m = floor(2^32 (2^l - d) / d) + 1,
+// n / d = (t + ((n - t) >> 1)) >> (l - 1) where t = mulhi(n, m), exact for every 32-bit n.
+struct FastDiv {
+  uint32_t d = 1, m = 0, l = 0;
+  FastDiv() = default;
+  __host__ explicit FastDiv(uint32_t divisor) : d(divisor) {
+    if (d > 1) {
+      l = 32u - (uint32_t)__builtin_clz(d - 1);
+      m = (uint32_t)((((uint64_t)1 << 32) * (((uint64_t)1 << l) - d)) / d + 1);
+    }
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t n) const {
+    if (d == 1) return n;
+    const uint32_t t = __umulhi(n, m);
+    return (t + ((n - t) >> 1)) >> (l - 1);
+  }
+};
+
 // Round both lanes to T (nearest even) and widen back: the value a T store would keep.
 template <typename T> __device__ __forceinline__ float2 round2(float2 v);
 template <> __device__ __forceinline__ float2 round2<float>(float2 v) { return v; }

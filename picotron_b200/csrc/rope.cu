@@ -20,10 +20,11 @@ namespace pt {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kUnroll = 2;
+constexpr int kUnroll = 4;
 
 struct RopeGeom {
   uint32_t n0, n1, n2;          // outer sizes, outermost first (memory order of x)
+  FastDiv div_vpr, div_n2, div_n1;  // divisions of the flat vector index
   int64_t xs0, xs1, xs2;         // x strides of those dims (elements)
   int64_t os0, os1, os2;         // out strides
   int s_axis;                    // which of the three is the sequence axis
@@ -73,12 +74,12 @@ rope_vec(const T* __restrict__ x, T* __restrict__ out, const TT* __restrict__ co
     for (int k = 0; k < kUnroll; ++k) {
       const uint32_t idx = i0 + k * blockDim.x;
       if (idx >= total) continue;
-      vj[k] = idx % g.vpr;
-      uint32_t row = idx / g.vpr;
-      const uint32_t i2 = row % g.n2;
-      row /= g.n2;
-      const uint32_t i1 = row % g.n1;
-      const uint32_t i0_ = row / g.n1;
+      const uint32_t row = g.div_vpr.div(idx);
+      vj[k] = idx - row * g.vpr;
+      const uint32_t r2 = g.div_n2.div(row);
+      const uint32_t i2 = row - r2 * g.n2;
+      const uint32_t i0_ = g.div_n1.div(r2);
+      const uint32_t i1 = r2 - i0_ * g.n1;
       srow[k] = g.s_axis == 0 ? i0_ : (g.s_axis == 1 ? i1 : i2);
       xo[k] = (int64_t)i0_ * g.xs0 + (int64_t)i1 * g.xs1 + (int64_t)i2 * g.xs2;
       oo[k] = (int64_t)i0_ * g.os0 + (int64_t)i1 * g.os1 + (int64_t)i2 * g.os2;
@@ -195,6 +196,9 @@ int rope_impl(const void* x_, const int64_t* xst, void* out_, const int64_t* ost
   const int64_t total_vec = rows * (span / V);
   if (vec && total_vec < (int64_t)UINT32_MAX - (int64_t)kThreads * kUnroll * sms * 8) {
     g.vpr = (uint32_t)(span / V);
+    g.div_vpr = FastDiv(g.vpr);
+    g.div_n2 = FastDiv(g.n2 > 0 ? g.n2 : 1);
+    g.div_n1 = FastDiv(g.n1 > 0 ? g.n1 : 1);
     const int64_t blocks = (total_vec + (int64_t)kThreads * kUnroll - 1) / (kThreads * kUnroll);
     const int64_t cap = (int64_t)sms * (2048 / kThreads);
     const int grid = (int)std::max<int64_t>(1, std::min(blocks, cap));
