@@ -43,8 +43,16 @@ struct MaxSum {
   float m, s;
 };
 
+// 2^x on the special-function unit (PTX ex2.approx.ftz: relative error below 2^-22; results
+// under 2^-126 flush to zero, which is negligible next to a row's largest term, 1).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float scale_to(float a, float M) {
-  return a == -INFINITY ? 0.0f : exp2f((a - M) * kLog2e);
+  return a == -INFINITY ? 0.0f : fast_exp2((a - M) * kLog2e);
 }
 
 __device__ __forceinline__ MaxSum merge(MaxSum a, MaxSum b) {
@@ -52,20 +60,40 @@ __device__ __forceinline__ MaxSum merge(MaxSum a, MaxSum b) {
   return {M, a.s * scale_to(a.m, M) + b.s * scale_to(b.m, M)};
 }
 
-// Adds `n` values (fp32) to the running pair.
+// Per-thread running state: the max and two partial sums (paired FP32 lanes).
+struct Running {
+  float m = -INFINITY;
+  float2 s = make_float2(0.0f, 0.0f);
+};
+
+// Adds N values (N even, fp32) to the running state.
 template <int N>
-__device__ __forceinline__ void absorb(MaxSum& acc, const float* x) {
+__device__ __forceinline__ void absorb(Running& acc, const float* x) {
   float vmax = x[0];
 #pragma unroll
   for (int e = 1; e < N; ++e) vmax = fmaxf(vmax, x[e]);
   if (vmax > acc.m) {
-    acc.s *= scale_to(acc.m, vmax);
+    const float f = scale_to(acc.m, vmax);
+    acc.s = __fmul2_rn(acc.s, splat2(f));
     acc.m = vmax;
   }
   if (acc.m == -INFINITY) return;  // every value so far is -inf: nothing to add
-  const float mL = acc.m * kLog2e;
+  const float2 L2 = splat2(kLog2e), nmL2 = splat2(-acc.m * kLog2e);
 #pragma unroll
-  for (int e = 0; e < N; ++e) acc.s += exp2f(fmaf(x[e], kLog2e, -mL));
+  for (int e = 0; e < N; e += 2) {
+    const float2 t = __ffma2_rn(make_float2(x[e], x[e + 1]), L2, nmL2);
+    acc.s = __fadd2_rn(acc.s, make_float2(fast_exp2(t.x), fast_exp2(t.y)));
+  }
+}
+
+__device__ __forceinline__ void absorb1(Running& acc, float x) {
+  if (x > acc.m) {
+    const float f = scale_to(acc.m, x);
+    acc.s = __fmul2_rn(acc.s, splat2(f));
+    acc.m = x;
+  }
+  if (acc.m == -INFINITY) return;
+  acc.s.x += fast_exp2(fmaf(x, kLog2e, -acc.m * kLog2e));
 }
 
 __device__ __forceinline__ MaxSum block_merge(MaxSum v, MaxSum* red) {
@@ -104,12 +132,9 @@ ce_fwd_kernel(const T* __restrict__ logits, RowGrid lg, const int64_t* __restric
   __shared__ MaxSum red[kCeThreads / 32];
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const T* row = logits + lg.offset(r);
-    MaxSum acc{-INFINITY, 0.0f};
+    Running acc;
     const int64_t head = head_elems(row, vocab);
-    if (threadIdx.x < head) {
-      const float x = to_float(row[threadIdx.x]);
-      absorb<1>(acc, &x);
-    }
+    if (threadIdx.x < head) absorb1(acc, to_float(row[threadIdx.x]));
     const T* body = row + head;
     const int64_t nvec = (vocab - head) / V;
     int64_t v = threadIdx.x;
@@ -129,13 +154,11 @@ ce_fwd_kernel(const T* __restrict__ logits, RowGrid lg, const int64_t* __restric
       unpack<T>(ld_stream(body + v * V), x);
       absorb<V>(acc, x);
     }
-    for (int64_t c = head + nvec * V + threadIdx.x; c < vocab; c += kCeThreads) {
-      const float x = to_float(row[c]);
-      absorb<1>(acc, &x);
-    }
-    acc = block_merge(acc, red);
+    for (int64_t c = head + nvec * V + threadIdx.x; c < vocab; c += kCeThreads)
+      absorb1(acc, to_float(row[c]));
+    const MaxSum tot = block_merge(MaxSum{acc.m, acc.s.x + acc.s.y}, red);
     if (threadIdx.x == 0) {
-      const float lse = acc.m + logf(acc.s);
+      const float lse = tot.m + logf(tot.s);
       const int64_t t = targets[tg.offset(r)];
       float loss;
       if (t == ignore_index) {
@@ -203,9 +226,31 @@ ce_bwd_kernel(const T* __restrict__ logits, RowGrid lg, const int64_t* __restric
     const float nlL = -row_lse[r] * kLog2e;
     auto grad = [&](float x, int64_t c) {
       if (skip) return 0.0f;
-      float p = exp2f(fmaf(x, kLog2e, nlL));
+      float p = fast_exp2(fmaf(x, kLog2e, nlL));
       if (c == t) p -= 1.0f;
       return p * scale;
+    };
+    // V consecutive values from column c0: softmax pairs, the target's 1 subtracted before
+    // scaling (so a near-certain target keeps its precision), scaled by grad / count.
+    const float2 L2 = splat2(kLog2e), nlL2 = splat2(nlL), sc2 = splat2(skip ? 0.0f : scale);
+    auto grad_vec = [&](float* x, int64_t c0) {
+#pragma unroll
+      for (int e = 0; e < V; e += 2) {
+        const float2 tt = __ffma2_rn(make_float2(x[e], x[e + 1]), L2, nlL2);
+        x[e] = fast_exp2(tt.x);
+        x[e + 1] = fast_exp2(tt.y);
+      }
+      if ((uint64_t)(t - c0) < (uint64_t)V) {
+#pragma unroll
+        for (int e = 0; e < V; ++e)
+          if (c0 + e == t) x[e] -= 1.0f;
+      }
+#pragma unroll
+      for (int e = 0; e < V; e += 2) {
+        const float2 d = __fmul2_rn(make_float2(x[e], x[e + 1]), sc2);
+        x[e] = d.x;
+        x[e + 1] = d.y;
+      }
     };
     const int64_t head = head_elems(row, vocab);
     const bool vec_ok = head == head_elems(drow, vocab);
@@ -228,18 +273,14 @@ ce_bwd_kernel(const T* __restrict__ logits, RowGrid lg, const int64_t* __restric
       for (int u = 0; u < kCeUnroll; ++u) {
         float x[V];
         unpack<T>(raw[u], x);
-        const int64_t c0 = head + (v + u * kCeThreads) * V;
-#pragma unroll
-        for (int e = 0; e < V; ++e) x[e] = grad(x[e], c0 + e);
+        grad_vec(x, head + (v + u * kCeThreads) * V);
         st_stream(dbody + (v + u * kCeThreads) * V, pack<T>(x));
       }
     }
     for (; v < nvec; v += kCeThreads) {
       float x[V];
       unpack<T>(ld_stream(body + v * V), x);
-      const int64_t c0 = head + v * V;
-#pragma unroll
-      for (int e = 0; e < V; ++e) x[e] = grad(x[e], c0 + e);
+      grad_vec(x, head + v * V);
       st_stream(dbody + v * V, pack<T>(x));
     }
     for (int64_t c = head + nvec * V + threadIdx.x; c < vocab; c += kCeThreads)
