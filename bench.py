@@ -492,8 +492,9 @@ class OpWorkload:
 
             self.cos, self.sin = rotary_cos_sin(2048, 128, 500000.0, device=device, dtype=bf)
             self.bytes = 4 * (self.q[0].numel() + self.k[0].numel()) * BF16
-            self.launches_per_step = 4
-            self.dominant = ("rope_vec (q)", 2 * self.q[0].numel() * BF16)
+            self.launches_per_step = 2
+            self.dominant = ("rope_vec (q and k, forward)",
+                             2 * (self.q[0].numel() + self.k[0].numel()) * BF16)
             self.tokens = b * 2048
         else:
             raise SystemExit(f"unknown workload {op}")
@@ -582,14 +583,17 @@ class OpWorkload:
                                           self.du.data_ptr(), n, c.PT_BFLOAT16, stream), "bwd")
             if ev: ev[1].record()
         else:
-            for t, o, direction in ((self.q[i], self.qo, "fwd"), (self.k[i], self.ko, "fwd"),
-                                    (self.qo, self.q[i], "bwd"), (self.ko, self.k[i], "bwd")):
-                xv, ov = t.transpose(1, 2), o.transpose(1, 2)
-                first = ev is not None and t is self.q[i] and direction == "fwd"
+            # Query and key in one launch per direction, as RotaryEmbedding.forward calls it.
+            for (q, k, qo, ko, direction) in ((self.q[i], self.k[i], self.qo, self.ko, "fwd"),
+                                              (self.qo, self.ko, self.q[i], self.k[i], "bwd")):
+                qv, kv = q.transpose(1, 2), k.transpose(1, 2)
+                qov, kov = qo.transpose(1, 2), ko.transpose(1, 2)
+                first = ev is not None and direction == "fwd"
                 if first: ev[0].record()
-                c.rope(direction, xv.data_ptr(), xv.stride(), ov.data_ptr(), ov.stride(), xv.shape,
-                       self.cos.data_ptr(), self.sin.data_ptr(), self.cos.stride(0),
-                       c.PT_ROPE_INTERLEAVED, c.PT_BFLOAT16, c.PT_BFLOAT16, stream)
+                c.rope_qk(direction, qv.data_ptr(), qv.stride(), qov.data_ptr(), qov.stride(),
+                          qv.shape, kv.data_ptr(), kv.stride(), kov.data_ptr(), kov.stride(),
+                          kv.shape, self.cos.data_ptr(), self.sin.data_ptr(), self.cos.stride(0),
+                          c.PT_ROPE_INTERLEAVED, c.PT_BFLOAT16, c.PT_BFLOAT16, stream)
                 if first: ev[1].record()
 
 

@@ -1,5 +1,7 @@
 /*
- * picotron_b200.h -- C ABI of the B200 (sm_100a) RMSNorm / SwiGLU / RoPE hot path.
+ * picotron_b200.h -- C ABI of the B200 (sm_100a) RMSNorm / SwiGLU / RoPE hot path and the
+ * next-step kernels around it (fused residual add + RMSNorm, SwiGLU fused into the gate/up
+ * GEMM, cross-entropy, AdamW).
  *
  * This is the drop-in boundary for picotron's `model.triton_kernels.{rmsnorm,swiglu,rope}`
  * kernels. Every entry point takes plain device pointers, element counts, strides (in
@@ -21,6 +23,10 @@
  *   src/picotron/nn/triton_kernels/rope.py     -- triton_apply_rotary_embedding
  *   src/picotron/nn/rope.py                    -- apply_rotary_embedding (eager fwd + autograd bwd)
  *   src/picotron/utils/hardware.py             -- detect_triton_support (capability probe)
+ *   src/picotron/models/picotron_decoder.py    -- residual add + norm of the decoder block
+ *   src/picotron/nn/feedforward.py             -- SwiGLU gate/up projections + activation
+ *   src/picotron/nn/triton_kernels/cross_entropy.py, training/train_loop.py -- the loss
+ *   src/picotron/nn/triton_kernels/adamw.py    -- the (reserved) fused AdamW step
  */
 #ifndef PICOTRON_B200_H
 #define PICOTRON_B200_H
@@ -316,6 +322,22 @@ PT_API int pt_rope_bwd(const void* dy, const int64_t dy_strides[4],
                 const int64_t sizes[4],
                 const void* cosine, const void* sine, int64_t table_row_stride,
                 int layout, int dtype, int table_dtype, void* stream);
+
+/* pt_rope_fwd / pt_rope_bwd of a query and a key tensor that share head_dim, the sequence
+ * length and the tables, in one launch (the pair RotaryEmbedding.forward rotates,
+ * src/picotron/nn/rope.py:70-107). Each tensor has its own sizes and strides, as above. */
+PT_API int pt_rope_qk_fwd(const void* q, const int64_t q_strides[4], void* q_out,
+                          const int64_t q_out_strides[4], const int64_t q_sizes[4],
+                          const void* k, const int64_t k_strides[4], void* k_out,
+                          const int64_t k_out_strides[4], const int64_t k_sizes[4],
+                          const void* cosine, const void* sine, int64_t table_row_stride,
+                          int layout, int dtype, int table_dtype, void* stream);
+PT_API int pt_rope_qk_bwd(const void* dq, const int64_t dq_strides[4], void* dq_out,
+                          const int64_t dq_out_strides[4], const int64_t q_sizes[4],
+                          const void* dk, const int64_t dk_strides[4], void* dk_out,
+                          const int64_t dk_out_strides[4], const int64_t k_sizes[4],
+                          const void* cosine, const void* sine, int64_t table_row_stride,
+                          int layout, int dtype, int table_dtype, void* stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -79,6 +79,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
                                _c_int, ctypes.c_double, ctypes.c_double, ctypes.c_double, _c_int,
                                _c_ptr]),
+    "pt_rope_qk_fwd": (_c_int, [_c_ptr, _c_i64_4, _c_ptr, _c_i64_4, _c_i64_4, _c_ptr, _c_i64_4,
+                                _c_ptr, _c_i64_4, _c_i64_4, _c_ptr, _c_ptr, _c_i64, _c_int,
+                                _c_int, _c_int, _c_ptr]),
+    "pt_rope_qk_bwd": (_c_int, [_c_ptr, _c_i64_4, _c_ptr, _c_i64_4, _c_i64_4, _c_ptr, _c_i64_4,
+                                _c_ptr, _c_i64_4, _c_i64_4, _c_ptr, _c_ptr, _c_i64, _c_int,
+                                _c_int, _c_int, _c_ptr]),
     "pt_add_rmsnorm_fwd": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64,
                                     _c_ptr, _c_i64, _c_ptr, _c_i64, _c_i64, _c_int, _c_int,
                                     _c_float, _c_ptr]),
@@ -327,6 +333,19 @@ def adamw_step(params, grads, exp_avgs, exp_avg_sqs, numels, steps, lrs, weight_
         (ctypes.c_double * n)(*[float(x) for x in weight_decays]), n, float(beta1),
         float(beta2), float(eps), int(bool(maximize)), stream)
     _check("pt_adamw_step", status, error_type)
+
+
+def rope_qk(direction: str, q: int, q_strides, q_out: int, q_out_strides, q_sizes, k: int,
+            k_strides, k_out: int, k_out_strides, k_sizes, cosine: int, sine: int,
+            table_row_stride: int, layout: int, dtype: int, table_dtype: int, stream: int,
+            error_type: type[Exception] | None = None) -> None:
+    """Query and key in one launch; ``direction`` is "fwd" or "bwd" (see pt_rope_qk_fwd)."""
+
+    fn = library().pt_rope_qk_fwd if direction == "fwd" else library().pt_rope_qk_bwd
+    status = fn(q, _i64x4(q_strides), q_out, _i64x4(q_out_strides), _i64x4(q_sizes), k,
+                _i64x4(k_strides), k_out, _i64x4(k_out_strides), _i64x4(k_sizes), cosine, sine,
+                table_row_stride, layout, dtype, table_dtype, stream)
+    _check("pt_rope_qk_" + direction, status, error_type)
 
 
 def take_device_error() -> int:

@@ -60,13 +60,25 @@ __device__ __forceinline__ void load_table(const TT* p, float* f) {
   }
 }
 
+// Up to two tensors rotated by one launch (query and key share positions and tables): CTAs
+// [0, blocks0) walk tensor 0, the rest tensor 1, each in proportion to its size.
+template <typename T> struct RopeJobs {
+  RopeGeom g[2];
+  const T* x[2];
+  T* out[2];
+  uint32_t total[2];  // vectors
+  uint32_t blocks0;
+};
+
 template <typename T, typename TT, bool kRotateHalf>
-__global__ void __launch_bounds__(kThreads)
-rope_vec(const T* __restrict__ x, T* __restrict__ out, const TT* __restrict__ cosine,
-         const TT* __restrict__ sine, RopeGeom g, int half_dim, uint32_t total) {
+__device__ __forceinline__ void rope_vec_body(const T* __restrict__ x, T* __restrict__ out,
+                                              const TT* __restrict__ cosine,
+                                              const TT* __restrict__ sine, const RopeGeom& g,
+                                              int half_dim, uint32_t total, uint32_t block,
+                                              uint32_t nblocks) {
   constexpr int V = Vec16<T>::N;
-  const uint32_t step = gridDim.x * blockDim.x * kUnroll;
-  for (uint32_t i0 = blockIdx.x * blockDim.x * kUnroll + threadIdx.x; i0 < total; i0 += step) {
+  const uint32_t step = nblocks * blockDim.x * kUnroll;
+  for (uint32_t i0 = block * blockDim.x * kUnroll + threadIdx.x; i0 < total; i0 += step) {
     uint4 a[kUnroll], b[kUnroll];
     int64_t xo[kUnroll], oo[kUnroll];
     uint32_t srow[kUnroll], vj[kUnroll];
@@ -127,6 +139,20 @@ rope_vec(const T* __restrict__ x, T* __restrict__ out, const TT* __restrict__ co
   }
 }
 
+template <typename T, typename TT, bool kRotateHalf>
+__global__ void __launch_bounds__(kThreads)
+rope_vec(const __grid_constant__ RopeJobs<T> jobs, const TT* __restrict__ cosine,
+         const TT* __restrict__ sine, int half_dim) {
+  // Two copies of the loop, each reading its tensor's geometry at fixed parameter offsets.
+  if (blockIdx.x < jobs.blocks0)
+    rope_vec_body<T, TT, kRotateHalf>(jobs.x[0], jobs.out[0], cosine, sine, jobs.g[0],
+                                      half_dim, jobs.total[0], blockIdx.x, jobs.blocks0);
+  else
+    rope_vec_body<T, TT, kRotateHalf>(jobs.x[1], jobs.out[1], cosine, sine, jobs.g[1],
+                                      half_dim, jobs.total[1], blockIdx.x - jobs.blocks0,
+                                      gridDim.x - jobs.blocks0);
+}
+
 // Scalar path: one pair per thread iteration, any even D, any strides and alignment.
 template <typename T, typename TT, bool kRotateHalf>
 __global__ void __launch_bounds__(kThreads)
@@ -153,21 +179,14 @@ rope_scalar(const T* __restrict__ x, T* __restrict__ out, const TT* __restrict__
   }
 }
 
+// Geometry of one tensor: outer dims (B, H, S) ordered by decreasing x stride, and whether
+// the 16-byte vector path can take it.
 template <typename T, typename TT>
-int rope_impl(const void* x_, const int64_t* xst, void* out_, const int64_t* ost,
-              const int64_t* sizes, const void* cos_, const void* sin_, int64_t tstride,
-              int layout, float sign, cudaStream_t stream, const char* what) {
-  const T* x = static_cast<const T*>(x_);
-  T* out = static_cast<T*>(out_);
-  const TT* cosine = static_cast<const TT*>(cos_);
-  const TT* sine = static_cast<const TT*>(sin_);
-  int dev = 0, sms = 0;
-  if (int st = current_device_info(&dev, &sms)) return st;
-
-  // Order the outer dims (B, H, S) by decreasing x stride; remember where S went.
+bool make_geom(RopeGeom& g, const void* x, const int64_t* xst, const void* out,
+               const int64_t* ost, const int64_t* sizes, const void* cosine, const void* sine,
+               int64_t tstride, bool rh, float sign, int64_t* total_vec) {
   int order[3] = {0, 1, 2};
   std::stable_sort(order, order + 3, [&](int a, int b) { return xst[a] > xst[b]; });
-  RopeGeom g;
   g.n0 = (uint32_t)sizes[order[0]];
   g.n1 = (uint32_t)sizes[order[1]];
   g.n2 = (uint32_t)sizes[order[2]];
@@ -177,14 +196,11 @@ int rope_impl(const void* x_, const int64_t* xst, void* out_, const int64_t* ost
   g.table_stride = tstride;
   g.sign = sign;
   const int64_t D = sizes[3];
-  const int half = (int)(D / 2);
-  const bool rh = layout == PT_ROPE_ROTATE_HALF;
   const int64_t rows = sizes[0] * sizes[1] * sizes[2];
-
   constexpr int V = Vec16<T>::N;
   // Vector path: whole vectors per row, 16-byte aligned rows, table runs aligned to
   // their own size.
-  const int64_t span = rh ? half : D;  // elements covered by the vectors of one row
+  const int64_t span = rh ? D / 2 : D;  // elements covered by the vectors of one row
   const int tbytes = (rh ? V : V / 2) * (int)sizeof(TT);
   const int talign = tbytes >= 16 ? 16 : tbytes;
   bool vec = span % V == 0 && aligned16(x) && aligned16(out);
@@ -193,44 +209,97 @@ int rope_impl(const void* x_, const int64_t* xst, void* out_, const int64_t* ost
   vec = vec && (reinterpret_cast<uintptr_t>(cosine) % talign == 0) &&
         (reinterpret_cast<uintptr_t>(sine) % talign == 0) &&
         ((tstride * (int64_t)sizeof(TT)) % talign == 0);
-  const int64_t total_vec = rows * (span / V);
-  if (vec && total_vec < (int64_t)UINT32_MAX - (int64_t)kThreads * kUnroll * sms * 8) {
-    g.vpr = (uint32_t)(span / V);
-    g.div_vpr = FastDiv(g.vpr);
-    g.div_n2 = FastDiv(g.n2 > 0 ? g.n2 : 1);
-    g.div_n1 = FastDiv(g.n1 > 0 ? g.n1 : 1);
-    const int64_t blocks = (total_vec + (int64_t)kThreads * kUnroll - 1) / (kThreads * kUnroll);
+  *total_vec = rows * (span / V);
+  vec = vec && *total_vec < (int64_t)UINT32_MAX / 2;
+  g.vpr = (uint32_t)(span / V);
+  g.div_vpr = FastDiv(g.vpr > 0 ? g.vpr : 1);
+  g.div_n2 = FastDiv(g.n2 > 0 ? g.n2 : 1);
+  g.div_n1 = FastDiv(g.n1 > 0 ? g.n1 : 1);
+  return vec;
+}
+
+template <typename T, typename TT>
+void launch_scalar(const T* x, T* out, const TT* cosine, const TT* sine, const RopeGeom& g,
+                   int half, int64_t rows, bool rh, int sms, cudaStream_t stream) {
+  const int64_t total = rows * half;
+  const int64_t blocks = (total + kThreads - 1) / kThreads;
+  const int64_t cap = (int64_t)sms * (2048 / kThreads);
+  const int grid = (int)std::max<int64_t>(1, std::min(blocks, cap));
+  if (rh)
+    rope_scalar<T, TT, true><<<grid, kThreads, 0, stream>>>(x, out, cosine, sine, g, half, total);
+  else
+    rope_scalar<T, TT, false><<<grid, kThreads, 0, stream>>>(x, out, cosine, sine, g, half,
+                                                             total);
+}
+
+// Rotates one or two tensors (n = 1 or 2) that share head_dim, the sequence length and the
+// tables; two vector-path tensors go in one launch.
+template <typename T, typename TT>
+int rope_impl(int n, const void* const* xs, const int64_t* const* xsts, void* const* outs,
+              const int64_t* const* osts, const int64_t* const* sizes, const void* cos_,
+              const void* sin_, int64_t tstride, int layout, float sign, cudaStream_t stream,
+              const char* what) {
+  const TT* cosine = static_cast<const TT*>(cos_);
+  const TT* sine = static_cast<const TT*>(sin_);
+  int dev = 0, sms = 0;
+  if (int st = current_device_info(&dev, &sms)) return st;
+  const bool rh = layout == PT_ROPE_ROTATE_HALF;
+  const int half = (int)(sizes[0][3] / 2);
+  RopeJobs<T> jobs;
+  int nvec = 0;
+  for (int i = 0; i < n; ++i) {
+    const int64_t rows = sizes[i][0] * sizes[i][1] * sizes[i][2];
+    if (rows == 0) continue;
+    RopeGeom g;
+    int64_t total = 0;
+    const bool vec = make_geom<T, TT>(g, xs[i], xsts[i], outs[i], osts[i], sizes[i], cos_, sin_,
+                                      tstride, rh, sign, &total);
+    if (!vec) {
+      launch_scalar<T, TT>(static_cast<const T*>(xs[i]), static_cast<T*>(outs[i]), cosine,
+                           sine, g, half, rows, rh, sms, stream);
+      continue;
+    }
+    jobs.g[nvec] = g;
+    jobs.x[nvec] = static_cast<const T*>(xs[i]);
+    jobs.out[nvec] = static_cast<T*>(outs[i]);
+    jobs.total[nvec] = (uint32_t)total;
+    ++nvec;
+  }
+  if (nvec > 0) {
+    if (nvec == 1) {
+      jobs.g[1] = jobs.g[0];
+      jobs.x[1] = jobs.x[0];
+      jobs.out[1] = jobs.out[0];
+      jobs.total[1] = 0;
+    }
     const int64_t cap = (int64_t)sms * (2048 / kThreads);
-    const int grid = (int)std::max<int64_t>(1, std::min(blocks, cap));
+    const int64_t per_block = (int64_t)kThreads * kUnroll;
+    const int64_t need0 = (jobs.total[0] + per_block - 1) / per_block;
+    const int64_t need1 = (jobs.total[1] + per_block - 1) / per_block;
+    int64_t b0, b1;
+    if (need0 + need1 <= cap) {
+      b0 = need0;
+      b1 = need1;
+    } else {
+      // Split the resident CTAs in proportion to the work, at least one each.
+      b0 = std::max<int64_t>(1, (int64_t)((double)cap * jobs.total[0] /
+                                         ((double)jobs.total[0] + (double)jobs.total[1])));
+      b1 = jobs.total[1] > 0 ? std::max<int64_t>(1, cap - b0) : 0;
+    }
+    jobs.blocks0 = (uint32_t)b0;
+    const int grid = (int)std::max<int64_t>(1, b0 + b1);
     if (rh)
-      rope_vec<T, TT, true><<<grid, kThreads, 0, stream>>>(x, out, cosine, sine, g, half,
-                                                            (uint32_t)total_vec);
+      rope_vec<T, TT, true><<<grid, kThreads, 0, stream>>>(jobs, cosine, sine, half);
     else
-      rope_vec<T, TT, false><<<grid, kThreads, 0, stream>>>(x, out, cosine, sine, g, half,
-                                                             (uint32_t)total_vec);
-  } else {
-    g.vpr = 0;
-    const int64_t total = rows * half;
-    const int64_t blocks = (total + kThreads - 1) / kThreads;
-    const int64_t cap = (int64_t)sms * (2048 / kThreads);
-    const int grid = (int)std::max<int64_t>(1, std::min(blocks, cap));
-    if (rh)
-      rope_scalar<T, TT, true><<<grid, kThreads, 0, stream>>>(x, out, cosine, sine, g, half, total);
-    else
-      rope_scalar<T, TT, false><<<grid, kThreads, 0, stream>>>(x, out, cosine, sine, g, half,
-                                                               total);
+      rope_vec<T, TT, false><<<grid, kThreads, 0, stream>>>(jobs, cosine, sine, half);
   }
   return check_launch(what);
 }
 
-int rope_entry(const void* x, const int64_t* xst, void* out, const int64_t* ost,
-               const int64_t* sizes, const void* cosine, const void* sine, int64_t tstride,
-               int layout, int dtype, int table_dtype, float sign, void* stream,
-               const char* what) {
+int check_tensor(const void* x, const int64_t* xst, const void* out, const int64_t* ost,
+                 const int64_t* sizes, int64_t tstride, const char* what) {
   if (xst == nullptr || ost == nullptr || sizes == nullptr)
     return set_error(PT_ERR_INVALID_ARGUMENT, "%s: strides/sizes must not be NULL", what);
-  if (layout != PT_ROPE_INTERLEAVED && layout != PT_ROPE_ROTATE_HALF)
-    return set_error(PT_ERR_INVALID_ARGUMENT, "%s: unknown layout %d", what, layout);
   for (int i = 0; i < 4; ++i)
     if (sizes[i] < 0)
       return set_error(PT_ERR_SHAPE, "%s: sizes[%d] = %lld < 0", what, i, (long long)sizes[i]);
@@ -246,20 +315,39 @@ int rope_entry(const void* x, const int64_t* xst, void* out, const int64_t* ost,
   if (tstride < D / 2)
     return set_error(PT_ERR_SHAPE, "%s: table_row_stride (%lld) < head_dim/2 (%lld)", what,
                      (long long)tstride, (long long)(D / 2));
+  if (sizes[0] * sizes[1] * sizes[2] == 0) return PT_OK;
+  if (int st = check_device_ptr(x, "x")) return st;
+  if (int st = check_device_ptr(out, "out")) return st;
+  return PT_OK;
+}
+
+// n = 1 or 2 tensors sharing head_dim, sequence length and the cosine/sine tables.
+int rope_entry(int n, const void* const* xs, const int64_t* const* xsts, void* const* outs,
+               const int64_t* const* osts, const int64_t* const* sizes, const void* cosine,
+               const void* sine, int64_t tstride, int layout, int dtype, int table_dtype,
+               float sign, void* stream, const char* what) {
+  if (layout != PT_ROPE_INTERLEAVED && layout != PT_ROPE_ROTATE_HALF)
+    return set_error(PT_ERR_INVALID_ARGUMENT, "%s: unknown layout %d", what, layout);
+  int64_t rows = 0;
+  for (int i = 0; i < n; ++i) {
+    if (int st = check_tensor(xs[i], xsts[i], outs[i], osts[i], sizes[i], tstride, what))
+      return st;
+    rows += sizes[i][0] * sizes[i][1] * sizes[i][2];
+  }
+  if (n == 2 && (sizes[0][3] != sizes[1][3] || sizes[0][2] != sizes[1][2]))
+    return set_error(PT_ERR_SHAPE, "%s: query and key must share head_dim and sequence length",
+                     what);
   if (dtype_size(dtype) == 0 || dtype_size(table_dtype) == 0)
     return set_error(PT_ERR_UNSUPPORTED_DTYPE, "%s: unsupported dtype (%d, table %d)", what, dtype,
                      table_dtype);
-  const int64_t rows = sizes[0] * sizes[1] * sizes[2];
   if (rows == 0) return ok();
-  if (int st = check_device_ptr(x, "x")) return st;
-  if (int st = check_device_ptr(out, "out")) return st;
   if (int st = check_device_ptr(cosine, "cosine")) return st;
   if (int st = check_device_ptr(sine, "sine")) return st;
   cudaStream_t s = as_stream(stream);
 #define PT_ROPE_CASE(DT, T, TDT, TT)                                                        \
   if (dtype == DT && table_dtype == TDT)                                                    \
-    return rope_impl<T, TT>(x, xst, out, ost, sizes, cosine, sine, tstride, layout, sign, s, \
-                            what);
+    return rope_impl<T, TT>(n, xs, xsts, outs, osts, sizes, cosine, sine, tstride, layout,   \
+                            sign, s, what);
   PT_ROPE_CASE(PT_BFLOAT16, __nv_bfloat16, PT_BFLOAT16, __nv_bfloat16)
   PT_ROPE_CASE(PT_BFLOAT16, __nv_bfloat16, PT_FLOAT32, float)
   PT_ROPE_CASE(PT_FLOAT16, __half, PT_FLOAT16, __half)
@@ -280,15 +368,62 @@ extern "C" {
 int pt_rope_fwd(const void* x, const int64_t x_strides[4], void* out, const int64_t out_strides[4],
                 const int64_t sizes[4], const void* cosine, const void* sine,
                 int64_t table_row_stride, int layout, int dtype, int table_dtype, void* stream) {
-  return pt::rope_entry(x, x_strides, out, out_strides, sizes, cosine, sine, table_row_stride,
-                        layout, dtype, table_dtype, 1.0f, stream, "pt_rope_fwd");
+  const void* xs[1] = {x};
+  const int64_t* xst[1] = {x_strides};
+  void* outs[1] = {out};
+  const int64_t* ost[1] = {out_strides};
+  const int64_t* sz[1] = {sizes};
+  return pt::rope_entry(1, xs, xst, outs, ost, sz, cosine, sine, table_row_stride, layout, dtype,
+                        table_dtype, 1.0f, stream, "pt_rope_fwd");
 }
 
 int pt_rope_bwd(const void* dy, const int64_t dy_strides[4], void* dx, const int64_t dx_strides[4],
                 const int64_t sizes[4], const void* cosine, const void* sine,
                 int64_t table_row_stride, int layout, int dtype, int table_dtype, void* stream) {
-  return pt::rope_entry(dy, dy_strides, dx, dx_strides, sizes, cosine, sine, table_row_stride,
-                        layout, dtype, table_dtype, -1.0f, stream, "pt_rope_bwd");
+  const void* xs[1] = {dy};
+  const int64_t* xst[1] = {dy_strides};
+  void* outs[1] = {dx};
+  const int64_t* ost[1] = {dx_strides};
+  const int64_t* sz[1] = {sizes};
+  return pt::rope_entry(1, xs, xst, outs, ost, sz, cosine, sine, table_row_stride, layout, dtype,
+                        table_dtype, -1.0f, stream, "pt_rope_bwd");
+}
+
+static int rope_qk(const void* q, const int64_t q_strides[4], void* q_out,
+                   const int64_t q_out_strides[4], const int64_t q_sizes[4], const void* k,
+                   const int64_t k_strides[4], void* k_out, const int64_t k_out_strides[4],
+                   const int64_t k_sizes[4], const void* cosine, const void* sine,
+                   int64_t table_row_stride, int layout, int dtype, int table_dtype, float sign,
+                   void* stream, const char* what) {
+  const void* xs[2] = {q, k};
+  const int64_t* xst[2] = {q_strides, k_strides};
+  void* outs[2] = {q_out, k_out};
+  const int64_t* ost[2] = {q_out_strides, k_out_strides};
+  const int64_t* sz[2] = {q_sizes, k_sizes};
+  return pt::rope_entry(2, xs, xst, outs, ost, sz, cosine, sine, table_row_stride, layout, dtype,
+                        table_dtype, sign, stream, what);
+}
+
+int pt_rope_qk_fwd(const void* q, const int64_t q_strides[4], void* q_out,
+                   const int64_t q_out_strides[4], const int64_t q_sizes[4], const void* k,
+                   const int64_t k_strides[4], void* k_out, const int64_t k_out_strides[4],
+                   const int64_t k_sizes[4], const void* cosine, const void* sine,
+                   int64_t table_row_stride, int layout, int dtype, int table_dtype,
+                   void* stream) {
+  return rope_qk(q, q_strides, q_out, q_out_strides, q_sizes, k, k_strides, k_out, k_out_strides,
+                 k_sizes, cosine, sine, table_row_stride, layout, dtype, table_dtype, 1.0f,
+                 stream, "pt_rope_qk_fwd");
+}
+
+int pt_rope_qk_bwd(const void* dq, const int64_t dq_strides[4], void* dq_out,
+                   const int64_t dq_out_strides[4], const int64_t q_sizes[4], const void* dk,
+                   const int64_t dk_strides[4], void* dk_out, const int64_t dk_out_strides[4],
+                   const int64_t k_sizes[4], const void* cosine, const void* sine,
+                   int64_t table_row_stride, int layout, int dtype, int table_dtype,
+                   void* stream) {
+  return rope_qk(dq, dq_strides, dq_out, dq_out_strides, q_sizes, dk, dk_strides, dk_out,
+                 dk_out_strides, k_sizes, cosine, sine, table_row_stride, layout, dtype,
+                 table_dtype, -1.0f, stream, "pt_rope_qk_bwd");
 }
 
 }  // extern "C"

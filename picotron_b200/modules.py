@@ -211,6 +211,8 @@ class RotaryEmbedding(nn.Module):
         if self.use_triton_rope:
             if query.is_cuda and key.is_cuda:
                 layout = ops.LAYOUTS["interleaved"]
+                if query.dtype == key.dtype and query.device == key.device:
+                    return torch.ops.picotron_b200.rope_qk(query, key, cosine, sine, layout)
                 return (
                     torch.ops.picotron_b200.rope(query, cosine, sine, layout),
                     torch.ops.picotron_b200.rope(key, cosine, sine, layout),

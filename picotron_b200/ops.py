@@ -18,6 +18,8 @@ backward op:
 * ``cross_entropy_backward(grad, logits, targets, row_lse, mean_out, ignore_index) -> dlogits``
 * ``rope(x, cosine, sine, layout) -> out``           (reference nn/rope.py:35-51)
 * ``rope_backward(dy, cosine, sine, layout) -> dx``
+* ``rope_qk(q, k, cosine, sine, layout) -> (q_out, k_out)``  (query and key in one launch,
+  reference nn/rope.py:70-107) and ``rope_qk_backward``
 
 All ops run only on CUDA tensors of a compute-capability-10.0 device and launch on the
 current stream of the tensors' device. Any failure raises the reference's exception
@@ -645,3 +647,78 @@ def _rope_bwd(ctx, grad: Tensor):
 
 
 rope.register_autograd(_rope_bwd, setup_context=_rope_setup)
+
+
+def _rope_prepare(x: Tensor, cosine: Tensor, sine: Tensor, layout: int):
+    _validate_rope(x, cosine, sine, layout)
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    out = torch.empty_like(x)
+    if out.stride(-1) != 1:
+        out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    return x, out
+
+
+def _rope_qk_launch(direction: str, q: Tensor, k: Tensor, cosine: Tensor, sine: Tensor,
+                    layout: int) -> tuple[Tensor, Tensor]:
+    if q.dtype != k.dtype or q.device != k.device:
+        raise TritonRoPEUnavailable("query and key must share dtype and device.")
+    q, q_out = _rope_prepare(q, cosine, sine, layout)
+    k, k_out = _rope_prepare(k, cosine, sine, layout)
+    if cosine.stride(-1) != 1 or sine.stride(-1) != 1 or cosine.stride(0) != sine.stride(0):
+        cosine, sine = cosine.contiguous(), sine.contiguous()
+    if cosine.dtype not in (q.dtype, torch.float32):
+        cosine, sine = cosine.to(torch.float32), sine.to(torch.float32)
+    if q.numel() == 0 and k.numel() == 0:
+        return q_out, k_out
+    with _OnDevice(q.device):
+        _capi.rope_qk(direction, q.data_ptr(), q.stride(), q_out.data_ptr(), q_out.stride(),
+                      q.shape, k.data_ptr(), k.stride(), k_out.data_ptr(), k_out.stride(),
+                      k.shape, cosine.data_ptr(), sine.data_ptr(), cosine.stride(0), layout,
+                      DTYPE_CODES[q.dtype], DTYPE_CODES[cosine.dtype], _stream(q.device),
+                      TritonRoPEUnavailable)
+    return q_out, k_out
+
+
+@torch.library.custom_op("picotron_b200::rope_qk", mutates_args=())
+def rope_qk(q: Tensor, k: Tensor, cosine: Tensor, sine: Tensor,
+            layout: int) -> tuple[Tensor, Tensor]:
+    return _rope_qk_launch("fwd", q, k, cosine, sine, layout)
+
+
+def _rope_qk_fake(q, k, cosine, sine, layout):
+    return _rope_fake(q, cosine, sine, layout), _rope_fake(k, cosine, sine, layout)
+
+
+rope_qk.register_fake(_rope_qk_fake)
+
+
+@torch.library.custom_op("picotron_b200::rope_qk_backward", mutates_args=())
+def rope_qk_backward(dq: Tensor, dk: Tensor, cosine: Tensor, sine: Tensor,
+                     layout: int) -> tuple[Tensor, Tensor]:
+    return _rope_qk_launch("bwd", dq, dk, cosine, sine, layout)
+
+
+rope_qk_backward.register_fake(_rope_qk_fake)
+
+
+def _rope_qk_setup(ctx, inputs, output) -> None:
+    q, k, cosine, sine, layout = inputs
+    ctx.save_for_backward(cosine, sine)
+    ctx.layout = layout
+    ctx.q_meta = (q.shape, q.dtype, q.device)
+    ctx.k_meta = (k.shape, k.dtype, k.device)
+    ctx.set_materialize_grads(False)
+
+
+def _rope_qk_bwd(ctx, dq: Tensor | None, dk: Tensor | None):
+    cosine, sine = ctx.saved_tensors
+    if dq is None:
+        dq = torch.zeros(ctx.q_meta[0], dtype=ctx.q_meta[1], device=ctx.q_meta[2])
+    if dk is None:
+        dk = torch.zeros(ctx.k_meta[0], dtype=ctx.k_meta[1], device=ctx.k_meta[2])
+    gq, gk = torch.ops.picotron_b200.rope_qk_backward(dq, dk, cosine, sine, ctx.layout)
+    return gq, gk, None, None, None
+
+
+rope_qk.register_autograd(_rope_qk_bwd, setup_context=_rope_qk_setup)

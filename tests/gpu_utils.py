@@ -172,3 +172,13 @@ def cross_entropy(logits, targets, ignore_index=-100, grad=None, want_grad=True)
                             g.data_ptr() if g is not None else None, d.data_ptr(), ds, code,
                             stream())
     return mean[0], row_loss, dview
+
+
+def rope_qk(direction: str, q, k, cos, sin, layout: str = "interleaved"):
+    code = {"interleaved": _capi.PT_ROPE_INTERLEAVED, "rotate_half": _capi.PT_ROPE_ROTATE_HALF}
+    qo, ko = torch.empty_like(q), torch.empty_like(k)
+    _capi.rope_qk(direction, q.data_ptr(), q.stride(), qo.data_ptr(), qo.stride(), q.shape,
+                  k.data_ptr(), k.stride(), ko.data_ptr(), ko.stride(), k.shape, cos.data_ptr(),
+                  sin.data_ptr(), cos.stride(0), code[layout], DTYPE_CODES[q.dtype],
+                  DTYPE_CODES[cos.dtype], stream())
+    return qo, ko

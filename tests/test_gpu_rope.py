@@ -110,3 +110,23 @@ def test_full_size_config4_bf16():
         for layout in ("interleaved", "rotate_half"):
             _check(x, dy, cos, sin, layout, f"cfg4 h={heads} {layout}")
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("layout", ["interleaved", "rotate_half"])
+@pytest.mark.parametrize("direction", ["fwd", "bwd"])
+def test_query_and_key_in_one_launch(layout, direction):
+    # [B, S, H, D] memory seen as [B, H, S, D]; k with fewer heads (grouped-query attention).
+    from oracle import picotron_oracle as po
+    q = gu.randn((2, 96, 8, 128), 201, torch.bfloat16).transpose(1, 2)
+    k = gu.randn((2, 96, 2, 128), 202, torch.bfloat16).transpose(1, 2)
+    cos, sin = po.rotary_cos_sin(96, 128, 500_000.0, torch.bfloat16)
+    cos, sin = cos.to(gu.DEV), sin.to(gu.DEV)
+    qo, ko = gu.rope_qk(direction, q, k, cos, sin, layout)
+    assert torch.equal(qo, gu.rope(direction, q, cos, sin, layout))
+    assert torch.equal(ko, gu.rope(direction, k, cos, sin, layout))
+    # One tensor on the vector path, the other (odd offset) on the scalar path.
+    flat = gu.randn(k.numel() + 1, 203, torch.bfloat16)
+    k_odd = flat[1:].view(2, 96, 2, 128).transpose(1, 2)
+    qo2, ko2 = gu.rope_qk(direction, q, k_odd, cos, sin, layout)
+    assert torch.equal(qo2, qo)
+    assert torch.equal(ko2, gu.rope(direction, k_odd, cos, sin, layout))
