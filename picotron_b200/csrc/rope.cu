@@ -28,6 +28,8 @@ struct RopeGeom {
   int64_t xs0, xs1, xs2;         // x strides of those dims (elements)
   int64_t os0, os1, os2;         // out strides
   int s_axis;                    // which of the three is the sequence axis
+  bool same;                     // out strides == x strides
+  bool small;                    // every element offset of x and out is below 2^31
   uint32_t vpr;                  // vectors handled per row (per (b, h, s))
   int64_t table_stride;          // elements between table rows
   float sign;                    // +1 forward, -1 backward
@@ -93,8 +95,15 @@ __device__ __forceinline__ void rope_vec_body(const T* __restrict__ x, T* __rest
       const uint32_t i0_ = g.div_n1.div(r2);
       const uint32_t i1 = r2 - i0_ * g.n1;
       srow[k] = g.s_axis == 0 ? i0_ : (g.s_axis == 1 ? i1 : i2);
-      xo[k] = (int64_t)i0_ * g.xs0 + (int64_t)i1 * g.xs1 + (int64_t)i2 * g.xs2;
-      oo[k] = (int64_t)i0_ * g.os0 + (int64_t)i1 * g.os1 + (int64_t)i2 * g.os2;
+      if (g.small) {  // every offset fits in 32 bits: cheaper index arithmetic
+        xo[k] = (int64_t)(i0_ * (uint32_t)g.xs0 + i1 * (uint32_t)g.xs1 + i2 * (uint32_t)g.xs2);
+        oo[k] = g.same ? xo[k]
+                       : (int64_t)(i0_ * (uint32_t)g.os0 + i1 * (uint32_t)g.os1 +
+                                   i2 * (uint32_t)g.os2);
+      } else {
+        xo[k] = (int64_t)i0_ * g.xs0 + (int64_t)i1 * g.xs1 + (int64_t)i2 * g.xs2;
+        oo[k] = g.same ? xo[k] : (int64_t)i0_ * g.os0 + (int64_t)i1 * g.os1 + (int64_t)i2 * g.os2;
+      }
       const int64_t d0 = (int64_t)vj[k] * V;
       a[k] = ld_stream(x + xo[k] + d0);
       if (kRotateHalf) b[k] = ld_stream(x + xo[k] + d0 + half_dim);
@@ -197,6 +206,13 @@ bool make_geom(RopeGeom& g, const void* x, const int64_t* xst, const void* out,
   g.sign = sign;
   const int64_t D = sizes[3];
   const int64_t rows = sizes[0] * sizes[1] * sizes[2];
+  g.same = xst[0] == ost[0] && xst[1] == ost[1] && xst[2] == ost[2];
+  int64_t xmax = D, omax = D;
+  for (int i = 0; i < 3; ++i) {
+    xmax += (sizes[i] > 0 ? sizes[i] - 1 : 0) * xst[i];
+    omax += (sizes[i] > 0 ? sizes[i] - 1 : 0) * ost[i];
+  }
+  g.small = xmax < ((int64_t)1 << 31) && omax < ((int64_t)1 << 31);
   constexpr int V = Vec16<T>::N;
   // Vector path: whole vectors per row, 16-byte aligned rows, table runs aligned to
   // their own size.
