@@ -46,8 +46,11 @@ constexpr int kTmemCols = 2 * kAccCols;  // double-buffered: 512 columns (all of
 constexpr int kThreads = 256;        // warp 0 TMA, 1 MMA, 2 TMEM owner, 3 idle, 4-7 epilogue
 constexpr int kEpiWarp0 = 4;
 constexpr int kEpiWarps = kThreads / 32 - kEpiWarp0;
-constexpr int kGroupM = 16;          // m-tiles per raster group (L2 reuse of the weights)
-constexpr int kMaxStages = 6;
+#ifndef PT_GEMM_GROUP_M
+#define PT_GEMM_GROUP_M 16
+#endif
+constexpr int kGroupM = PT_GEMM_GROUP_M;  // m-tiles per raster group (L2 reuse of the weights)
+constexpr int kMaxStages = 7;
 constexpr long long kWaitCycles = 2000000000LL;  // about one second of SM clock
 
 // Two shapes of the same pipeline:
@@ -59,8 +62,11 @@ constexpr long long kWaitCycles = 2000000000LL;  // about one second of SM clock
 //    with M = 256, N = 256, which reads both CTAs' shared memory and leaves each CTA's 128
 //    rows of both accumulators in its own tensor memory. Per SM this halves the weight bytes
 //    moved per FLOP, so twice the bytes per SM can be in flight.
+#ifndef PT_GEMM_PAIR_STAGES
+#define PT_GEMM_PAIR_STAGES 6
+#endif
 template <bool kPair> struct Shape {
-  static constexpr int kStages = kPair ? 6 : 4;
+  static constexpr int kStages = kPair ? PT_GEMM_PAIR_STAGES : 4;
   static constexpr int kStageBytes = kATileBytes + (kPair ? 1 : 2) * kWTileBytes;
   static constexpr int kTileM = kPair ? 2 * kBM : kBM;
   static constexpr int kCtas = kPair ? 2 : 1;
