@@ -214,9 +214,11 @@ def init_distributed(gpus: int):
     if world > 1:
         import torch.distributed as dist
 
-        # rank 0 must print exactly one line on stdout: keep NCCL's version banner off it
+        # rank 0 must print exactly one line on stdout: NCCL writes its log, the version
+        # banner included, to stdout unless told otherwise, so send it to stderr.
         if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
             os.environ["NCCL_DEBUG"] = "WARN"
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
