@@ -561,26 +561,32 @@ rmsnorm_bwd_generic(const T* __restrict__ dy, int64_t dys, const T* __restrict__
 }
 
 constexpr int kReduceWarps = 32;
+constexpr int kReduceCols = 16;                    // columns per CTA (half a warp)
+constexpr int kReduceGroups = kReduceWarps * 2;    // row groups per CTA (half-warps)
 constexpr int kReduceUnroll = 4;
 
 template <typename TW>
 __global__ void __launch_bounds__(kReduceWarps * 32)
 rmsnorm_dw_reduce_kernel(const float* __restrict__ partials, int num_partials, int64_t hidden,
                          TW* __restrict__ dw) {
-  // 32 columns per CTA (one per lane). Warp w sums the partial rows p = w*U + u + i*W*U
-  // (u < U) into U independent doubly compensated (Sum2) fp32 accumulators, in increasing
-  // i; the U (sum, error) pairs are combined in fp64, the W warp sums are added in fp64 in
-  // warp order, and the result is rounded once. The order depends only on num_partials, so
-  // the result is deterministic, and Sum2 keeps it correctly rounded in practice even when
-  // the partials cancel.
-  __shared__ double s[kReduceWarps][33];
+  // 16 columns per CTA: each half-warp covers them (64-byte loads), and the 64 half-warps of
+  // the CTA split the partial rows: group g sums the rows p = g*U + u + i*G*U (u < U) into U
+  // independent doubly compensated (Sum2) fp32 accumulators, in increasing i; the U (sum,
+  // error) pairs are combined in fp64 and the G group sums are added in fp64 in group order,
+  // then rounded once. The order depends only on num_partials, so the result is
+  // deterministic, and Sum2 keeps it correctly rounded in practice even when the partials
+  // cancel. Twice as many CTAs as a warp-per-32-columns layout keeps every SM busy.
+  __shared__ double s[kReduceGroups][kReduceCols + 1];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t c = (int64_t)blockIdx.x * 32 + lane;
+  const int col = lane & (kReduceCols - 1);
+  const int group = warp * 2 + (lane >> 4);
+  const int64_t c = (int64_t)blockIdx.x * kReduceCols + col;
   float acc[kReduceUnroll], comp[kReduceUnroll];
 #pragma unroll
   for (int u = 0; u < kReduceUnroll; ++u) acc[u] = comp[u] = 0.0f;
   if (c < hidden) {
-    for (int p0 = warp * kReduceUnroll; p0 < num_partials; p0 += kReduceWarps * kReduceUnroll) {
+    for (int p0 = group * kReduceUnroll; p0 < num_partials;
+         p0 += kReduceGroups * kReduceUnroll) {
       float v[kReduceUnroll];
 #pragma unroll
       for (int u = 0; u < kReduceUnroll; ++u)
@@ -592,12 +598,12 @@ rmsnorm_dw_reduce_kernel(const float* __restrict__ partials, int num_partials, i
   double t = 0.0;
 #pragma unroll
   for (int u = 0; u < kReduceUnroll; ++u) t += (double)acc[u] + (double)comp[u];
-  s[warp][lane] = t;
+  s[group][col] = t;
   __syncthreads();
-  if (warp == 0 && c < hidden) {
+  if (threadIdx.x < kReduceCols && c < hidden) {
     double sum = 0.0;
-#pragma unroll
-    for (int i = 0; i < kReduceWarps; ++i) sum += s[i][lane];
+#pragma unroll 8
+    for (int i = 0; i < kReduceGroups; ++i) sum += s[i][col];
     dw[c] = from_float<TW>((float)sum);
   }
 }
@@ -1063,7 +1069,7 @@ int pt_rmsnorm_dw_reduce(const float* dw_partials, int num_partials, int64_t hid
     return set_error(PT_ERR_SHAPE, "hidden must be in [1, 2^30] (got %lld)", (long long)hidden);
   if (int st = check_device_ptr(dw_partials, "dw_partials")) return st;
   if (int st = check_device_ptr(dw, "dw")) return st;
-  const int grid = (int)((hidden + 31) / 32);
+  const int grid = (int)((hidden + kReduceCols - 1) / kReduceCols);
   const int threads = kReduceWarps * 32;
   cudaStream_t s = as_stream(stream);
   switch (dw_dtype) {
