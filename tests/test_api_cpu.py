@@ -204,3 +204,74 @@ def test_rotary_tables_match_reference_formula():
 
     rc, rs = po.rotary_cos_sin(16, 32, 500_000.0, torch.bfloat16)
     assert torch.equal(cos, rc) and torch.equal(sin, rs)
+
+
+def test_next_step_entry_points_on_cpu():
+    # The loss and optimizer-step objects keep the reference's CPU contract: with the switch
+    # on and CPU tensors they warn once (reference message) and use PyTorch.
+    from picotron_b200.kernels import (
+        AdamWStepWithFallback,
+        CrossEntropyWithFallback,
+        TritonAdamWUnavailable,
+        TritonCrossEntropyUnavailable,
+        fused_add_rms_norm,
+        swiglu_gate_up,
+        triton_adamw_step,
+        triton_cross_entropy,
+    )
+
+    logits, targets = torch.randn(2, 7, 5), torch.randint(0, 7, (2, 5))
+    loss_fn = CrossEntropyWithFallback(use_triton=True)
+    with pytest.warns(RuntimeWarning, match="Triton cross-entropy unavailable"):
+        loss = loss_fn(logits, targets)
+    torch.testing.assert_close(loss, F.cross_entropy(logits, targets))
+    with pytest.raises(TritonCrossEntropyUnavailable):
+        triton_cross_entropy(logits[:, :, 0], targets[:, 0])
+
+    p = torch.nn.Parameter(torch.randn(4))
+    p.grad = torch.randn(4)
+    opt = torch.optim.AdamW([p], lr=1e-2)
+    ref = torch.optim.AdamW([q := torch.nn.Parameter(p.detach().clone())], lr=1e-2)
+    q.grad = p.grad.clone()
+    with pytest.raises(TritonAdamWUnavailable):
+        triton_adamw_step(opt)
+    assert len(opt.state[p]) == 0  # refused before touching the state
+    with pytest.warns(RuntimeWarning, match="Triton AdamW unavailable"):
+        AdamWStepWithFallback(use_triton=True).step(opt)
+    ref.step()
+    assert torch.equal(p, q)
+
+    with pytest.raises(TritonRMSNormUnavailable):
+        fused_add_rms_norm(torch.randn(2, 8), torch.randn(2, 8), torch.ones(8), 1e-6)
+    with pytest.raises(TritonSwiGLUUnavailable):
+        swiglu_gate_up(torch.randn(2, 8), torch.randn(16, 8), torch.randn(16, 8))
+    # Module hooks take the eager steps on CPU.
+    norm = RMSNorm(8, use_triton_rmsnorm=False)
+    r, b = torch.randn(2, 8), torch.randn(2, 8)
+    h, y = norm.forward_with_residual(r, b)
+    torch.testing.assert_close(h, r + b)
+    torch.testing.assert_close(y, norm(r + b))
+    mlp = SwiGLU(8, 16)
+    mlp.fuse_gate_up = True
+    x = torch.randn(3, 8)
+    torch.testing.assert_close(
+        mlp(x), mlp.down_projection(F.silu(mlp.gate_projection(x)) * mlp.up_projection(x)))
+
+
+def test_fake_implementations_of_next_step_ops():
+    x = torch.empty(3, 5, 64, device="meta", dtype=torch.bfloat16)
+    w = torch.empty(64, device="meta", dtype=torch.float32)
+    h, y = torch.ops.picotron_b200.add_rms_norm(x, x, w, 1e-6)
+    assert h.shape == x.shape and y.shape == x.shape
+    wg = torch.empty(96, 64, device="meta", dtype=torch.bfloat16)
+    act, g, u = torch.ops.picotron_b200.swiglu_gate_up(x, wg, wg)
+    assert act.shape == (3, 5, 96) and g.shape == act.shape and u.dtype == torch.bfloat16
+    logits = torch.empty(2, 1000, 7, device="meta", dtype=torch.bfloat16)
+    targets = torch.empty(2, 7, device="meta", dtype=torch.long)
+    loss, lse, mean = torch.ops.picotron_b200.cross_entropy(logits, targets, -100)
+    assert loss.shape == () and lse.shape == (14,) and mean.shape == (2,)
+    q = torch.empty(2, 5, 4, 16, device="meta", dtype=torch.bfloat16).transpose(1, 2)
+    k = torch.empty(2, 5, 1, 16, device="meta", dtype=torch.bfloat16).transpose(1, 2)
+    cos = torch.empty(5, 8, device="meta", dtype=torch.bfloat16)
+    qo, ko = torch.ops.picotron_b200.rope_qk(q, k, cos, cos, ops.LAYOUTS["interleaved"])
+    assert qo.shape == q.shape and ko.shape == k.shape
