@@ -482,7 +482,12 @@ class OpWorkload:
             self.bytes = 8 * tokens * INTER * BF16
             self.launches_per_step = 2
             self.dominant = ("swiglu_bwd_vec", 5 * tokens * INTER * BF16)
-        elif op == "rope":
+        elif op in ("rope", "rope_rh"):
+            # rope: the reference's interleaved pairs; rope_rh: the rotate-half pairing that
+            # BASELINE config 4 names (same bytes, same kernel, other pair layout).
+            self.rope_layout = (_capi.PT_ROPE_ROTATE_HALF if op == "rope_rh"
+                                else _capi.PT_ROPE_INTERLEAVED)
+            op = self.op = "rope"
             # BASELINE config 4 per 2048-token sequence: q [B,S,32,128], k [B,S,8,128] memory.
             b = max(1, tokens // 2048)
             self.q = [torch.randn((b, 2048, 32, 128), generator=gen, device=device, dtype=bf)
@@ -595,7 +600,7 @@ class OpWorkload:
                 c.rope_qk(direction, qv.data_ptr(), qv.stride(), qov.data_ptr(), qov.stride(),
                           qv.shape, kv.data_ptr(), kv.stride(), kov.data_ptr(), kov.stride(),
                           kv.shape, self.cos.data_ptr(), self.sin.data_ptr(), self.cos.stride(0),
-                          c.PT_ROPE_INTERLEAVED, c.PT_BFLOAT16, c.PT_BFLOAT16, stream)
+                          self.rope_layout, c.PT_BFLOAT16, c.PT_BFLOAT16, stream)
                 if first: ev[1].record()
 
 
@@ -679,7 +684,7 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tokens", type=int, default=2048)
-    ap.add_argument("--workload", choices=["stack", "rmsnorm", "swiglu", "rope", "addnorm", "mlpup",
+    ap.add_argument("--workload", choices=["stack", "rmsnorm", "swiglu", "rope", "rope_rh", "addnorm", "mlpup",
                                            "ce", "adamw"],
                     default="stack",
                     help="stack = BASELINE config 5 (the headline); rmsnorm, swiglu, rope are "
@@ -699,7 +704,8 @@ def main() -> None:
     names = {"stack": "llama3-8b norm/act stack (BASELINE config 5)",
              "rmsnorm": "RMSNorm fwd+bwd bf16 h4096 (BASELINE config 2)",
              "swiglu": "SwiGLU fwd+bwd bf16 i14336 (BASELINE config 3)",
-             "rope": "RoPE q+k fwd+bwd bf16 (BASELINE config 4)",
+             "rope": "RoPE q+k fwd+bwd bf16 (BASELINE config 4), interleaved pairs (reference)",
+             "rope_rh": "RoPE q+k fwd+bwd bf16 (BASELINE config 4), rotate-half pairs",
              "addnorm": "fused residual add + RMSNorm fwd+bwd bf16 h4096 (config 2 shapes)",
              "mlpup": "gate/up GEMMs + SwiGLU epilogue fwd bf16 4096->14336 (config 3/5 shapes)",
              "ce": "cross-entropy fwd+bwd bf16, vocab 128256 (Llama-3 head)",
