@@ -22,7 +22,9 @@ __device__ int g_ce_error = 0;
 
 namespace {
 
-constexpr int kCeThreads = 256;
+// One row per 128-thread CTA (A/B on B200 at 16384 x 128256 bf16: forward 0.92 and backward
+// 0.92 of the HBM peak, against 0.85 / 0.87 with 256 threads): more rows in flight per SM.
+constexpr int kCeThreads = 128;
 constexpr int kCeUnroll = 4;
 constexpr int kMeanThreads = 1024;
 constexpr float kLog2e = 1.4426950408889634f;  // log2(e): exp(a) = 2^(a * log2(e))

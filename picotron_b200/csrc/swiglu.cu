@@ -16,7 +16,8 @@
 namespace pt {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 256;      // forward and scalar paths
+constexpr int kThreadsBwd = 512;   // backward vector path (A/B on B200: 0.94 vs 0.92 with 256)
 constexpr int kUnrollFwd = 4;
 constexpr int kUnrollBwd = 2;
 
@@ -52,7 +53,7 @@ swiglu_fwd_vec(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__
 }
 
 template <typename T, int U>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreadsBwd)
 swiglu_bwd_vec(const T* __restrict__ dout, const T* __restrict__ g, const T* __restrict__ u,
                T* __restrict__ dg, T* __restrict__ du, int64_t nvec) {
   constexpr int V = Vec16<T>::N;
@@ -117,8 +118,8 @@ swiglu_bwd_scalar(const T* __restrict__ dout, const T* __restrict__ g, const T* 
   }
 }
 
-int grid_for(int64_t work_items, int sms, int per_sm) {
-  const int64_t blocks = (work_items + kThreads - 1) / kThreads;
+int grid_for(int64_t work_items, int sms, int per_sm, int threads = kThreads) {
+  const int64_t blocks = (work_items + threads - 1) / threads;
   const int64_t cap = (int64_t)sms * per_sm;
   int64_t gsz = blocks < cap ? blocks : cap;
   return (int)(gsz < 1 ? 1 : gsz);
@@ -163,8 +164,9 @@ int bwd_impl(const void* o_, const void* g_, const void* u_, void* dg_, void* du
   if (vec) {
     const int64_t nvec = n / V;
     if (nvec > 0) {
-      const int grid = grid_for((nvec + kUnrollBwd - 1) / kUnrollBwd, sms, 2048 / kThreads);
-      swiglu_bwd_vec<T, kUnrollBwd><<<grid, kThreads, 0, s>>>(o, g, u, dg, du, nvec);
+      const int grid = grid_for((nvec + kUnrollBwd - 1) / kUnrollBwd, sms, 2048 / kThreadsBwd,
+                                kThreadsBwd);
+      swiglu_bwd_vec<T, kUnrollBwd><<<grid, kThreadsBwd, 0, s>>>(o, g, u, dg, du, nvec);
     }
     done = nvec * V;
   }
