@@ -12,13 +12,15 @@
 //
 // One persistent CTA per SM walks 128 x 128 output tiles. Per tile and per 64-wide K block,
 // one TMA producer thread loads the x tile [128 x 64] and the gate and up weight tiles
-// [128 x 64] each (128-byte swizzle) into a 4-stage shared-memory ring; one MMA thread issues
+// [128 x 64] each (128-byte swizzle) into a 3-stage shared-memory ring; one MMA thread issues
 // tcgen05.mma (kind::f16, M = 128, N = 256: the gate rows and the up rows of the B tile side
 // by side, so one instruction produces both accumulators) into one of two 256-column tensor
 // memory buffers; four epilogue warps read the finished buffer with tcgen05.ld while the next
-// tile accumulates into the other. Barriers are mbarriers with bounded waits: a wait that
+// tile accumulates into the other, stage each 32 x 32 output block in shared memory and write
+// it with a TMA store. Barriers are mbarriers with bounded waits: a wait that
 // runs out records an error word (pt_take_device_error) and the kernel drains its copies and
-// MMAs, frees its tensor memory and returns. No cluster launch and no multicast of any kind.
+// MMAs, frees its tensor memory and returns. Large m runs the CTA-pair shape described below;
+// no TMA load uses cluster multicast (each CTA loads its own tiles).
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -52,25 +54,33 @@ constexpr int kEpiWarps = kThreads / 32 - kEpiWarp0;
 constexpr int kGroupM = PT_GEMM_GROUP_M;  // m-tiles per raster group (L2 reuse of the weights)
 constexpr int kMaxStages = 7;
 constexpr long long kWaitCycles = 2000000000LL;  // about one second of SM clock
+// Epilogue staging: each epilogue warp writes its 32 rows x 32 columns of act, gate and up
+// (bf16/fp16: 64 bytes a row) into shared memory in the 64-byte swizzle pattern and hands
+// them to TMA stores, instead of scattered 16-byte global stores from every thread.
+constexpr int kEpiCols = 32;
+constexpr int kStageOut = 32 * kEpiCols * 2;               // one 32 x 32 16-bit tile: 2 KB
+constexpr int kEpiBufs = 2;  // double-buffered: a chunk is staged while the last one is stored
+constexpr int kStagingBytes = kEpiWarps * kEpiBufs * 3 * kStageOut;  // per warp: (act, gate, up)
 
 // Two shapes of the same pipeline:
 //  * single CTA (kPair = false): a 128 x 128 tile per CTA; each stage holds the x tile and
-//    both weight tiles (48 KB), 4 stages; tcgen05.mma cta_group::1 with M = 128, N = 256.
+//    both weight tiles (48 KB), 3 stages; tcgen05.mma cta_group::1 with M = 128, N = 256.
 //  * CTA pair (kPair = true, a cluster of two CTAs on two SMs): a 256 x 128 tile per pair;
 //    each CTA stages its own 128 rows of x and one weight tile (the even CTA the gate rows,
-//    the odd CTA the up rows: 32 KB), 6 stages; the even CTA issues tcgen05.mma cta_group::2
+//    the odd CTA the up rows: 32 KB), 5 stages; the even CTA issues tcgen05.mma cta_group::2
 //    with M = 256, N = 256, which reads both CTAs' shared memory and leaves each CTA's 128
 //    rows of both accumulators in its own tensor memory. Per SM this halves the weight bytes
 //    moved per FLOP, so twice the bytes per SM can be in flight.
 #ifndef PT_GEMM_PAIR_STAGES
-#define PT_GEMM_PAIR_STAGES 6
+#define PT_GEMM_PAIR_STAGES 5
 #endif
 template <bool kPair> struct Shape {
-  static constexpr int kStages = kPair ? PT_GEMM_PAIR_STAGES : 4;
+  static constexpr int kStages = kPair ? PT_GEMM_PAIR_STAGES : 3;
   static constexpr int kStageBytes = kATileBytes + (kPair ? 1 : 2) * kWTileBytes;
   static constexpr int kTileM = kPair ? 2 * kBM : kBM;
   static constexpr int kCtas = kPair ? 2 : 1;
-  static constexpr int kSmemBytes = 1024 /* alignment slack */ + kStages * kStageBytes + 256;
+  static constexpr int kSmemBytes =
+      1024 /* alignment slack */ + kStages * kStageBytes + kStagingBytes + 256;
 };
 static_assert(Shape<false>::kStages <= kMaxStages && Shape<true>::kStages <= kMaxStages, "");
 
@@ -144,6 +154,46 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
         : "memory");
   }
+}
+
+// 2-D tiled TMA store of a {kEpiCols, 32} box from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y,
+                                             uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], "
+      "[%1], %4;"
+      :
+      : "l"(reinterpret_cast<uint64_t>(map)), "r"(src), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+// L2 policy that marks written lines first to be evicted: the outputs are not re-read by
+// this kernel, the x and weight tiles are (A/B on B200: about 1 % faster than no hint).
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until at most kPending committed bulk-store groups of this thread still read shared
+// memory.
+template <int kPending>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kPending) : "memory");
+}
+// Wait until every committed bulk store of this thread has completed.
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy reads.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// Byte offset of 16-byte chunk `chunk` of row `row` in a tile of 64-byte rows laid out as TMA
+// reads it with 64-byte swizzle: the chunk index is XORed with bits 1-2 of the row.
+__device__ __forceinline__ uint32_t swz64(int row, int chunk) {
+  return (uint32_t)(row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4));
 }
 
 // Shared-memory matrix descriptor of a K-major operand tile stored as TMA wrote it with
@@ -304,15 +354,18 @@ struct TileGrid {
 template <typename T, bool kPair>
 __device__ __forceinline__ void swiglu_gemm_body(const CUtensorMap* map_x,
                                                  const CUtensorMap* map_wg,
-                                                 const CUtensorMap* map_wu, T* act,
-                                                 int64_t act_stride, T* gate_out, T* up_out,
-                                                 int64_t pre_stride, int m, int n, int k) {
+                                                 const CUtensorMap* map_wu,
+                                                 const CUtensorMap* map_act,
+                                                 const CUtensorMap* map_gate,
+                                                 const CUtensorMap* map_up, int save_pre, int m,
+                                                 int n, int k) {
   using S = Shape<kPair>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   const uint32_t pad = ((raw + 1023u) & ~1023u) - raw;
   unsigned char* tiles = smem_raw + pad;
-  GemmBarriers* bars = reinterpret_cast<GemmBarriers*>(tiles + S::kStages * S::kStageBytes);
+  unsigned char* staging = tiles + S::kStages * S::kStageBytes;  // 1024-byte aligned
+  GemmBarriers* bars = reinterpret_cast<GemmBarriers*>(staging + kStagingBytes);
   const uint32_t tiles_addr = raw + pad;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -431,6 +484,7 @@ __device__ __forceinline__ void swiglu_gemm_body(const CUtensorMap* map_x,
     const int q = warp & 3;  // this warp may read tensor-memory lanes [32q, 32q + 32)
     const uint32_t empty_addr0 = kPair ? peer_addr(&bars->tmem_empty[0], 0)
                                        : smem_addr(&bars->tmem_empty[0]);
+    const uint64_t policy = evict_first_policy();
     int i = 0;
     for (int t = unit; t < grid.count(); t += units, ++i) {
       const int b = i & 1;
@@ -441,44 +495,57 @@ __device__ __forceinline__ void swiglu_gemm_body(const CUtensorMap* map_x,
       tc_fence_after();
       int mb, nb;
       grid.coords(t, mb, nb);
-      const int row = mb * S::kTileM + (int)rank * kBM + q * 32 + lane;
+      const int row0 = mb * S::kTileM + (int)rank * kBM + q * 32;  // this warp's rows
       const uint32_t tg = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * kAccCols);
+      unsigned char* st0 = staging + (size_t)(warp - kEpiWarp0) * kEpiBufs * 3 * kStageOut;
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
+      for (int c = 0; c < kBN / kEpiCols; ++c) {
+        unsigned char* st = st0 + (c % kEpiBufs) * 3 * kStageOut;
+        const uint32_t st_addr = smem_addr(st);
         uint32_t gr[32], ur[32];
-        tmem_ld32(tg + c * 32, gr);
-        tmem_ld32(tg + kBN + c * 32, ur);
+        tmem_ld32(tg + c * kEpiCols, gr);
+        tmem_ld32(tg + kBN + c * kEpiCols, ur);
         tmem_wait_ld();
         reg_fence32(gr);
         reg_fence32(ur);
-        const int col0 = nb * kBN + c * 32;
-        if (row < m) {
+        // The TMA stores that last used this staging buffer must have read it.
+        if (lane == 0) bulk_wait_read<kEpiBufs - 1>();
+        __syncwarp();
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const int col = col0 + v * 8;
-            if (col >= n) break;  // n is a multiple of 8: vectors are all in or all out
-            float g8[8], u8[8], a8[8];
+        for (int v = 0; v < 4; ++v) {  // 16-byte chunk v of this thread's row
+          float g8[8], u8[8], a8[8];
 #pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-              // gate and up as stored (rounded to T); the activation uses those values.
-              const float2 g2 = round2<T>(make_float2(__uint_as_float(gr[v * 8 + e]),
-                                                      __uint_as_float(gr[v * 8 + e + 1])));
-              const float2 u2 = round2<T>(make_float2(__uint_as_float(ur[v * 8 + e]),
-                                                      __uint_as_float(ur[v * 8 + e + 1])));
-              g8[e] = g2.x;
-              g8[e + 1] = g2.y;
-              u8[e] = u2.x;
-              u8[e + 1] = u2.y;
-              a8[e] = (g2.x * sigmoid_f32(g2.x)) * u2.x;
-              a8[e + 1] = (g2.y * sigmoid_f32(g2.y)) * u2.y;
-            }
-            *reinterpret_cast<uint4*>(act + (int64_t)row * act_stride + col) = pack<T>(a8);
-            if (gate_out != nullptr) {
-              *reinterpret_cast<uint4*>(gate_out + (int64_t)row * pre_stride + col) =
-                  pack<T>(g8);
-              *reinterpret_cast<uint4*>(up_out + (int64_t)row * pre_stride + col) = pack<T>(u8);
-            }
+          for (int e = 0; e < 8; e += 2) {
+            // gate and up as stored (rounded to T); the activation uses those values.
+            const float2 g2 = round2<T>(make_float2(__uint_as_float(gr[v * 8 + e]),
+                                                    __uint_as_float(gr[v * 8 + e + 1])));
+            const float2 u2 = round2<T>(make_float2(__uint_as_float(ur[v * 8 + e]),
+                                                    __uint_as_float(ur[v * 8 + e + 1])));
+            g8[e] = g2.x;
+            g8[e + 1] = g2.y;
+            u8[e] = u2.x;
+            u8[e + 1] = u2.y;
+            a8[e] = (g2.x * sigmoid_f32(g2.x)) * u2.x;
+            a8[e + 1] = (g2.y * sigmoid_f32(g2.y)) * u2.y;
           }
+          const uint32_t off = swz64(lane, v);
+          *reinterpret_cast<uint4*>(st + off) = pack<T>(a8);
+          if (save_pre) {
+            *reinterpret_cast<uint4*>(st + kStageOut + off) = pack<T>(g8);
+            *reinterpret_cast<uint4*>(st + 2 * kStageOut + off) = pack<T>(u8);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          // Rows past m and columns past n are clipped by the tensor maps.
+          const int col0 = nb * kBN + c * kEpiCols;
+          tma_store_2d(map_act, st_addr, col0, row0, policy);
+          if (save_pre) {
+            tma_store_2d(map_gate, st_addr + kStageOut, col0, row0, policy);
+            tma_store_2d(map_up, st_addr + 2 * kStageOut, col0, row0, policy);
+          }
+          bulk_commit();
         }
       }
       tc_fence_before();
@@ -486,6 +553,9 @@ __device__ __forceinline__ void swiglu_gemm_body(const CUtensorMap* map_x,
       // Release this buffer to the MMA issuer (on the even CTA of a pair).
       if (lane == 0) mbar_arrive_cluster(empty_addr0 + (uint32_t)(b * sizeof(uint64_t)));
     }
+    // The staging tiles must stay valid until this warp's last TMA stores have completed.
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -498,22 +568,25 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
 swiglu_gemm_kernel(const __grid_constant__ CUtensorMap map_x,
                    const __grid_constant__ CUtensorMap map_wg,
-                   const __grid_constant__ CUtensorMap map_wu, T* __restrict__ act,
-                   int64_t act_stride, T* __restrict__ gate_out, T* __restrict__ up_out,
-                   int64_t pre_stride, int m, int n, int k) {
-  swiglu_gemm_body<T, false>(&map_x, &map_wg, &map_wu, act, act_stride, gate_out, up_out,
-                             pre_stride, m, n, k);
+                   const __grid_constant__ CUtensorMap map_wu,
+                   const __grid_constant__ CUtensorMap map_act,
+                   const __grid_constant__ CUtensorMap map_gate,
+                   const __grid_constant__ CUtensorMap map_up, int save_pre, int m, int n, int k) {
+  swiglu_gemm_body<T, false>(&map_x, &map_wg, &map_wu, &map_act, &map_gate, &map_up, save_pre,
+                             m, n, k);
 }
 
 template <typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 swiglu_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
                         const __grid_constant__ CUtensorMap map_wg,
-                        const __grid_constant__ CUtensorMap map_wu, T* __restrict__ act,
-                        int64_t act_stride, T* __restrict__ gate_out, T* __restrict__ up_out,
-                        int64_t pre_stride, int m, int n, int k) {
-  swiglu_gemm_body<T, true>(&map_x, &map_wg, &map_wu, act, act_stride, gate_out, up_out,
-                            pre_stride, m, n, k);
+                        const __grid_constant__ CUtensorMap map_wu,
+                        const __grid_constant__ CUtensorMap map_act,
+                        const __grid_constant__ CUtensorMap map_gate,
+                        const __grid_constant__ CUtensorMap map_up, int save_pre, int m, int n,
+                        int k) {
+  swiglu_gemm_body<T, true>(&map_x, &map_wg, &map_wu, &map_act, &map_gate, &map_up, save_pre, m,
+                            n, k);
 }
 
 // ------------------------------------------------------------------------ host ------
@@ -534,17 +607,19 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // Tensor map of a row-major [rows, cols] matrix (unit column stride, row stride `ld`
-// elements) read in boxes of kBK columns x box_rows rows with 128-byte swizzle.
+// elements) moved in boxes of box_cols x box_rows: operands are read as kBK columns with
+// 128-byte swizzle, outputs written as kEpiCols columns with 64-byte swizzle.
 int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int64_t ld,
-             int box_rows, CUtensorMapDataType type, const char* name) {
+             int box_rows, CUtensorMapDataType type, const char* name, int box_cols = kBK,
+             CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_fn();
   if (fn == nullptr) return set_error(PT_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   const cuuint32_t elem[2] = {1, 1};
   const CUresult r = fn(map, type, 2, const_cast<void*>(ptr), dims, strides, box, elem,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(PT_ERR_INVALID_ARGUMENT, "cannot describe %s for TMA (CUresult %d)", name,
@@ -578,11 +653,25 @@ int gemm_impl(const void* x, int64_t xs, const void* wg, const void* wu, int64_t
   if (int st = make_map(&mx, x, m, k, xs, kBM, type, "x")) return st;
   if (int st = make_map(&mg, wg, n, k, ws, kBN, type, "w_gate")) return st;
   if (int st = make_map(&mu, wu, n, k, ws, kBN, type, "w_up")) return st;
+  // Outputs: one 32-row x kEpiCols box per TMA store. Without gate/up outputs their maps
+  // repeat the activation's and are never used.
+  const int save_pre = gate_out != nullptr;
+  CUtensorMap ma, mgo, muo;
+  if (int st = make_map(&ma, act, m, n, as, 32, type, "act", kEpiCols, CU_TENSOR_MAP_SWIZZLE_64B))
+    return st;
+  if (save_pre) {
+    if (int st = make_map(&mgo, gate_out, m, n, ps, 32, type, "gate_out", kEpiCols,
+                          CU_TENSOR_MAP_SWIZZLE_64B))
+      return st;
+    if (int st = make_map(&muo, up_out, m, n, ps, 32, type, "up_out", kEpiCols,
+                          CU_TENSOR_MAP_SWIZZLE_64B))
+      return st;
+  } else {
+    mgo = ma;
+    muo = ma;
+  }
   int dev = 0, sms = 0;
   if (int st = current_device_info(&dev, &sms)) return st;
-  T* a = static_cast<T*>(act);
-  T* g = static_cast<T*>(gate_out);
-  T* u = static_cast<T*>(up_out);
   const int64_t tiles_n = (n + kBN - 1) / kBN;
   // CTA pairs whenever there are at least two row blocks to pair up.
   if (m > kBM && sms >= 2) {
@@ -593,7 +682,7 @@ int gemm_impl(const void* x, int64_t xs, const void* wg, const void* wu, int64_t
     const int64_t tiles = ((m + S::kTileM - 1) / S::kTileM) * tiles_n;
     const int pairs = (int)std::min<int64_t>(tiles, sms / 2);
     swiglu_gemm_pair_kernel<T><<<2 * pairs, kThreads, S::kSmemBytes, stream>>>(
-        mx, mg, mu, a, as, g, u, ps, (int)m, (int)n, (int)k);
+        mx, mg, mu, ma, mgo, muo, save_pre, (int)m, (int)n, (int)k);
   } else {
     using S = Shape<false>;
     const void* fn = (const void*)swiglu_gemm_kernel<T>;
@@ -601,8 +690,8 @@ int gemm_impl(const void* x, int64_t xs, const void* wg, const void* wu, int64_t
       return set_error(PT_ERR_CUDA, "cannot raise the shared memory limit of the GEMM kernel");
     const int64_t tiles = ((m + S::kTileM - 1) / S::kTileM) * tiles_n;
     const int grid = (int)std::min<int64_t>(tiles, sms);
-    swiglu_gemm_kernel<T><<<grid, kThreads, S::kSmemBytes, stream>>>(mx, mg, mu, a, as, g, u, ps,
-                                                                       (int)m, (int)n, (int)k);
+    swiglu_gemm_kernel<T><<<grid, kThreads, S::kSmemBytes, stream>>>(
+        mx, mg, mu, ma, mgo, muo, save_pre, (int)m, (int)n, (int)k);
   }
   return check_launch("pt_swiglu_gemm_fwd");
 }

@@ -73,6 +73,28 @@ def test_without_saved_preactivations_and_strided_x():
     tolerance.assert_close(act, po.swiglu_forward(g, u, "exact"), "strided act")
 
 
+def test_strided_outputs_leave_neighbours_untouched():
+    # act into columns [8, 8 + n) of a wider buffer, gate and up side by side in one [m, 2n]
+    # buffer; the padding columns and the rows past m keep their sentinel.
+    m, n, k = 200, 264, 512
+    x = gu.randn((m, k), 92, torch.bfloat16)
+    wg = gu.randn((n, k), 93, torch.bfloat16, scale=k ** -0.5)
+    wu = gu.randn((n, k), 94, torch.bfloat16, scale=k ** -0.5)
+    sentinel = 7.0
+    act_buf = torch.full((m + 3, n + 24), sentinel, dtype=torch.bfloat16, device=gu.DEV)
+    pre_buf = torch.full((m + 3, 2 * n), sentinel, dtype=torch.bfloat16, device=gu.DEV)
+    act, g, u = act_buf[:m, 8:8 + n], pre_buf[:m, :n], pre_buf[:m, n:]
+    _capi.swiglu_gemm_fwd(x.data_ptr(), k, wg.data_ptr(), wu.data_ptr(), k, act.data_ptr(),
+                          act.stride(0), g.data_ptr(), u.data_ptr(), pre_buf.stride(0), m, n, k,
+                          _capi.PT_BFLOAT16, gu.stream())
+    torch.cuda.synchronize()
+    assert _capi.take_device_error() == 0
+    ea, eg, eu = gu.swiglu_gemm(x, wg, wu)
+    assert torch.equal(act, ea) and torch.equal(g, eg) and torch.equal(u, eu)
+    assert bool((act_buf[:, :8] == sentinel).all()) and bool((act_buf[:, 8 + n:] == sentinel).all())
+    assert bool((act_buf[m:] == sentinel).all()) and bool((pre_buf[m:] == sentinel).all())
+
+
 def test_deterministic():
     m, n, k = 512, 1024, 2048
     x = gu.randn((m, k), 87, torch.bfloat16)
