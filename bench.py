@@ -2,8 +2,9 @@
 
 Default workload: a Llama-3-8B-shaped norm/activation stack, bf16,
 32 layers x (2 RMSNorm h4096 + SwiGLU i14336), forward then backward, 16384 tokens per GPU
-(4 x 4096), data-parallel over N GPUs with one packed all-reduce of the 64 RMSNorm weight
-gradients (fp32, NCCL) per step. Every layer has its own inputs (x for both norms, gate,
+(4 x 4096), data-parallel over N GPUs; the 64 RMSNorm weight gradients (fp32) are averaged
+over the ranks in four NCCL all-reduces of 16 norms each, each issued as soon as the
+backward has produced its layers and overlapping the backward of the layers below. Every layer has its own inputs (x for both norms, gate,
 up, and the upstream gradients), all larger than L2, so no L2 flush is needed.
 
 Numbers reported (rank 0 prints, other ranks stay silent):
@@ -337,6 +338,7 @@ class Stack:
         self.partials = torch.empty((self.num_partials, HIDDEN), device=device,
                                     dtype=torch.float32)
         self.launches_per_step = layers * 8
+        self.layers_per_bucket = 8  # dweights of 8 layers (16 norms, 256 KB) per all-reduce
         self.events_per_step = layers  # one (start, end) pair per SwiGLU backward launch
         self.dominant = ("swiglu_bwd_vec (SwiGLU backward)", 5 * tokens * INTER * BF16)
         self.traffic_key = "swiglu_bwd"
@@ -364,6 +366,7 @@ class Stack:
             self._check(lib.pt_swiglu_fwd(self.gate[l].data_ptr(), self.up[l].data_ptr(), act,
                                           T * INTER, b16, stream), "swiglu fwd")
         part, P = self.partials.data_ptr(), self.num_partials
+        pending = []
         for l in reversed(range(L)):
             if swiglu_bwd_events is not None:
                 start, end = swiglu_bwd_events[l]
@@ -383,7 +386,13 @@ class Stack:
                 self._check(lib.pt_rmsnorm_dw_reduce(part, P, HIDDEN,
                                                      self.bucket.slot(2 * l + k).data_ptr(), f32,
                                                      stream), "dw reduce")
-        self.bucket.all_reduce()
+            if l % self.layers_per_bucket == 0:
+                # This bucket's layers are done: average their dweights over the ranks on
+                # the process group's stream while the earlier layers' backward runs.
+                stop = 2 * min(l + self.layers_per_bucket, L)
+                pending.append(self.bucket.all_reduce_async(2 * l, stop))
+        for p in pending:
+            p.wait()
 
 
 class OpWorkload:

@@ -3,9 +3,12 @@
 Token rows shard across ranks with no communication for RMSNorm, SwiGLU or RoPE. The
 only exchange is the RMSNorm weight gradient: each rank reduces its per-CTA partials to
 one fp32 vector per norm layer directly into a slot of one packed buffer
-(``DWeightBucket``), and one all-reduce of that buffer per step averages the gradients
-over ranks, which is what the reference's DistributedDataParallel does for these
-parameters (src/picotron/parallel/ddp.py:72-91). With NCCL the all-reduce uses
+(``DWeightBucket``), and all-reduces of that buffer average the gradients over ranks,
+which is what the reference's DistributedDataParallel does for these parameters
+(src/picotron/parallel/ddp.py:72-91, gradient buckets reduced as they fill). Either the
+whole buffer at once (``all_reduce``) or a range of slots as soon as the backward has
+produced them (``all_reduce_async``: the collective runs on the process group's own
+stream while the backward of earlier layers continues). With NCCL the all-reduce uses
 ``ReduceOp.AVG``; backends without AVG (gloo) sum and divide by the world size.
 """
 
@@ -14,6 +17,24 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 from torch import Tensor
+
+
+class PendingAllReduce:
+    """An all-reduce issued by ``DWeightBucket.all_reduce_async``; ``wait`` completes it.
+
+    With NCCL, ``wait`` only makes the current CUDA stream wait for the collective (the
+    host does not block); with gloo it blocks and then applies the average."""
+
+    def __init__(self, work, view: Tensor | None, divide_by: int) -> None:
+        self._work, self._view, self._divide_by = work, view, divide_by
+
+    def wait(self) -> None:
+        if self._work is not None:
+            self._work.wait()
+            self._work = None
+        if self._view is not None and self._divide_by > 1:
+            self._view.div_(self._divide_by)
+        self._view = None
 
 
 class DWeightBucket:
@@ -53,3 +74,24 @@ class DWeightBucket:
         dist.all_reduce(self.buffer, op=dist.ReduceOp.SUM, group=group)
         if average:
             self.buffer.div_(world)
+
+    def all_reduce_async(self, first: int, stop: int, group: dist.ProcessGroup | None = None,
+                         average: bool = True) -> PendingAllReduce:
+        """Start the sum (or average) of slots ``[first, stop)`` over the ranks of ``group``.
+
+        Every rank must issue the same ranges in the same order. Returns a handle whose
+        ``wait`` must be called before the slots are read."""
+
+        if not 0 <= first < stop <= len(self.sizes):
+            raise ValueError(f"slot range [{first}, {stop}) is outside [0, {len(self.sizes)})")
+        if not dist.is_available() or not dist.is_initialized():
+            return PendingAllReduce(None, None, 1)
+        world = dist.get_world_size(group)
+        if world == 1:
+            return PendingAllReduce(None, None, 1)
+        view = self.buffer[self.offsets[first] : self.offsets[stop]]
+        if average and dist.get_backend(group) == "nccl":
+            work = dist.all_reduce(view, op=dist.ReduceOp.AVG, group=group, async_op=True)
+            return PendingAllReduce(work, None, 1)
+        work = dist.all_reduce(view, op=dist.ReduceOp.SUM, group=group, async_op=True)
+        return PendingAllReduce(work, view, world if average else 1)
