@@ -79,14 +79,28 @@ namespace {
 #ifndef PT_RMS_REDUCERS
 #define PT_RMS_REDUCERS 4  // reducer warps per CTA
 #endif
+// 16-bit backward without the fused add: 3 reducer warps and a 96 KB ring (6 slots of x and
+// dy rows at hidden 4096). A/B on B200 at 16384 x 4096 bf16: 0.81 -> 0.85 of the HBM peak
+// against 4 reducers and 4 slots; the same change made the fp32 backward and the forward
+// slower, so they keep the defaults.
+#ifndef PT_RMS_REDUCERS_BWD16
+#define PT_RMS_REDUCERS_BWD16 3
+#endif
+#ifndef PT_RMS_SMEM_BWD16
+#define PT_RMS_SMEM_BWD16 (96 * 1024)
+#endif
 constexpr int kElemsFwd = PT_RMS_ELEMS_FWD;
 constexpr int kElemsBwd = PT_RMS_ELEMS_BWD;
 constexpr int kSmemFwd = PT_RMS_SMEM_FWD;
 constexpr int kSmemBwd = PT_RMS_SMEM_BWD;
 constexpr int kMinStages = PT_RMS_MIN_STAGES;
 constexpr int kReducers = PT_RMS_REDUCERS;
+constexpr int kReducersBwd16 = PT_RMS_REDUCERS_BWD16;
+constexpr int kSmemBwd16 = PT_RMS_SMEM_BWD16;
 constexpr int kMaxStages = 16;
 static_assert(kReducers >= 1 && kReducers <= kMaxStages, "reducer count must fit the ring");
+static_assert(kReducersBwd16 >= 1 && kReducersBwd16 <= kReducers,
+              "the kernels' warp bound assumes at most kReducers reducers");
 constexpr int kMaxConsumers = 16;  // owner warps per CTA
 // CTAs of up to this many owner warps (rows of up to 4096 elements) get a tighter
 // launch bound (two CTAs per SM); the backward owners hold half as many elements.
@@ -715,12 +729,15 @@ FastPlan plan_fast(int64_t hidden) {
   // stages must be a multiple of the reducer count: then each slot is served by exactly
   // one reducer, which visits it in row order, so no waiter can reach a slot's barrier two
   // phases early (try_wait.parity cannot tell use k from use k - 2).
-  const int64_t budget = (int64_t)(kBwd ? kSmemBwd : kSmemFwd) * (kAdd ? 3 : 2) / 2;
+  constexpr bool kBwd16 = kBwd && !kAdd && sizeof(T) == 2;
+  const int reducers = kBwd16 ? kReducersBwd16 : kReducers;
+  const int64_t budget =
+      kBwd16 ? (int64_t)kSmemBwd16 : (int64_t)(kBwd ? kSmemBwd : kSmemFwd) * (kAdd ? 3 : 2) / 2;
   int stages = (int)std::min<int64_t>(kMaxStages, budget / slot_bytes);
   stages = std::max(stages, kMinStages);
-  stages = std::max(kReducers, stages / kReducers * kReducers);
+  stages = std::max(reducers, stages / reducers * reducers);
   plan.stages = stages;
-  plan.reducers = kReducers;
+  plan.reducers = reducers;
   plan.smem = (int)(stages * slot_bytes + (kBwd ? nvec * V * 4 : 0));
   plan.ok = true;
   return plan;
