@@ -89,6 +89,15 @@ namespace {
 #ifndef PT_RMS_SMEM_BWD16
 #define PT_RMS_SMEM_BWD16 (96 * 1024)
 #endif
+#ifndef PT_RMS_REDUCERS_FWD
+#define PT_RMS_REDUCERS_FWD PT_RMS_REDUCERS
+#endif
+#ifndef PT_RMS_REDUCERS_ADDBWD16
+#define PT_RMS_REDUCERS_ADDBWD16 PT_RMS_REDUCERS
+#endif
+#ifndef PT_RMS_SMEM_ADDBWD16
+#define PT_RMS_SMEM_ADDBWD16 (PT_RMS_SMEM_BWD * 3 / 2)
+#endif
 constexpr int kElemsFwd = PT_RMS_ELEMS_FWD;
 constexpr int kElemsBwd = PT_RMS_ELEMS_BWD;
 constexpr int kSmemFwd = PT_RMS_SMEM_FWD;
@@ -729,10 +738,18 @@ FastPlan plan_fast(int64_t hidden) {
   // stages must be a multiple of the reducer count: then each slot is served by exactly
   // one reducer, which visits it in row order, so no waiter can reach a slot's barrier two
   // phases early (try_wait.parity cannot tell use k from use k - 2).
-  constexpr bool kBwd16 = kBwd && !kAdd && sizeof(T) == 2;
-  const int reducers = kBwd16 ? kReducersBwd16 : kReducers;
-  const int64_t budget =
-      kBwd16 ? (int64_t)kSmemBwd16 : (int64_t)(kBwd ? kSmemBwd : kSmemFwd) * (kAdd ? 3 : 2) / 2;
+  constexpr bool k16 = sizeof(T) == 2;
+  int reducers = kReducers;
+  int64_t budget = (int64_t)(kBwd ? kSmemBwd : kSmemFwd) * (kAdd ? 3 : 2) / 2;
+  if (kBwd && k16 && !kAdd) {
+    reducers = kReducersBwd16;
+    budget = kSmemBwd16;
+  } else if (kBwd && k16 && kAdd) {
+    reducers = PT_RMS_REDUCERS_ADDBWD16;
+    budget = PT_RMS_SMEM_ADDBWD16;
+  } else if (!kBwd) {
+    reducers = PT_RMS_REDUCERS_FWD;
+  }
   int stages = (int)std::min<int64_t>(kMaxStages, budget / slot_bytes);
   stages = std::max(stages, kMinStages);
   stages = std::max(reducers, stages / reducers * reducers);
