@@ -28,8 +28,8 @@
 // (dy * x) * r is accumulated in fp64 with one fma (dy * x of two 16-bit floats is exact
 // in fp32, of two fp32 values exact in fp64). Each CTA's partial is therefore the exact
 // sum to about 2^-50 relative, however many rows it reduces; it is stored as an fp32 pair
-// (rounded sum, rounded remainder) and pt_rmsnorm_dw_reduce adds the partials with
-// compensated fp32 sums combined in fp64. One fp64 fma and one conversion per element
+// (rounded sum, rounded remainder) and pt_rmsnorm_dw_reduce adds the partials in fp64 in a
+// fixed order. One fp64 fma and one conversion per element
 // leave the fp64 pipe far from saturated at HBM speed.
 //
 // Generic path: any hidden size, stride or alignment; one row per CTA iteration with
@@ -593,48 +593,44 @@ rmsnorm_bwd_generic(const T* __restrict__ dy, int64_t dys, const T* __restrict__
 constexpr int kReduceWarps = 32;
 constexpr int kReduceCols = 16;                    // columns per CTA (half a warp)
 constexpr int kReduceGroups = kReduceWarps * 2;    // row groups per CTA (half-warps)
-constexpr int kReduceUnroll = 4;
+constexpr int kReduceBatch = 8;                    // partial rows loaded per group at once
 
 template <typename TW>
 __global__ void __launch_bounds__(kReduceWarps * 32)
 rmsnorm_dw_reduce_kernel(const float* __restrict__ partials, int num_partials, int64_t hidden,
                          TW* __restrict__ dw) {
-  // 16 columns per CTA: each half-warp covers them (64-byte loads), and the 64 half-warps of
-  // the CTA split the partial rows: group g sums the rows p = g*U + u + i*G*U (u < U) into U
-  // independent doubly compensated (Sum2) fp32 accumulators, in increasing i; the U (sum,
-  // error) pairs are combined in fp64 and the G group sums are added in fp64 in group order,
-  // then rounded once. The order depends only on num_partials, so the result is
-  // deterministic, and Sum2 keeps it correctly rounded in practice even when the partials
-  // cancel. Twice as many CTAs as a warp-per-32-columns layout keeps every SM busy.
-  __shared__ double s[kReduceGroups][kReduceCols + 1];
+  // 16 columns per CTA: each half-warp covers them (64-byte loads) and the 64 half-warps of
+  // the CTA split the partial rows: group g adds rows g, g + 64, g + 128, ... in that order
+  // in fp64, loading kReduceBatch of them at a time. Warp w < 16 then adds the 64 group sums
+  // of column w with a fixed shuffle tree, and the result is rounded once. The order depends
+  // only on num_partials, so the result is deterministic; the fp64 sums of the fp32 partial
+  // pairs (rounded sum, rounded remainder) are exact to far below the output's precision.
+  __shared__ double s[kReduceCols][kReduceGroups + 1];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int col = lane & (kReduceCols - 1);
   const int group = warp * 2 + (lane >> 4);
   const int64_t c = (int64_t)blockIdx.x * kReduceCols + col;
-  float acc[kReduceUnroll], comp[kReduceUnroll];
-#pragma unroll
-  for (int u = 0; u < kReduceUnroll; ++u) acc[u] = comp[u] = 0.0f;
+  double t = 0.0;
   if (c < hidden) {
-    for (int p0 = group * kReduceUnroll; p0 < num_partials;
-         p0 += kReduceGroups * kReduceUnroll) {
-      float v[kReduceUnroll];
+    for (int p0 = group; p0 < num_partials; p0 += kReduceGroups * kReduceBatch) {
+      float v[kReduceBatch];
 #pragma unroll
-      for (int u = 0; u < kReduceUnroll; ++u)
-        v[u] = p0 + u < num_partials ? partials[(int64_t)(p0 + u) * hidden + c] : 0.0f;
+      for (int u = 0; u < kReduceBatch; ++u) {
+        const int p = p0 + u * kReduceGroups;
+        v[u] = p < num_partials ? partials[(int64_t)p * hidden + c] : 0.0f;
+      }
 #pragma unroll
-      for (int u = 0; u < kReduceUnroll; ++u) sum2_add(acc[u], comp[u], v[u]);
+      for (int u = 0; u < kReduceBatch; ++u) t += (double)v[u];
     }
   }
-  double t = 0.0;
-#pragma unroll
-  for (int u = 0; u < kReduceUnroll; ++u) t += (double)acc[u] + (double)comp[u];
-  s[group][col] = t;
+  s[col][group] = t;
   __syncthreads();
-  if (threadIdx.x < kReduceCols && c < hidden) {
-    double sum = 0.0;
-#pragma unroll 8
-    for (int i = 0; i < kReduceGroups; ++i) sum += s[i][col];
-    dw[c] = from_float<TW>((float)sum);
+  if (warp < kReduceCols) {
+    const int64_t cw = (int64_t)blockIdx.x * kReduceCols + warp;
+    double v = s[warp][lane] + s[warp][lane + 32];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_down_sync(0xffffffffu, v, off);
+    if (lane == 0 && cw < hidden) dw[cw] = from_float<TW>((float)v);
   }
 }
 
