@@ -210,6 +210,13 @@ PT_API int pt_add_rmsnorm_bwd(const void* dy, int64_t dy_row_stride,
  * No reference counterpart: the reference has no device-side waits. */
 PT_API int pt_take_device_error(int* code);
 
+/* Self-test of the failure path above without a GPU fault: launches one CTA whose thread 0
+ * waits on a shared-memory barrier that nothing arrives at, gives up after limit_cycles SM
+ * cycles (1 .. 2e9; about 1 ms per 2e6 at 1.9 GHz), records code 1 in the device error word
+ * exactly as the pipelines' bounded waits do, and returns, leaving the context usable.
+ * No reference counterpart. */
+PT_API int pt_selftest_wait_timeout(int64_t limit_cycles, void* stream);
+
 /* ----------------------------------------------------------------- SwiGLU -------- */
 
 /* out = gate * sigmoid(gate) * up over n contiguous elements, fp32 math, one rounding.

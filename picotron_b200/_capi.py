@@ -97,6 +97,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                         _c_i64, _c_ptr, _c_i64, _c_i64, _c_int, _c_int,
                                         _c_float, _c_ptr]),
     "pt_take_device_error": (_c_int, [ctypes.POINTER(_c_int)]),
+    "pt_selftest_wait_timeout": (_c_int, [_c_i64, _c_ptr]),
     "pt_swiglu_fwd": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_i64, _c_int, _c_ptr]),
     "pt_swiglu_bwd": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_int, _c_ptr]),
     "pt_rope_fwd": (_c_int, [_c_ptr, _c_i64_4, _c_ptr, _c_i64_4, _c_i64_4, _c_ptr, _c_ptr,
@@ -346,6 +347,13 @@ def rope_qk(direction: str, q: int, q_strides, q_out: int, q_out_strides, q_size
                 _i64x4(k_strides), k_out, _i64x4(k_out_strides), _i64x4(k_sizes), cosine, sine,
                 table_row_stride, layout, dtype, table_dtype, stream)
     _check("pt_rope_qk_" + direction, status, error_type)
+
+
+def selftest_wait_timeout(limit_cycles: int, stream: int) -> None:
+    """Launch the bounded-wait self-test (see pt_selftest_wait_timeout)."""
+
+    _check("pt_selftest_wait_timeout",
+           library().pt_selftest_wait_timeout(limit_cycles, stream), None)
 
 
 def take_device_error() -> int:

@@ -491,6 +491,18 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
   }
 }
 
+// Self-test of the bounded-wait failure path, with no GPU fault: thread 0 waits on an
+// mbarrier that nothing arrives at, gives up after `limit` SM cycles, records the timeout
+// in the device error word as the pipelines do, and the kernel returns normally.
+__global__ void wait_timeout_selftest_kernel(long long limit) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    if (!mbar_wait_bounded(&bar, 0, limit)) record_timeout();
+  }
+}
+
 // --------------------------------------------------------------- generic paths -----
 template <typename T, typename TW>
 __global__ void __launch_bounds__(kGenericThreads)
@@ -1191,6 +1203,16 @@ int pt_rmsnorm_bwd_noalloc(const void* dy, int64_t dy_row_stride, const void* x,
                               w_dtype, eps, stream))
     return st;
   return pt_rmsnorm_dw_reduce(scratch, num_partials, hidden, dw, w_dtype, stream);
+}
+
+int pt_selftest_wait_timeout(int64_t limit_cycles, void* stream) {
+  if (limit_cycles < 1 || limit_cycles > kWaitLimitCycles)
+    return set_error(PT_ERR_INVALID_ARGUMENT, "limit_cycles must be in [1, %lld] (got %lld)",
+                     kWaitLimitCycles, (long long)limit_cycles);
+  int dev = 0, sms = 0;
+  if (int st = current_device_info(&dev, &sms)) return st;
+  wait_timeout_selftest_kernel<<<1, 32, 0, as_stream(stream)>>>((long long)limit_cycles);
+  return check_launch("pt_selftest_wait_timeout");
 }
 
 int pt_take_device_error(int* code) {

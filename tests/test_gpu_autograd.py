@@ -231,3 +231,22 @@ def test_op_errors_are_typed():
         torch.ops.picotron_b200.rms_norm(x, torch.ones(32, device=gu.DEV), 1e-6)
     with pytest.raises(TritonRMSNormUnavailable, match="dtype"):
         torch.ops.picotron_b200.rms_norm(x.double(), torch.ones(64, device=gu.DEV), 1e-6)
+
+
+def test_bounded_wait_timeout_is_reported_and_the_context_survives():
+    # Failure detection without a GPU fault: a wait on a barrier that nothing arrives at gives
+    # up after ~5 ms of SM clock, the device error word reads 1 (then 0 once taken), and the
+    # next kernels run normally.
+    assert _capi.take_device_error() == 0
+    _capi.selftest_wait_timeout(10_000_000, gu.stream())
+    torch.cuda.synchronize()
+    assert _capi.take_device_error() == 1
+    assert _capi.take_device_error() == 0
+    x = gu.randn((64, 512), 95, torch.bfloat16)
+    w = gu.randn((512,), 96, torch.float32, scale=0.02, shift=1.0)
+    y = gu.rmsnorm_fwd(x, w, 1e-5)
+    ye, _ = po.rms_norm_forward(x.cpu(), w.cpu(), 1e-5, "exact")
+    tolerance.assert_close(y, ye, "rmsnorm after a reported timeout")
+    assert _capi.take_device_error() == 0
+    with pytest.raises(_capi.PtError):
+        _capi.selftest_wait_timeout(0, gu.stream())
