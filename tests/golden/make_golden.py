@@ -2,7 +2,7 @@
 
 Run in the build container, where the reference is mounted read-only:
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py [--reference-src DIR]
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py --reference-src DIR
 
 It imports the reference's own hot-path functions
 (``picotron.nn.triton_kernels.rmsnorm.rms_norm_with_pytorch_forward``,
@@ -131,9 +131,11 @@ def _rope(rope_mod, q_phys, theta, dy_phys):
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference-src", default=os.environ.get("PICOTRON_REFERENCE_SRC",
-                                                                  "/root/reference/src"))
+    parser.add_argument("--reference-src", default=os.environ.get("PICOTRON_REFERENCE_SRC"),
+                        help="the reference's src directory (or set PICOTRON_REFERENCE_SRC)")
     args = parser.parse_args()
+    if not args.reference_src:
+        parser.error("give --reference-src or set PICOTRON_REFERENCE_SRC")
     sys.path.insert(0, args.reference_src)
     torch.set_num_threads(1)
     from picotron.nn import feedforward as ffn_mod
