@@ -62,7 +62,10 @@ namespace {
 #define PT_RMS_ELEMS_BWD 16  // backward owners also hold an fp64 dweight sum each
 #endif
 #ifndef PT_RMS_SMEM_FWD
-#define PT_RMS_SMEM_FWD (48 * 1024)  // forward ring budget per CTA
+#define PT_RMS_SMEM_FWD (48 * 1024)  // forward ring budget per CTA (fp32 rows)
+#endif
+#ifndef PT_RMS_SMEM_FWD16
+#define PT_RMS_SMEM_FWD16 (24 * 1024)  // forward ring budget per CTA (16-bit rows)
 #endif
 #ifndef PT_RMS_SMEM_BWD
 #define PT_RMS_SMEM_BWD (64 * 1024)  // backward ring budget per CTA (plus the staged weight)
@@ -89,8 +92,13 @@ namespace {
 #ifndef PT_RMS_SMEM_BWD16
 #define PT_RMS_SMEM_BWD16 (96 * 1024)
 #endif
+// 16-bit forward: 3 reducer warps and 3 ring slots (24 KB at hidden 4096 bf16). A/B on B200
+// at 16384 x 4096 bf16: 0.90 of the HBM peak against 0.88 with 4 reducers and 4 slots, and
+// the fused add forward 0.94 against 0.85; deeper rings (6-12 slots), 2 reducers, or one CTA
+// per SM were slower: the forward runs best with few rows in flight per SM. fp32 rows keep
+// 4 reducers and the 48 KB budget (0.90 against 0.89).
 #ifndef PT_RMS_REDUCERS_FWD
-#define PT_RMS_REDUCERS_FWD PT_RMS_REDUCERS
+#define PT_RMS_REDUCERS_FWD 3
 #endif
 #ifndef PT_RMS_REDUCERS_ADDBWD16
 #define PT_RMS_REDUCERS_ADDBWD16 PT_RMS_REDUCERS
@@ -105,10 +113,14 @@ constexpr int kSmemBwd = PT_RMS_SMEM_BWD;
 constexpr int kMinStages = PT_RMS_MIN_STAGES;
 constexpr int kReducers = PT_RMS_REDUCERS;
 constexpr int kReducersBwd16 = PT_RMS_REDUCERS_BWD16;
+constexpr int kReducersFwd = PT_RMS_REDUCERS_FWD;
+constexpr int kReducersAddBwd16 = PT_RMS_REDUCERS_ADDBWD16;
 constexpr int kSmemBwd16 = PT_RMS_SMEM_BWD16;
 constexpr int kMaxStages = 16;
 static_assert(kReducers >= 1 && kReducers <= kMaxStages, "reducer count must fit the ring");
-static_assert(kReducersBwd16 >= 1 && kReducersBwd16 <= kReducers,
+static_assert(kReducersBwd16 >= 1 && kReducersBwd16 <= kReducers && kReducersFwd >= 1 &&
+                  kReducersFwd <= kReducers && kReducersAddBwd16 >= 1 &&
+                  kReducersAddBwd16 <= kReducers,
               "the kernels' warp bound assumes at most kReducers reducers");
 constexpr int kMaxConsumers = 16;  // owner warps per CTA
 // CTAs of up to this many owner warps (rows of up to 4096 elements) get a tighter
@@ -753,10 +765,11 @@ FastPlan plan_fast(int64_t hidden) {
     reducers = kReducersBwd16;
     budget = kSmemBwd16;
   } else if (kBwd && k16 && kAdd) {
-    reducers = PT_RMS_REDUCERS_ADDBWD16;
+    reducers = kReducersAddBwd16;
     budget = PT_RMS_SMEM_ADDBWD16;
-  } else if (!kBwd) {
-    reducers = PT_RMS_REDUCERS_FWD;
+  } else if (!kBwd && k16) {
+    reducers = kReducersFwd;
+    budget = (int64_t)PT_RMS_SMEM_FWD16 * (kAdd ? 3 : 2) / 2;
   }
   int stages = (int)std::min<int64_t>(kMaxStages, budget / slot_bytes);
   stages = std::max(stages, kMinStages);
