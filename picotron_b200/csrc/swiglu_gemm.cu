@@ -83,6 +83,8 @@ template <bool kPair> struct Shape {
       1024 /* alignment slack */ + kStages * kStageBytes + kStagingBytes + 256;
 };
 static_assert(Shape<false>::kStages <= kMaxStages && Shape<true>::kStages <= kMaxStages, "");
+static_assert(Shape<false>::kSmemBytes <= 227 * 1024 && Shape<true>::kSmemBytes <= 227 * 1024,
+              "stage ring + epilogue staging must fit the 227 KB of shared memory per CTA");
 
 struct GemmBarriers {
   uint64_t full[kMaxStages];
