@@ -11,8 +11,9 @@ Numbers reported (rank 0 prints, other ranks stay silent):
 * ``value``: tokens/s of the whole job = N x 16384 / (max over ranks of the CUDA-event
   time of one step), inputs resident in HBM, kernels called through the C ABI.
 * ``e2e``: the same metric through the public API (``picotron_b200.kernels``, torch ops
-  with autograd), with each step's inputs copied from pinned host memory and the reduced
-  weight gradients read back to the host inside the timed region.
+  with autograd), with each step's inputs copied from pinned host memory (on a copy stream,
+  each layer's compute starting once its own inputs have landed) and the reduced weight
+  gradients read back to the host inside the timed region.
 * ``roofline``: the dominant kernel (SwiGLU backward) -- algorithmic bytes per launch /
   its mean CUDA-event duration inside the timed region, against MEASURED_PEAKS.json.
 * ``cpu_baseline``: the reference's PyTorch CPU path (the oracle's "eager" form) on a
@@ -639,15 +640,30 @@ def e2e_run(stack: Stack, steps: int, warmup: int, world: int) -> dict:
     h2d = sum(t.numel() * t.element_size() for t in pin.values()) * stack.layers
     d2h = result_host.numel() * 4
 
+    copy_stream = torch.cuda.Stream(device=dev)
+
     def one_step():
         for w in weights:
             w.grad = None
+        # Host-to-device copies run on their own stream, each layer's compute waiting only
+        # for its own inputs, so the compute of layer l overlaps the copies of the layers
+        # after it (an input pipeline's prefetch). The copy stream first waits for everything
+        # the compute stream has queued, so no buffer is overwritten while still in use.
+        main = torch.cuda.current_stream(dev)
+        copy_stream.wait_stream(main)
+        ready = []
+        with torch.cuda.stream(copy_stream):
+            for l in range(stack.layers):
+                stack.x[l].copy_(pin["x"], non_blocking=True)
+                stack.dy[l].copy_(pin["dy"], non_blocking=True)
+                stack.gate[l].copy_(pin["gate"], non_blocking=True)
+                stack.up[l].copy_(pin["up"], non_blocking=True)
+                stack.dout[l].copy_(pin["dout"], non_blocking=True)
+                event = torch.cuda.Event()
+                event.record(copy_stream)
+                ready.append(event)
         for l in range(stack.layers):
-            stack.x[l].copy_(pin["x"], non_blocking=True)
-            stack.dy[l].copy_(pin["dy"], non_blocking=True)
-            stack.gate[l].copy_(pin["gate"], non_blocking=True)
-            stack.up[l].copy_(pin["up"], non_blocking=True)
-            stack.dout[l].copy_(pin["dout"], non_blocking=True)
+            main.wait_event(ready[l])
             xa = stack.x[l, 0].detach().requires_grad_(True)
             xm = stack.x[l, 1].detach().requires_grad_(True)
             g = stack.gate[l].detach().requires_grad_(True)
