@@ -8,10 +8,16 @@
 //
 // Layout: a logical [B, H, S, D] tensor with arbitrary strides in elements (stride of D
 // = 1), e.g. the reference's transposed view of [B, S, H, D] projections
-// (src/picotron/nn/attention.py:196-203), read in place with no .contiguous() copy. The
-// host orders the three outer dimensions by decreasing input stride so consecutive
-// threads walk memory in address order. Each thread rotates 16-byte vectors (U per
-// iteration, loads first); the angle tables are tiny and stay in L1/L2.
+// (src/picotron/nn/attention.py:196-203), read in place with no .contiguous() copy.
+// Three paths, chosen per call on the host:
+//  * rows (rope_rows, interleaved pairs): every (b, s) row of heads x head_dim is
+//    contiguous, as in that view; q and k rows of one position are rotated together with
+//    one load of the table entries per thread and row;
+//  * vector (rope_vec): any strides with 16-byte aligned rows; the host orders the outer
+//    dimensions by decreasing input stride so consecutive threads walk memory in address
+//    order, and each thread rotates U 16-byte vectors per iteration (loads first);
+//  * scalar (rope_scalar): any even head_dim, any alignment.
+// All three use the same explicitly rounded fp32 rotation, so they agree bit for bit.
 #include <algorithm>
 
 #include "common.cuh"
@@ -38,6 +44,14 @@ struct RopeGeom {
   int64_t table_stride;          // elements between table rows
   float sign;                    // +1 forward, -1 backward
 };
+
+// One rotation in fp32 with explicit roundings (no contraction into fused multiply-adds), so
+// that the rows, vector and scalar paths give bit-identical results:
+//   r1 = e * c - o * s,  r2 = e * s + o * c.
+__device__ __forceinline__ void rotate(float e, float o, float c, float s, float& r1, float& r2) {
+  r1 = __fsub_rn(__fmul_rn(e, c), __fmul_rn(o, s));
+  r2 = __fadd_rn(__fmul_rn(e, s), __fmul_rn(o, c));
+}
 
 // Loads N consecutive table entries of TT starting at p as fp32. The host guarantees
 // that p is aligned to min(16, N * sizeof(TT)) bytes on the vector path.
@@ -125,11 +139,8 @@ __device__ __forceinline__ void rope_vec_body(const T* __restrict__ x, T* __rest
         load_table<TT, V / 2>(sine + t, s);
         unpack<T>(a[k], f);
 #pragma unroll
-        for (int p = 0; p < V / 2; ++p) {
-          const float e = f[2 * p], o = f[2 * p + 1], sn = g.sign * s[p];
-          f[2 * p] = e * c[p] - o * sn;
-          f[2 * p + 1] = e * sn + o * c[p];
-        }
+        for (int p = 0; p < V / 2; ++p)
+          rotate(f[2 * p], f[2 * p + 1], c[p], g.sign * s[p], f[2 * p], f[2 * p + 1]);
         st_stream(out + oo[k] + d0, pack<T>(f));
       } else {
         // First-half vector at d0 pairs with the second-half vector at d0 + D/2.
@@ -140,11 +151,7 @@ __device__ __forceinline__ void rope_vec_body(const T* __restrict__ x, T* __rest
         unpack<T>(a[k], f1);
         unpack<T>(b[k], f2);
 #pragma unroll
-        for (int p = 0; p < V; ++p) {
-          const float e = f1[p], o = f2[p], sn = g.sign * s[p];
-          f1[p] = e * c[p] - o * sn;
-          f2[p] = o * c[p] + e * sn;
-        }
+        for (int p = 0; p < V; ++p) rotate(f1[p], f2[p], c[p], g.sign * s[p], f1[p], f2[p]);
         st_stream(out + oo[k] + d0, pack<T>(f1));
         st_stream(out + oo[k] + d0 + half_dim, pack<T>(f2));
       }
@@ -164,6 +171,81 @@ rope_vec(const __grid_constant__ RopeJobs<T> jobs, const TT* __restrict__ cosine
     rope_vec_body<T, TT, kRotateHalf>(jobs.x[1], jobs.out[1], cosine, sine, jobs.g[1],
                                       half_dim, jobs.total[1], blockIdx.x - jobs.blocks0,
                                       gridDim.x - jobs.blocks0);
+}
+
+// Rows path (interleaved pairs), for the layout the attention projections produce: each
+// (b, s) row of a tensor is contiguous (head stride = head_dim, head_dim stride 1), as in the
+// [B,H,S,D] view of [B,S,H,D] memory. A CTA takes whole rows of q and k together (the same
+// position, so one row of the angle tables); a unit is one 16-byte vector. Units per head
+// divide the block size, so every unit a thread touches sits at the same place in its head
+// and needs the same table entries: the thread loads them once per row, and no index
+// division is left but b = r / S. (For rotate-half pairs this layout ran slower than the
+// vector path in A/B runs, so those keep it.)
+// 4 units per thread in flight: A/B on B200 at config 4 (q + k, bf16) gave 0.917 of the HBM
+// peak, against 0.851 / 0.895 / 0.913 with 2 / 5 / 8 and 0.879 on the vector path.
+#ifndef PT_ROPE_ROW_UNITS
+#define PT_ROPE_ROW_UNITS 4
+#endif
+constexpr int kRowThreads = 128;
+constexpr int kRowUnits = PT_ROPE_ROW_UNITS;  // units of a row per thread in flight
+
+template <typename T> struct RopeRows {
+  const T* x[2];
+  T* out[2];
+  int64_t xb[2], xs[2], ob[2], os[2];  // batch and sequence strides (elements)
+  uint32_t units0, units;              // units per row: of tensor 0, of both tensors
+  uint32_t rows, S;                    // rows = B * S
+  FastDiv div_s;
+  int64_t table_stride;
+  int uh_log2;  // log2 of the units per head
+  float sign;   // +1 forward, -1 backward
+};
+
+template <typename T, typename TT>
+__global__ void __launch_bounds__(kRowThreads)
+rope_rows(const __grid_constant__ RopeRows<T> p, const TT* __restrict__ cosine,
+          const TT* __restrict__ sine) {
+  constexpr int V = Vec16<T>::N;
+  constexpr int NT = V / 2;  // table entries (pairs) per unit
+  const uint32_t t = threadIdx.x;
+  const int dj = (int)(t & ((1u << p.uh_log2) - 1)) * V;  // the unit's offset in its head
+  for (uint32_t r = blockIdx.x; r < p.rows; r += gridDim.x) {
+    const uint32_t b = p.div_s.div(r);
+    const uint32_t s = r - b * p.S;
+    float c[NT], sn[NT];
+    const int64_t tb = (int64_t)s * p.table_stride + dj / 2;
+    load_table<TT, NT>(cosine + tb, c);
+    load_table<TT, NT>(sine + tb, sn);
+#pragma unroll
+    for (int e = 0; e < NT; ++e) sn[e] = p.sign * sn[e];
+    const T* xr0 = p.x[0] + (int64_t)b * p.xb[0] + (int64_t)s * p.xs[0];
+    const T* xr1 = p.x[1] + (int64_t)b * p.xb[1] + (int64_t)s * p.xs[1];
+    T* or0 = p.out[0] + (int64_t)b * p.ob[0] + (int64_t)s * p.os[0];
+    T* or1 = p.out[1] + (int64_t)b * p.ob[1] + (int64_t)s * p.os[1];
+    for (uint32_t u0 = t; u0 < p.units; u0 += kRowThreads * kRowUnits) {
+      uint4 a[kRowUnits];
+      int64_t off[kRowUnits];
+#pragma unroll
+      for (int k = 0; k < kRowUnits; ++k) {
+        const uint32_t u = u0 + k * kRowThreads;
+        if (u >= p.units) continue;
+        const bool second = u >= p.units0;
+        off[k] = (int64_t)(second ? u - p.units0 : u) * V;
+        a[k] = ld_stream((second ? xr1 : xr0) + off[k]);
+      }
+#pragma unroll
+      for (int k = 0; k < kRowUnits; ++k) {
+        const uint32_t u = u0 + k * kRowThreads;
+        if (u >= p.units) continue;
+        float f[V];
+        unpack<T>(a[k], f);
+#pragma unroll
+        for (int q = 0; q < V / 2; ++q)
+          rotate(f[2 * q], f[2 * q + 1], c[q], sn[q], f[2 * q], f[2 * q + 1]);
+        st_stream((u >= p.units0 ? or1 : or0) + off[k], pack<T>(f));
+      }
+    }
+  }
 }
 
 // Scalar path: one pair per thread iteration, any even D, any strides and alignment.
@@ -186,9 +268,10 @@ rope_scalar(const T* __restrict__ x, T* __restrict__ out, const TT* __restrict__
     const int64_t dod = kRotateHalf ? pi + half_dim : 2 * pi + 1;
     const float c = to_float(cosine[s_idx * g.table_stride + pi]);
     const float sn = g.sign * to_float(sine[s_idx * g.table_stride + pi]);
-    const float e = to_float(x[xo + de]), o = to_float(x[xo + dod]);
-    out[oo + de] = from_float<T>(e * c - o * sn);
-    out[oo + dod] = from_float<T>(e * sn + o * c);
+    float r1, r2;
+    rotate(to_float(x[xo + de]), to_float(x[xo + dod]), c, sn, r1, r2);
+    out[oo + de] = from_float<T>(r1);
+    out[oo + dod] = from_float<T>(r2);
   }
 }
 
@@ -238,6 +321,57 @@ bool make_geom(RopeGeom& g, const void* x, const int64_t* xst, const void* out,
   return vec;
 }
 
+// Whether the rows path can take these tensors (see rope_rows), and its parameters.
+template <typename T, typename TT>
+bool make_rows(RopeRows<T>& p, int n, const void* const* xs, const int64_t* const* xsts,
+               void* const* outs, const int64_t* const* osts, const int64_t* const* sizes,
+               const void* cosine, const void* sine, int64_t tstride, bool rh, float sign) {
+  constexpr int V = Vec16<T>::N;
+  if (rh) return false;
+  const int64_t B = sizes[0][0], S = sizes[0][2], D = sizes[0][3];
+  const int64_t uh = D / V;  // units per head
+  if (D % V != 0 || uh < 1 || uh > kRowThreads || (uh & (uh - 1)) != 0) return false;
+  const int tbytes = (V / 2) * (int)sizeof(TT);
+  const int talign = tbytes >= 16 ? 16 : tbytes;
+  if (reinterpret_cast<uintptr_t>(cosine) % talign || reinterpret_cast<uintptr_t>(sine) % talign ||
+      (tstride * (int64_t)sizeof(TT)) % talign)
+    return false;
+  if (B * S >= (int64_t)UINT32_MAX) return false;
+  int64_t units[2] = {0, 0};
+  for (int i = 0; i < n; ++i) {
+    const int64_t* sz = sizes[i];
+    const int64_t* xst = xsts[i];
+    const int64_t* ost = osts[i];
+    if (sz[0] != B || sz[2] != S || sz[3] != D) return false;
+    if (xst[1] != D || ost[1] != D) return false;  // contiguous (b, s) rows of heads
+    if (!aligned16(xs[i]) || !aligned16(outs[i])) return false;
+    for (int a : {0, 2})
+      if ((xst[a] * (int64_t)sizeof(T)) % 16 || (ost[a] * (int64_t)sizeof(T)) % 16) return false;
+    units[i] = sz[1] * uh;
+  }
+  if (units[0] + units[1] >= (int64_t)UINT32_MAX / 2) return false;
+  for (int i = 0; i < 2; ++i) {
+    const int k = i < n ? i : 0;
+    p.x[i] = static_cast<const T*>(xs[k]);
+    p.out[i] = static_cast<T*>(outs[k]);
+    p.xb[i] = xsts[k][0];
+    p.xs[i] = xsts[k][2];
+    p.ob[i] = osts[k][0];
+    p.os[i] = osts[k][2];
+  }
+  p.units0 = (uint32_t)units[0];
+  p.units = (uint32_t)(units[0] + units[1]);
+  p.rows = (uint32_t)(B * S);
+  p.S = (uint32_t)S;
+  p.div_s = FastDiv((uint32_t)(S > 0 ? S : 1));
+  p.table_stride = tstride;
+  int lg = 0;
+  while ((int64_t(1) << lg) < uh) ++lg;
+  p.uh_log2 = lg;
+  p.sign = sign;
+  return p.units > 0;
+}
+
 template <typename T, typename TT>
 void launch_scalar(const T* x, T* out, const TT* cosine, const TT* sine, const RopeGeom& g,
                    int half, int64_t rows, bool rh, int sms, cudaStream_t stream) {
@@ -265,6 +399,13 @@ int rope_impl(int n, const void* const* xs, const int64_t* const* xsts, void* co
   if (int st = current_device_info(&dev, &sms)) return st;
   const bool rh = layout == PT_ROPE_ROTATE_HALF;
   const int half = (int)(sizes[0][3] / 2);
+  RopeRows<T> rp;
+  if (make_rows<T, TT>(rp, n, xs, xsts, outs, osts, sizes, cos_, sin_, tstride, rh, sign)) {
+    const int grid = (int)std::max<int64_t>(
+        1, std::min<int64_t>(rp.rows, (int64_t)sms * (2048 / kRowThreads)));
+    rope_rows<T, TT><<<grid, kRowThreads, 0, stream>>>(rp, cosine, sine);
+    return check_launch(what);
+  }
   RopeJobs<T> jobs;
   int nvec = 0;
   for (int i = 0; i < n; ++i) {

@@ -130,3 +130,22 @@ def test_query_and_key_in_one_launch(layout, direction):
     qo2, ko2 = gu.rope_qk(direction, q, k_odd, cos, sin, layout)
     assert torch.equal(qo2, qo)
     assert torch.equal(ko2, gu.rope(direction, k_odd, cos, sin, layout))
+
+
+@pytest.mark.parametrize("layout", ["interleaved", "rotate_half"])
+@pytest.mark.parametrize("dtype,tdtype", [(torch.bfloat16, torch.bfloat16),
+                                          (torch.float16, torch.float32),
+                                          (torch.float32, torch.float32)], ids=str)
+def test_rows_path_is_bit_identical_to_the_vector_path(layout, dtype, tdtype):
+    # The same values as the [B,H,S,D] view of [B,S,H,D] memory (contiguous (b, s) rows: the
+    # rows path for interleaved pairs) and as a contiguous [B,H,S,D] tensor (the vector path).
+    b, s, h, d = 2, 40, 6, 64
+    cos, sin = _tables(s, d, 10_000.0, tdtype)
+    rows_view = gu.randn((b, s, h, d), 31, dtype).transpose(1, 2)
+    dense = rows_view.contiguous()
+    for direction in ("fwd", "bwd"):
+        r = gu.rope(direction, rows_view, cos, sin, layout)
+        v = gu.rope(direction, dense, cos, sin, layout)
+        assert torch.equal(r.contiguous(), v), f"{direction} {layout}"
+    tolerance.assert_close(gu.rope("fwd", rows_view, cos, sin, layout),
+                           po.rope_forward(rows_view, cos, sin, "exact", layout), "rows fwd")
