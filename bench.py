@@ -493,6 +493,7 @@ class OpWorkload:
             self.launches_per_step = 2
             self.dominant = ("swiglu_bwd_vec", 5 * tokens * INTER * BF16)
         elif op in ("rope", "rope_rh"):
+            op_name = op
             # rope: the reference's interleaved pairs; rope_rh: the rotate-half pairing that
             # BASELINE config 4 names (same bytes, same kernel, other pair layout).
             self.rope_layout = (_capi.PT_ROPE_ROTATE_HALF if op == "rope_rh"
@@ -510,7 +511,8 @@ class OpWorkload:
             self.cos, self.sin = rotary_cos_sin(2048, 128, 500000.0, device=device, dtype=bf)
             self.bytes = 4 * (self.q[0].numel() + self.k[0].numel()) * BF16
             self.launches_per_step = 2
-            self.dominant = ("rope_vec (q and k, forward)",
+            kernel = "rope_vec" if op_name == "rope_rh" else "rope_rows"
+            self.dominant = (f"{kernel} (q and k, forward)",
                              2 * (self.q[0].numel() + self.k[0].numel()) * BF16)
             self.tokens = b * 2048
         else:
