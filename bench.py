@@ -3,9 +3,10 @@
 Default workload: a Llama-3-8B-shaped norm/activation stack, bf16,
 32 layers x (2 RMSNorm h4096 + SwiGLU i14336), forward then backward, 16384 tokens per GPU
 (4 x 4096), data-parallel over N GPUs; the 64 RMSNorm weight gradients (fp32) are averaged
-over the ranks in four NCCL all-reduces of 16 norms each, each issued as soon as the
-backward has produced its layers and overlapping the backward of the layers below. Every layer has its own inputs (x for both norms, gate,
-up, and the upstream gradients), all larger than L2, so no L2 flush is needed.
+over the ranks in NCCL all-reduces of 8 layers each (layer 0 alone in the last one), each
+issued as soon as the backward has produced its layers and overlapping the backward of the
+layers below. Every layer has its own inputs (x for both norms, gate, up, and the upstream
+gradients), all larger than L2, so no L2 flush is needed.
 
 Numbers reported (rank 0 prints, other ranks stay silent):
 * ``value``: tokens/s of the whole job = N x 16384 / (max over ranks of the CUDA-event
@@ -16,10 +17,16 @@ Numbers reported (rank 0 prints, other ranks stay silent):
   gradients read back to the host inside the timed region.
 * ``roofline``: the dominant kernel (SwiGLU backward) -- algorithmic bytes per launch /
   its mean CUDA-event duration inside the timed region, against MEASURED_PEAKS.json.
-* ``cpu_baseline``: the reference's PyTorch CPU path (the oracle's "eager" form) on a
-  bounded sample of the same workload, rank 0 at N=1 only.
+* ``per_kernel``: every kernel of the step, timed in instrumented steps after the timed
+  region; ``rope_cfg4``: BASELINE config 4 (RoPE q+k forward and backward);
+  ``library_baseline``: the reference's own GPU path (Triton forwards + eager backwards,
+  from the reference installed under baseline/_ref) on the same inputs.
+* ``cpu_baseline``: the reference's PyTorch CPU path (the reference itself from
+  baseline/_ref, else the oracle's eager form) on one full layer of the workload, rank 0 at
+  N=1 only.
 
-``--impl reference`` times only the reference's CPU path (rank 0; other ranks exit 0).
+``--impl reference`` times only that CPU path (rank 0; other ranks exit 0): each "step" is
+one full layer at 16384 tokens, and ``value`` extrapolates to the 32-layer stack.
 
 Run: ``python bench.py [--gpus N --steps K --warmup W]``; for N>1 under torchrun.
 """
@@ -216,10 +223,11 @@ def init_distributed(gpus: int):
     if world > 1:
         import torch.distributed as dist
 
-        # rank 0 must print exactly one line on stdout: NCCL writes its log, the version
-        # banner included, to stdout unless told otherwise, so send it to stderr.
-        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
-            os.environ["NCCL_DEBUG"] = "WARN"
+        # NCCL's INIT log (communicator size, rank, channels, NVLS) goes to stderr so the
+        # rank count can be checked, while rank 0 prints exactly one line on stdout (NCCL
+        # writes to stdout unless NCCL_DEBUG_FILE says otherwise).
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
@@ -247,11 +255,40 @@ def max_over_ranks(value: float, world: int, device) -> float:
 # ---------------------------------------------------------------- CPU reference path --
 
 
-def cpu_reference_layer(tokens: int, seed: int = 0):
-    """One layer of the stack on the reference's PyTorch CPU path (the oracle's eager
-    form: the reference's own forward and backward arithmetic), bf16 like the GPU run."""
+REF_DIR = ROOT / "baseline" / "_ref"
 
-    from oracle import picotron_oracle as po
+
+def import_reference():
+    """The reference package installed under baseline/_ref (pip --target), or None.
+
+    Returns (rms_norm_with_pytorch_forward, swiglu_with_pytorch_forward, triton_rms_norm,
+    triton_swiglu) from picotron.nn.triton_kernels, imported from that directory only."""
+
+    if not (REF_DIR / "picotron" / "__init__.py").is_file():
+        return None
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    import picotron
+
+    if Path(picotron.__file__).resolve().parent != (REF_DIR / "picotron").resolve():
+        raise SystemExit(f"'picotron' resolved to {picotron.__file__}, not {REF_DIR}")
+    from picotron.nn.triton_kernels.rmsnorm import rms_norm_with_pytorch_forward, triton_rms_norm
+    from picotron.nn.triton_kernels.swiglu import swiglu_with_pytorch_forward, triton_swiglu
+
+    return rms_norm_with_pytorch_forward, swiglu_with_pytorch_forward, triton_rms_norm, triton_swiglu
+
+
+def cpu_reference_layer(tokens: int, seed: int = 0):
+    """One layer of the stack (2 RMSNorm + SwiGLU, forward then backward) on the
+    reference's PyTorch CPU path, bf16 activations and fp32 weights like the GPU run.
+
+    With the reference installed under baseline/_ref this runs the reference itself:
+    ``rms_norm_with_pytorch_forward`` and ``swiglu_with_pytorch_forward``
+    (src/picotron/nn/triton_kernels/rmsnorm.py:163, swiglu.py:104, its CPU entry points),
+    then one autograd backward through their ``autograd.Function``s (the RMSNorm forward
+    saves the inverse RMS and the backward consumes it, rmsnorm.py:95-134). Without it, the
+    oracle's eager restatement in the same order (the forward's inverse RMS handed to the
+    backward). Returns (run, kind)."""
 
     g = torch.Generator().manual_seed(seed)
     xs = [torch.randn(tokens, HIDDEN, generator=g).bfloat16() for _ in range(2)]
@@ -261,15 +298,32 @@ def cpu_reference_layer(tokens: int, seed: int = 0):
     up = (torch.randn(tokens, INTER, generator=g) * 2).bfloat16()
     dout = torch.randn(tokens, INTER, generator=g).bfloat16()
 
+    ref = import_reference()
+    if ref is not None:
+        rms_fwd, swiglu_fwd = ref[0], ref[1]
+        params = [torch.nn.Parameter(w) for w in ws]
+
+        def run():
+            for p in params:
+                p.grad = None
+            xin = [x.detach().requires_grad_(True) for x in xs]
+            gi, ui = gate.detach().requires_grad_(True), up.detach().requires_grad_(True)
+            ys = [rms_fwd(x, p, EPS) for x, p in zip(xin, params)]
+            out = swiglu_fwd(gi, ui)
+            torch.autograd.backward([out, ys[1], ys[0]], [dout, dys[1], dys[0]])
+
+        return run, "reference"
+
+    from oracle import picotron_oracle as po
+
     def run():
-        for x, w in zip(xs, ws):
-            po.rms_norm_forward(x, w, EPS, "eager")
+        saved = [po.rms_norm_forward(x, w, EPS, "eager")[1] for x, w in zip(xs, ws)]
         po.swiglu_forward(gate, up, "eager")
         po.swiglu_backward(gate, up, dout, "eager")
-        for x, w, dy in zip(xs, ws, dys):
-            po.rms_norm_backward(x, w, dy, EPS, "eager")
+        for x, w, dy, inv in zip(xs, ws, dys, saved):
+            po.rms_norm_backward(x, w, dy, EPS, "eager", inverse_rms=inv)
 
-    return run
+    return run, "port"
 
 
 def cpu_cores() -> int:
@@ -279,10 +333,27 @@ def cpu_cores() -> int:
         return os.cpu_count() or 1
 
 
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
 def time_cpu_reference(tokens: int, steps: int, warmup: int, layers: int) -> dict:
+    """Times ``steps`` passes of one full layer of the stack on the host cores.
+
+    The timed unit is one layer at ``tokens`` tokens; ``value`` (tokens/s of the whole
+    ``layers``-layer stack) is the one extrapolation: mean layer time x ``layers``."""
+
     cores = cpu_cores()
     torch.set_num_threads(cores)
-    run = cpu_reference_layer(tokens)
+    run, kind = cpu_reference_layer(tokens)
     for _ in range(warmup):
         run()
     times = []
@@ -290,17 +361,24 @@ def time_cpu_reference(tokens: int, steps: int, warmup: int, layers: int) -> dic
         t0 = time.perf_counter()
         run()
         times.append(time.perf_counter() - t0)
-    per_layer = statistics.median(times)
+    per_layer = statistics.fmean(times)
     value = tokens / (per_layer * layers)
+    what = ("the reference itself (baseline/_ref: rms_norm_with_pytorch_forward, "
+            "swiglu_with_pytorch_forward, autograd backward)" if kind == "reference" else
+            "the oracle's eager restatement of the reference (baseline/_ref not installed)")
     return {
         "value": value,
         "unit": "tokens/s",
         "cores": cores,
-        "kind": "port",
-        "sample": (f"1 of {layers} layers (2 RMSNorm + SwiGLU fwd+bwd, bf16) at {tokens} tokens, "
-                   f"median of {steps} after {warmup} warm-up; tokens/s = tokens / (median "
-                   f"layer time x {layers})"),
+        "cpu_model": cpu_model(),
+        "kind": kind,
+        "sample": (f"1 full layer of the {layers}-layer stack (2 RMSNorm h{HIDDEN} + SwiGLU "
+                   f"i{INTER}, fwd+bwd, bf16) at {tokens} tokens, {what}; mean of {steps} "
+                   f"after {warmup} warm-up; tokens/s = {tokens} / (mean layer time x {layers})"),
         "seconds_per_layer": per_layer,
+        "layer_times_s": times,
+        "extrapolation": {"timed_unit": f"1 layer x {tokens} tokens", "layers_timed": 1,
+                          "layers": layers, "factor": layers},
     }
 
 
@@ -339,10 +417,24 @@ class Stack:
         self.partials = torch.empty((self.num_partials, HIDDEN), device=device,
                                     dtype=torch.float32)
         self.launches_per_step = layers * 8
-        self.layers_per_bucket = 8  # dweights of 8 layers (16 norms, 256 KB) per all-reduce
+        # All-reduce buckets of the dweights, by first layer: 8 layers (16 norms, 256 KB)
+        # each, except that layer 0 forms its own bucket (2 norms, 32 KB). The backward runs
+        # from the last layer down, so each bucket's all-reduce overlaps the backward of the
+        # layers below it; only layer 0's small one is left at the end of the step.
+        self.bucket_starts = sorted({0, 1} | set(range(0, layers, 8)) - {layers})
         self.events_per_step = layers  # one (start, end) pair per SwiGLU backward launch
         self.dominant = ("swiglu_bwd_vec (SwiGLU backward)", 5 * tokens * INTER * BF16)
         self.traffic_key = "swiglu_bwd"
+        t = tokens
+        # Algorithmic bytes of one launch of each kernel of the step (inputs read once,
+        # outputs written once); the dweight reduce moves its fp32 partial rows.
+        self.kernel_bytes = {
+            "rmsnorm_fwd": 2 * t * HIDDEN * BF16,
+            "swiglu_fwd": 3 * t * INTER * BF16,
+            "swiglu_bwd": 5 * t * INTER * BF16,
+            "rmsnorm_bwd": 3 * t * HIDDEN * BF16,
+            "rmsnorm_dw_reduce": self.num_partials * HIDDEN * 4,
+        }
 
     # algorithmic bytes (each input read once, each output written once)
     def bytes_per_step(self) -> int:
@@ -355,43 +447,57 @@ class Stack:
         if status != 0:
             raise RuntimeError(f"{name}: {self.capi.last_error()}")
 
-    def step(self, stream: int, world: int, swiglu_bwd_events: list | None = None) -> None:
+    def _launch(self, name: str, timer: dict | None, fn) -> None:
+        if timer is None:
+            self._check(fn(), name)
+            return
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        self._check(fn(), name)
+        b.record()
+        timer.setdefault(name, []).append((a, b))
+
+    def step(self, stream: int, world: int, swiglu_bwd_events: list | None = None,
+             timer: dict | None = None) -> None:
+        """One forward + backward of the stack. ``swiglu_bwd_events``: (start, end) event
+        pairs recorded around the SwiGLU backward launches. ``timer``: when given, every
+        launch is bracketed by events, collected per kernel name (an instrumented step)."""
+
         lib, L, T = self.lib, self.layers, self.tokens
         f32, b16 = self.capi.PT_FLOAT32, self.capi.PT_BFLOAT16
         y, act = self.y.data_ptr(), self.act.data_ptr()
         for l in range(L):
             for k in range(2):
-                self._check(lib.pt_rmsnorm_fwd(self.x[l, k].data_ptr(), HIDDEN,
-                                               self.w[l, k].data_ptr(), y, HIDDEN, None, T,
-                                               HIDDEN, b16, f32, EPS, stream), "rms fwd")
-            self._check(lib.pt_swiglu_fwd(self.gate[l].data_ptr(), self.up[l].data_ptr(), act,
-                                          T * INTER, b16, stream), "swiglu fwd")
+                self._launch("rmsnorm_fwd", timer, lambda: lib.pt_rmsnorm_fwd(
+                    self.x[l, k].data_ptr(), HIDDEN, self.w[l, k].data_ptr(), y, HIDDEN, None,
+                    T, HIDDEN, b16, f32, EPS, stream))
+            self._launch("swiglu_fwd", timer, lambda: lib.pt_swiglu_fwd(
+                self.gate[l].data_ptr(), self.up[l].data_ptr(), act, T * INTER, b16, stream))
         part, P = self.partials.data_ptr(), self.num_partials
         pending = []
+        starts = self.bucket_starts
         for l in reversed(range(L)):
             if swiglu_bwd_events is not None:
                 start, end = swiglu_bwd_events[l]
                 start.record()
-            self._check(lib.pt_swiglu_bwd(self.dout[l].data_ptr(), self.gate[l].data_ptr(),
-                                          self.up[l].data_ptr(), self.dg.data_ptr(),
-                                          self.du.data_ptr(), T * INTER, b16, stream),
-                        "swiglu bwd")
+            self._launch("swiglu_bwd", timer, lambda: lib.pt_swiglu_bwd(
+                self.dout[l].data_ptr(), self.gate[l].data_ptr(), self.up[l].data_ptr(),
+                self.dg.data_ptr(), self.du.data_ptr(), T * INTER, b16, stream))
             if swiglu_bwd_events is not None:
                 end.record()
             for k in (1, 0):
-                self._check(lib.pt_rmsnorm_bwd(self.dy[l, k].data_ptr(), HIDDEN,
-                                               self.x[l, k].data_ptr(), HIDDEN,
-                                               self.w[l, k].data_ptr(), None, self.dx.data_ptr(),
-                                               HIDDEN, part, P, T, HIDDEN, b16, f32, EPS, stream),
-                            "rms bwd")
-                self._check(lib.pt_rmsnorm_dw_reduce(part, P, HIDDEN,
-                                                     self.bucket.slot(2 * l + k).data_ptr(), f32,
-                                                     stream), "dw reduce")
-            if l % self.layers_per_bucket == 0:
+                self._launch("rmsnorm_bwd", timer, lambda: lib.pt_rmsnorm_bwd(
+                    self.dy[l, k].data_ptr(), HIDDEN, self.x[l, k].data_ptr(), HIDDEN,
+                    self.w[l, k].data_ptr(), None, self.dx.data_ptr(), HIDDEN, part, P, T,
+                    HIDDEN, b16, f32, EPS, stream))
+                self._launch("rmsnorm_dw_reduce", timer, lambda: lib.pt_rmsnorm_dw_reduce(
+                    part, P, HIDDEN, self.bucket.slot(2 * l + k).data_ptr(), f32, stream))
+            if l in starts:
                 # This bucket's layers are done: average their dweights over the ranks on
                 # the process group's stream while the earlier layers' backward runs.
-                stop = 2 * min(l + self.layers_per_bucket, L)
-                pending.append(self.bucket.all_reduce_async(2 * l, stop))
+                i = starts.index(l)
+                stop = starts[i + 1] if i + 1 < len(starts) else L
+                pending.append(self.bucket.all_reduce_async(2 * l, 2 * stop))
         for p in pending:
             p.wait()
 
@@ -603,17 +709,149 @@ class OpWorkload:
             if ev: ev[1].record()
         else:
             # Query and key in one launch per direction, as RotaryEmbedding.forward calls it.
-            for (q, k, qo, ko, direction) in ((self.q[i], self.k[i], self.qo, self.ko, "fwd"),
-                                              (self.qo, self.ko, self.q[i], self.k[i], "bwd")):
+            # Events: the first pair brackets the forward launch, a second pair (if given)
+            # the backward launch.
+            for d, (q, k, qo, ko, direction) in enumerate(
+                    ((self.q[i], self.k[i], self.qo, self.ko, "fwd"),
+                     (self.qo, self.ko, self.q[i], self.k[i], "bwd"))):
                 qv, kv = q.transpose(1, 2), k.transpose(1, 2)
                 qov, kov = qo.transpose(1, 2), ko.transpose(1, 2)
-                first = ev is not None and direction == "fwd"
-                if first: ev[0].record()
+                pair = dominant_events[d] if dominant_events and d < len(dominant_events) else None
+                if pair: pair[0].record()
                 c.rope_qk(direction, qv.data_ptr(), qv.stride(), qov.data_ptr(), qov.stride(),
                           qv.shape, kv.data_ptr(), kv.stride(), kov.data_ptr(), kov.stride(),
                           kv.shape, self.cos.data_ptr(), self.sin.data_ptr(), self.cos.stride(0),
                           self.rope_layout, c.PT_BFLOAT16, c.PT_BFLOAT16, stream)
-                if first: ev[1].record()
+                if pair: pair[1].record()
+
+
+def per_kernel_block(stack: Stack, stream: int, world: int, steps: int, peak: float) -> dict:
+    """Mean CUDA-event duration of every kernel of the stack's step, from ``steps``
+    instrumented steps run after the timed region (events around every launch, which the
+    timed steps do not carry), max over ranks."""
+
+    timer: dict = {}
+    for _ in range(steps):
+        stack.step(stream, world, timer=timer)
+    torch.cuda.synchronize()
+    out = {}
+    total_us = 0.0
+    for name, pairs in timer.items():
+        us = statistics.fmean(a.elapsed_time(b) for a, b in pairs) * 1e3
+        us = max_over_ranks(us, world, stack.device)
+        per_step = len(pairs) // steps
+        nbytes = stack.kernel_bytes[name]
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[name] = {"launches_per_step": per_step, "mean_us": us, "bytes_per_launch": nbytes,
+                     "gbs": gbs, "frac_of_hbm_peak": gbs / peak}
+        total_us += us * per_step
+    out["sum_us_per_step"] = total_us
+    out["how"] = (f"{steps} instrumented steps after the timed region, CUDA events around "
+                  "every launch, mean per kernel, max over ranks")
+    return out
+
+
+def rope_cfg4_block(device, stream: int, world: int, steps: int, warmup: int,
+                    peak: float) -> dict:
+    """BASELINE config 4 (q [8,2048,32,128], k [8,2048,8,128] bf16 in the attention layer's
+    [B,S,H,D] memory, theta 5e5, positions 0..2047): the query+key RoPE launch forward and
+    backward, CUDA events around each, for the reference's interleaved pairs and for the
+    rotate-half pairing config 4 names."""
+
+    out = {}
+    for op, label in (("rope", "interleaved"), ("rope_rh", "rotate_half")):
+        work = OpWorkload(op, 16384, device, seed=4321)
+        for _ in range(warmup):
+            work.step(stream, world)
+        torch.cuda.synchronize()
+        pairs = []
+        for _ in range(steps):
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(2)]
+            work.step(stream, world, ev)
+            pairs.append(ev)
+        torch.cuda.synchronize()
+        fwd_us = statistics.fmean(p[0][0].elapsed_time(p[0][1]) for p in pairs) * 1e3
+        bwd_us = statistics.fmean(p[1][0].elapsed_time(p[1][1]) for p in pairs) * 1e3
+        fwd_us = max_over_ranks(fwd_us, world, device)
+        bwd_us = max_over_ranks(bwd_us, world, device)
+        launch_bytes = work.bytes // 2
+        out[label] = {
+            "fwd_us": fwd_us, "bwd_us": bwd_us,
+            "bytes_per_launch": launch_bytes,
+            "fwd_frac_of_hbm_peak": launch_bytes / (fwd_us * 1e-6) / 1e9 / peak,
+            "bwd_frac_of_hbm_peak": launch_bytes / (bwd_us * 1e-6) / 1e9 / peak,
+            "tokens_per_s_fwd_bwd": work.tokens / ((fwd_us + bwd_us) * 1e-6),
+            "kernel": "rope_rows" if op == "rope" else "rope_vec",
+        }
+        del work
+    out["how"] = (f"{steps} steps after {warmup} warm-up, 3 rotating input sets (each larger "
+                  "than L2), CUDA events around each launch, mean, max over ranks")
+    torch.cuda.empty_cache()
+    return out
+
+
+def time_reference_gpu_stack(stack: Stack, steps: int, warmup: int, world: int) -> dict:
+    """The reference's own GPU path on the same inputs: its Triton RMSNorm and SwiGLU
+    forwards and its eager PyTorch backwards (``triton_rms_norm`` and ``triton_swiglu`` of
+    src/picotron/nn/triton_kernels/{rmsnorm,swiglu}.py, imported from the reference
+    installed under baseline/_ref), all layers forward then all backward, as the stack runs.
+    The dweight all-reduce is left out (per-rank timing only). Nothing of this repository
+    runs on that path."""
+
+    why = None
+    ms = float("inf")
+    try:
+        ref = import_reference()
+        if ref is None:
+            why = "the reference is not installed under baseline/_ref"
+        else:
+            _, _, rms_ref, swiglu_ref = ref
+            weights = [torch.nn.Parameter(stack.w[l, k].clone()) for l in range(stack.layers)
+                       for k in range(2)]
+
+            def one_step():
+                for w in weights:
+                    w.grad = None
+                saved = []
+                for l in range(stack.layers):
+                    xa = stack.x[l, 0].detach().requires_grad_(True)
+                    xm = stack.x[l, 1].detach().requires_grad_(True)
+                    g = stack.gate[l].detach().requires_grad_(True)
+                    u = stack.up[l].detach().requires_grad_(True)
+                    saved.append((rms_ref(xa, weights[2 * l], EPS),
+                                  rms_ref(xm, weights[2 * l + 1], EPS), swiglu_ref(g, u)))
+                for l in reversed(range(stack.layers)):
+                    ya, ym, out = saved.pop()
+                    torch.autograd.backward([out, ym, ya],
+                                            [stack.dout[l], stack.dy[l, 1], stack.dy[l, 0]])
+
+            for _ in range(warmup):
+                one_step()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(steps):
+                one_step()
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / steps
+            del weights
+    except Exception as exc:  # recorded, not raised: the reference may not run here
+        why = f"{type(exc).__name__}: {str(exc).splitlines()[0] if str(exc) else ''}"[:300]
+    torch.cuda.empty_cache()
+    ms = max_over_ranks(ms, world, stack.device)  # every rank takes this collective
+    if why is not None or ms == float("inf"):
+        return {"unavailable": why or "failed on another rank"}
+    return {
+        "what": ("the reference's GPU path: Triton forwards + eager PyTorch backwards "
+                 "(triton_rms_norm, triton_swiglu from baseline/_ref), same inputs, all 32 "
+                 "layers, without the dweight all-reduce"),
+        "ms_per_step": ms,
+        "steps": steps,
+        "value": world * stack.tokens / (ms / 1e3),
+        "unit": "tokens/s",
+    }
 
 
 def e2e_run(stack: Stack, steps: int, warmup: int, world: int) -> dict:
@@ -710,7 +948,10 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-tokens", type=int, default=2048)
+    ap.add_argument("--no-extras", action="store_true",
+                    help="stack: skip the config-4 RoPE block and the reference GPU path")
+    ap.add_argument("--cpu-tokens", type=int, default=16384,
+                    help="tokens of the one layer the CPU reference path times")
     ap.add_argument("--workload", choices=["stack", "rmsnorm", "swiglu", "rope", "rope_rh", "addnorm", "mlpup",
                                            "ce", "adamw"],
                     default="stack",
@@ -757,14 +998,19 @@ def main() -> None:
         if rank != 0:
             return
         ref = time_cpu_reference(args.cpu_tokens, args.steps, args.warmup, args.layers)
+        # A "step" of this arm is the timed unit it ran: one full layer of the stack at
+        # --cpu-tokens tokens. Only `value` extrapolates, to the 32-layer stack.
         line = {
             "metric": METRIC, "impl": "reference", "value": ref["value"], "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ref["seconds_per_layer"] * args.layers * 1e3 * 16384 / args.cpu_tokens,
+            "ms_per_step": ref["seconds_per_layer"] * 1e3,
+            "step_unit": ref["extrapolation"]["timed_unit"],
+            "extrapolation": ref["extrapolation"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) inputs of the BASELINE shapes)",
-            "config": config,
-            "cpu_baseline": {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "config": dict(config, tokens_per_gpu=args.cpu_tokens),
+            "cpu_baseline": {k: ref[k] for k in ("value", "unit", "cores", "cpu_model", "kind",
+                                                 "sample")},
             "e2e": {"value": ref["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
         }
@@ -839,6 +1085,15 @@ def main() -> None:
         library_ms = time_library_mlpup(work, stream, args.steps)
         library_what = "cuBLAS gate and up GEMMs (torch.matmul) + this library's SwiGLU kernel"
 
+    per_kernel = rope_cfg4 = reference_gpu = None
+    if args.workload == "stack":
+        # Untimed extras, after the timed region: every kernel of the step on its own
+        # clock, config 4 (RoPE), and the reference's own GPU path on the same inputs.
+        per_kernel = per_kernel_block(work, stream, world, 2, peak)
+        if not args.no_extras:
+            rope_cfg4 = rope_cfg4_block(device, stream, world, 10, 3, peak)
+            reference_gpu = time_reference_gpu_stack(work, 3, 2, world)
+
     e2e = None
     if not args.no_e2e:
         e2e = e2e_run(work, max(1, args.e2e_steps), 1, world)
@@ -846,7 +1101,8 @@ def main() -> None:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         ref = time_cpu_reference(args.cpu_tokens, 3, 1, args.layers)
-        cpu = {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        cpu = {k: ref[k] for k in ("value", "unit", "cores", "cpu_model", "kind", "sample",
+                                   "extrapolation")}
 
     if rank == 0:
         line = {
@@ -888,12 +1144,14 @@ def main() -> None:
                 "algorithmic_flops_per_launch": dom_bytes,
                 "mean_launch_us": dom_ms * 1e3,
             },
-            "library_baseline": None if library_ms is None else {
+            "library_baseline": reference_gpu if library_ms is None else {
                 "what": library_what,
                 "ms_per_step": library_ms,
                 "value": world * getattr(work, "units", work.tokens) / (library_ms / 1e3),
                 "unit": getattr(work, "unit", "tokens/s"),
             },
+            "per_kernel": per_kernel,
+            "rope_cfg4": rope_cfg4,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": work.launches_per_step * args.steps,

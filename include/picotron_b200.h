@@ -8,9 +8,13 @@
  * elements, not bytes), dtype codes and a CUDA stream passed as `void*` (a cudaStream_t;
  * NULL means the legacy default stream). No entry point allocates device memory except
  * where a comment says so; outputs are written into caller-owned buffers, inputs are
- * read-only. Calls are re-entrant: the library keeps no mutable state shared between
- * calls other than a per-device, write-once cache of device properties and the
- * thread-local error string returned by pt_last_error().
+ * read-only. Calls are re-entrant. The state the library shares between calls is:
+ *   - per-device caches of device properties and kernel occupancy (written once);
+ *   - the thread-local error string returned by pt_last_error();
+ *   - per-device error words in device memory, set by a kernel whose bounded wait ran out
+ *     and read and cleared by pt_take_device_error();
+ *   - the device scratch array of pt_rmsnorm_bwd_noalloc (see there), shared by all its
+ *     calls on a device.
  *
  * Every function returns a pt_status. On failure nothing has been launched and
  * pt_last_error() describes the cause on the calling thread. All pointers must be

@@ -43,12 +43,15 @@ def rms_norm_forward(x: Tensor, weight: Tensor, eps: float, mode: str = "eager")
     return (values * inv * weight.float()).to(dtype=x.dtype), inv
 
 
-def rms_norm_backward(x: Tensor, weight: Tensor, dy: Tensor, eps: float, mode: str = "eager"):
+def rms_norm_backward(x: Tensor, weight: Tensor, dy: Tensor, eps: float, mode: str = "eager",
+                      inverse_rms: Tensor | None = None):
     """Returns (dx, dweight).
 
     eager: ``_RMSNormAutogradFunction.backward`` (rmsnorm.py:109-134):
       g = dy * w; dot_mean = mean(g * x); dx = r * (g - x * r^2 * dot_mean);
       dw = sum_rows(dy * x * r); all fp32, dx cast to x dtype, dw to w dtype.
+      ``inverse_rms``: the r the forward saved (rmsnorm.py:103-104, as returned by
+      rms_norm_forward); without it r is recomputed, with the same bits.
     exact: the same in float64, unrounded.
     """
 
@@ -61,7 +64,8 @@ def rms_norm_backward(x: Tensor, weight: Tensor, dy: Tensor, eps: float, mode: s
         dx = inv * (g - xd * inv.square() * dot_mean)
         dw = (gd * xd * inv).reshape(-1, weight.numel()).sum(dim=0)
         return dx, dw
-    inverse_rms = torch.rsqrt(x.float().square().mean(dim=-1, keepdim=True) + eps)
+    if inverse_rms is None:
+        inverse_rms = torch.rsqrt(x.float().square().mean(dim=-1, keepdim=True) + eps)
     x32, w32, g32 = x.float(), weight.float(), dy.float()
     weighted_grad = g32 * w32
     dot_mean = (weighted_grad * x32).mean(dim=-1, keepdim=True)

@@ -47,11 +47,12 @@ class Comparison:
     violations: int
     numel: int
     worst: list
+    floor_only: int = 0  # elements over 2 ulp that pass only through the 2^-16 max floor
 
     def __str__(self) -> str:
         return (f"ok={self.ok} max_abs={self.max_abs:.3e} max_ulp={self.max_ulp:.2f} "
-                f"frac>2ulp={self.frac_over_2ulp:.2e} violations={self.violations}/{self.numel} "
-                f"worst={self.worst}")
+                f"frac>2ulp={self.frac_over_2ulp:.2e} floor_only={self.floor_only} "
+                f"violations={self.violations}/{self.numel} worst={self.worst}")
 
 
 def compare(out: Tensor, exact: Tensor, dtype: torch.dtype | None = None) -> Comparison:
@@ -71,6 +72,7 @@ def compare(out: Tensor, exact: Tensor, dtype: torch.dtype | None = None) -> Com
         return Comparison(True, 0.0, 0.0, 0.0, 0, 0, [])
     finite = torch.isfinite(out64)
     err = (out64 - ex).abs()
+    floor_only = 0
     if dtype == torch.float32:
         bound = FP32_ATOL + FP32_RTOL * ex.abs()
         max_ulp = 0.0
@@ -80,8 +82,10 @@ def compare(out: Tensor, exact: Tensor, dtype: torch.dtype | None = None) -> Com
         ulps = err / u
         bound = LOWP_ULPS * u + LOWP_FLOOR * ex.abs().max()
         max_ulp = float(ulps.max())
-        over2 = float((ulps > 2.0).double().mean())
-        del ulps, u
+        over = ulps > LOWP_ULPS
+        over2 = float(over.double().mean())
+        floor_only = int((over & (err <= bound)).sum())
+        del ulps, u, over
     bad = (~finite) | (err > bound)
     violations = int(bad.sum())
     worst = []
@@ -96,6 +100,7 @@ def compare(out: Tensor, exact: Tensor, dtype: torch.dtype | None = None) -> Com
         violations=violations,
         numel=n,
         worst=worst,
+        floor_only=floor_only,
     )
 
 

@@ -14,6 +14,8 @@ stream while the backward of earlier layers continues). With NCCL the all-reduce
 
 from __future__ import annotations
 
+import datetime
+
 import torch
 import torch.distributed as dist
 from torch import Tensor
@@ -28,9 +30,16 @@ class PendingAllReduce:
     def __init__(self, work, view: Tensor | None, divide_by: int) -> None:
         self._work, self._view, self._divide_by = work, view, divide_by
 
-    def wait(self) -> None:
+    def wait(self, timeout: datetime.timedelta | None = None) -> None:
+        """Completes the all-reduce. A peer that never issues the matching all-reduce makes
+        this raise (RuntimeError / DistBackendError) once ``timeout``, or else the process
+        group's timeout, has passed, instead of waiting for ever."""
+
         if self._work is not None:
-            self._work.wait()
+            if timeout is None:
+                self._work.wait()
+            else:
+                self._work.wait(timeout)
             self._work = None
         if self._view is not None and self._divide_by > 1:
             self._view.div_(self._divide_by)

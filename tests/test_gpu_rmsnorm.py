@@ -128,10 +128,10 @@ def test_full_size_config2_bf16():
     y = gu.rmsnorm_fwd(x, w, 1e-5)
     dx, dw = gu.rmsnorm_bwd(dy, x, w, 1e-5)
     ye, _ = po.rms_norm_forward(x, w, 1e-5, "exact")       # float64 on the GPU
-    tolerance.assert_close(y, ye, "cfg2 y")
+    gu.full_size_parity(y, ye, "cfg2 rmsnorm y", cancels=False)
     del ye
     dxe, dwe = po.rms_norm_backward(x, w, dy, 1e-5, "exact")
-    tolerance.assert_close(dx, dxe, "cfg2 dx")
-    tolerance.assert_close(dw, dwe, "cfg2 dw")
+    gu.full_size_parity(dx, dxe, "cfg2 rmsnorm dx", cancels=True)
+    gu.full_size_parity(dw, dwe, "cfg2 rmsnorm dw", cancels=True)
     del dxe, dwe
     torch.cuda.empty_cache()

@@ -23,13 +23,15 @@ def _tables(s, d, theta, dtype):
     return cos.to(gu.DEV), sin.to(gu.DEV)
 
 
-def _check(x, dy, cos, sin, layout, what):
+def _check(x, dy, cos, sin, layout, what, full_size=False):
     out = gu.rope("fwd", x, cos, sin, layout)
     dx = gu.rope("bwd", dy, cos, sin, layout)
     torch.cuda.synchronize()
     assert out.stride() == x.stride()
-    tolerance.assert_close(out, po.rope_forward(x, cos, sin, "exact", layout), f"{what} fwd")
-    tolerance.assert_close(dx, po.rope_backward(dy, cos, sin, "exact", layout), f"{what} bwd")
+    check = ((lambda o, e, w: gu.full_size_parity(o, e, w, cancels=True)) if full_size
+             else tolerance.assert_close)
+    check(out, po.rope_forward(x, cos, sin, "exact", layout), f"{what} fwd")
+    check(dx, po.rope_backward(dy, cos, sin, "exact", layout), f"{what} bwd")
 
 
 @pytest.mark.parametrize("case", ["rope_bf16", "rope_f32"])
@@ -108,7 +110,7 @@ def test_full_size_config4_bf16():
         x = gu.randn((8, 2048, heads, 128), seed, torch.bfloat16).transpose(1, 2)
         dy = gu.randn((8, 2048, heads, 128), seed + 10, torch.bfloat16).transpose(1, 2)
         for layout in ("interleaved", "rotate_half"):
-            _check(x, dy, cos, sin, layout, f"cfg4 h={heads} {layout}")
+            _check(x, dy, cos, sin, layout, f"cfg4 rope h={heads} {layout}", full_size=True)
     torch.cuda.empty_cache()
 
 
