@@ -388,7 +388,8 @@ def time_cpu_reference(tokens: int, steps: int, warmup: int, layers: int) -> dic
 class Stack:
     """Device-resident inputs of the config-5 stack and its step through the C ABI."""
 
-    def __init__(self, layers: int, tokens: int, device: torch.device, seed: int) -> None:
+    def __init__(self, layers: int, tokens: int, device: torch.device, seed: int,
+                 fused_dw: bool = True) -> None:
         from picotron_b200 import _capi
         from picotron_b200.dist import DWeightBucket
 
@@ -416,7 +417,13 @@ class Stack:
                                                            _capi.PT_FLOAT32)
         self.partials = torch.empty((self.num_partials, HIDDEN), device=device,
                                     dtype=torch.float32)
-        self.launches_per_step = layers * 8
+        # The RMSNorm backward with its dweight reduction in the same launch (the default), or
+        # the backward and the reduce as two launches (--rms-bwd pair, for A/B runs).
+        self.fused_dw = fused_dw
+        self.workspace = torch.zeros(
+            _capi.rmsnorm_bwd_fused_workspace(tokens, HIDDEN, _capi.PT_BFLOAT16,
+                                              _capi.PT_FLOAT32), device=device)
+        self.launches_per_step = layers * (6 if fused_dw else 8)
         # All-reduce buckets of the dweights, by first layer: 8 layers (16 norms, 256 KB)
         # each, except that layer 0 forms its own bucket (2 norms, 32 KB). The backward runs
         # from the last layer down, so each bucket's all-reduce overlaps the backward of the
@@ -474,6 +481,7 @@ class Stack:
             self._launch("swiglu_fwd", timer, lambda: lib.pt_swiglu_fwd(
                 self.gate[l].data_ptr(), self.up[l].data_ptr(), act, T * INTER, b16, stream))
         part, P = self.partials.data_ptr(), self.num_partials
+        ws, ws_floats = self.workspace.data_ptr(), self.workspace.numel()
         pending = []
         starts = self.bucket_starts
         for l in reversed(range(L)):
@@ -486,6 +494,13 @@ class Stack:
             if swiglu_bwd_events is not None:
                 end.record()
             for k in (1, 0):
+                if self.fused_dw:
+                    self._launch("rmsnorm_bwd", timer, lambda: lib.pt_rmsnorm_bwd_fused(
+                        self.dy[l, k].data_ptr(), HIDDEN, self.x[l, k].data_ptr(), HIDDEN,
+                        self.w[l, k].data_ptr(), None, self.dx.data_ptr(), HIDDEN,
+                        self.bucket.slot(2 * l + k).data_ptr(), ws, ws_floats, T, HIDDEN, b16,
+                        f32, EPS, stream))
+                    continue
                 self._launch("rmsnorm_bwd", timer, lambda: lib.pt_rmsnorm_bwd(
                     self.dy[l, k].data_ptr(), HIDDEN, self.x[l, k].data_ptr(), HIDDEN,
                     self.w[l, k].data_ptr(), None, self.dx.data_ptr(), HIDDEN, part, P, T,
@@ -507,10 +522,12 @@ class OpWorkload:
     ABI, on `tokens` rows with rotating input sets larger than L2. Used for per-kernel
     measurement and for small ncu captures; the default workload is the stack."""
 
-    def __init__(self, op: str, tokens: int, device: torch.device, seed: int) -> None:
+    def __init__(self, op: str, tokens: int, device: torch.device, seed: int,
+                 fused_dw: bool = True) -> None:
         from picotron_b200 import _capi
 
         self.capi, self.lib, self.op, self.tokens, self.device = _capi, _capi.library(), op, tokens, device
+        self.fused_dw = fused_dw
         gen = torch.Generator(device=device).manual_seed(seed)
         bf = torch.bfloat16
         sets = 3
@@ -525,9 +542,12 @@ class OpWorkload:
             self.dw = torch.empty(HIDDEN, device=device)
             self.P = _capi.rmsnorm_bwd_num_partials(tokens, HIDDEN, _capi.PT_BFLOAT16, _capi.PT_FLOAT32)
             self.part = torch.empty((self.P, HIDDEN), device=device)
+            self.ws = torch.zeros(_capi.rmsnorm_bwd_fused_workspace(
+                tokens, HIDDEN, _capi.PT_BFLOAT16, _capi.PT_FLOAT32), device=device)
             self.bytes = 5 * tokens * HIDDEN * BF16
-            self.launches_per_step = 3
-            self.dominant = ("rmsnorm_ws (backward)", 3 * tokens * HIDDEN * BF16)
+            self.launches_per_step = 2 if fused_dw else 3
+            self.dominant = ("rmsnorm_ws (backward, with the dweight reduction)",
+                             3 * tokens * HIDDEN * BF16)
         elif op == "addnorm":
             # Fused residual add + RMSNorm (the next-step row): h = res + branch, y = norm(h);
             # backward dx = norm_bwd(dy, h) + dh. Config 2 shapes and distributions.
@@ -542,9 +562,12 @@ class OpWorkload:
             self.P = _capi.add_rmsnorm_bwd_num_partials(tokens, HIDDEN, _capi.PT_BFLOAT16,
                                                         _capi.PT_FLOAT32)
             self.part = torch.empty((self.P, HIDDEN), device=device)
+            self.ws = torch.zeros(_capi.add_rmsnorm_bwd_fused_workspace(
+                tokens, HIDDEN, _capi.PT_BFLOAT16, _capi.PT_FLOAT32), device=device)
             self.bytes = 8 * tokens * HIDDEN * BF16
-            self.launches_per_step = 3
-            self.dominant = ("rmsnorm_ws (fused add, backward)", 4 * tokens * HIDDEN * BF16)
+            self.launches_per_step = 2 if fused_dw else 3
+            self.dominant = ("rmsnorm_ws (fused add, backward, with the dweight reduction)",
+                             4 * tokens * HIDDEN * BF16)
         elif op == "mlpup":
             # SwiGLU fused into the gate/up GEMM (the next-step row): x [tokens, 4096] bf16,
             # w_gate, w_up [14336, 4096] bf16; act, gate and up written (the training forward).
@@ -648,27 +671,42 @@ class OpWorkload:
                                            self.y.data_ptr(), HIDDEN, None, T, HIDDEN,
                                            c.PT_BFLOAT16, c.PT_FLOAT32, EPS, stream), "fwd")
             if ev: ev[0].record()
+            if self.fused_dw:
+                self._check(lib.pt_rmsnorm_bwd_fused(
+                    self.dy[i].data_ptr(), HIDDEN, self.x[i].data_ptr(), HIDDEN, self.w.data_ptr(),
+                    None, self.dx.data_ptr(), HIDDEN, self.dw.data_ptr(), self.ws.data_ptr(),
+                    self.ws.numel(), T, HIDDEN, c.PT_BFLOAT16, c.PT_FLOAT32, EPS, stream), "bwd")
+                if ev: ev[1].record()
+                return
             self._check(lib.pt_rmsnorm_bwd(self.dy[i].data_ptr(), HIDDEN, self.x[i].data_ptr(),
                                            HIDDEN, self.w.data_ptr(), None, self.dx.data_ptr(),
                                            HIDDEN, self.part.data_ptr(), self.P, T, HIDDEN,
                                            c.PT_BFLOAT16, c.PT_FLOAT32, EPS, stream), "bwd")
-            if ev: ev[1].record()
             self._check(lib.pt_rmsnorm_dw_reduce(self.part.data_ptr(), self.P, HIDDEN,
                                                  self.dw.data_ptr(), c.PT_FLOAT32, stream), "red")
+            if ev: ev[1].record()
         elif self.op == "addnorm":
             self._check(lib.pt_add_rmsnorm_fwd(self.res[i].data_ptr(), HIDDEN, self.br[i].data_ptr(),
                                                HIDDEN, self.w.data_ptr(), self.h[i].data_ptr(),
                                                HIDDEN, self.y.data_ptr(), HIDDEN, None, T, HIDDEN,
                                                c.PT_BFLOAT16, c.PT_FLOAT32, EPS, stream), "fwd")
             if ev: ev[0].record()
+            if self.fused_dw:
+                self._check(lib.pt_add_rmsnorm_bwd_fused(
+                    self.dy[i].data_ptr(), HIDDEN, self.dhs[i].data_ptr(), HIDDEN,
+                    self.h[i].data_ptr(), HIDDEN, self.w.data_ptr(), None, self.dx.data_ptr(),
+                    HIDDEN, self.dw.data_ptr(), self.ws.data_ptr(), self.ws.numel(), T, HIDDEN,
+                    c.PT_BFLOAT16, c.PT_FLOAT32, EPS, stream), "bwd")
+                if ev: ev[1].record()
+                return
             self._check(lib.pt_add_rmsnorm_bwd(self.dy[i].data_ptr(), HIDDEN, self.dhs[i].data_ptr(),
                                                HIDDEN, self.h[i].data_ptr(), HIDDEN,
                                                self.w.data_ptr(), None, self.dx.data_ptr(), HIDDEN,
                                                self.part.data_ptr(), self.P, T, HIDDEN,
                                                c.PT_BFLOAT16, c.PT_FLOAT32, EPS, stream), "bwd")
-            if ev: ev[1].record()
             self._check(lib.pt_rmsnorm_dw_reduce(self.part.data_ptr(), self.P, HIDDEN,
                                                  self.dw.data_ptr(), c.PT_FLOAT32, stream), "red")
+            if ev: ev[1].record()
         elif self.op == "mlpup":
             if ev: ev[0].record()
             x = self.x[i % 2]
@@ -948,6 +986,9 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rms-bwd", choices=["fused", "pair"], default="fused",
+                    help="RMSNorm backward: dweight reduced in the same launch (fused) or by a "
+                         "second kernel (pair)")
     ap.add_argument("--no-extras", action="store_true",
                     help="stack: skip the config-4 RoPE block and the reference GPU path")
     ap.add_argument("--cpu-tokens", type=int, default=16384,
@@ -989,6 +1030,8 @@ def main() -> None:
         "parallelism": f"dp{args.gpus}",
         "eps": EPS,
         "weight_dtype": "float32",
+        "rmsnorm_backward": ("dweight reduced in the same launch" if args.rms_bwd == "fused"
+                             else "dweight reduced by a second kernel"),
         "l2": "no flush: every layer has its own inputs, each larger than the 126 MB L2",
     }
 
@@ -1028,9 +1071,11 @@ def main() -> None:
         raise SystemExit(f"device rejected: {_capi.last_error()}")
 
     if args.workload == "stack":
-        work = Stack(args.layers, args.tokens, device, seed=1234 + rank)
+        work = Stack(args.layers, args.tokens, device, seed=1234 + rank,
+                     fused_dw=args.rms_bwd == "fused")
     else:
-        work = OpWorkload(args.workload, args.tokens, device, seed=1234 + rank)
+        work = OpWorkload(args.workload, args.tokens, device, seed=1234 + rank,
+                          fused_dw=args.rms_bwd == "fused")
     stream = torch.cuda.current_stream(device).cuda_stream
     torch.cuda.synchronize()
 

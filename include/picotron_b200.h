@@ -140,6 +140,38 @@ PT_API int pt_rmsnorm_bwd(const void* dy, int64_t dy_row_stride,
 PT_API int pt_rmsnorm_dw_reduce(const float* dw_partials, int num_partials, int64_t hidden,
                          void* dw, int dw_dtype, void* stream);
 
+/* Floats of device workspace that pt_rmsnorm_bwd_fused needs for this problem on the
+ * current device: a 64-float header, then pt_rmsnorm_bwd_num_partials rows of hidden. */
+PT_API int pt_rmsnorm_bwd_fused_workspace(int64_t rows, int64_t hidden, int x_dtype,
+                                          int w_dtype, int64_t* floats);
+
+/* pt_rmsnorm_bwd followed by pt_rmsnorm_dw_reduce in one kernel launch: dx (x dtype) and
+ * dw (w_dtype) with the same bits as that pair given pt_rmsnorm_bwd_num_partials partial
+ * rows. The backward's CTAs, all resident at once (a cooperative launch), write their
+ * dweight partial rows into the workspace, meet at a grid barrier and then reduce the
+ * partials among themselves in the fixed order of pt_rmsnorm_dw_reduce; this saves the
+ * second launch and the partials' trip through a second kernel. Rows the fast pipeline
+ * does not take (misaligned, hidden not a multiple of 16 bytes) run the two kernels
+ * instead, with the same results.
+ * workspace: caller-owned device memory, 256-byte aligned, of at least workspace_floats >=
+ * pt_rmsnorm_bwd_fused_workspace floats. Its first word is the grid barrier's counter,
+ * whose low 31 bits must be zero before the first call: zero the workspace once after
+ * allocating it. Every call that completes leaves the counter that way, so the same
+ * workspace serves any number of calls, of any shape, without clearing; after a device
+ * error reported by pt_take_device_error, zero it again. Calls that share a workspace must
+ * not overlap on the GPU (use one workspace per stream). Replaces
+ * _RMSNormAutogradFunction.backward (src/picotron/nn/triton_kernels/rmsnorm.py:109-134). */
+PT_API int pt_rmsnorm_bwd_fused(const void* dy, int64_t dy_row_stride,
+                                const void* x, int64_t x_row_stride,
+                                const void* weight,
+                                const float* rstd,
+                                void* dx, int64_t dx_row_stride,
+                                void* dw,
+                                float* workspace, int64_t workspace_floats,
+                                int64_t rows, int64_t hidden,
+                                int x_dtype, int w_dtype, float eps,
+                                void* stream);
+
 /* pt_rmsnorm_bwd without any device allocation, for callers that cannot allocate device
  * memory themselves: a host runtime whose memory pool owns all of the device's memory, a
  * training step that must not pay cudaMalloc/cudaFree's implicit device synchronisation,
@@ -204,6 +236,26 @@ PT_API int pt_add_rmsnorm_bwd(const void* dy, int64_t dy_row_stride,
                               int64_t rows, int64_t hidden,
                               int x_dtype, int w_dtype, float eps,
                               void* stream);
+
+/* Workspace floats of pt_add_rmsnorm_bwd_fused (as pt_rmsnorm_bwd_fused_workspace, with
+ * the partial count of pt_add_rmsnorm_bwd_num_partials). */
+PT_API int pt_add_rmsnorm_bwd_fused_workspace(int64_t rows, int64_t hidden, int x_dtype,
+                                              int w_dtype, int64_t* floats);
+
+/* pt_add_rmsnorm_bwd followed by pt_rmsnorm_dw_reduce in one launch, as
+ * pt_rmsnorm_bwd_fused is for pt_rmsnorm_bwd (same workspace contract); dh == NULL is
+ * pt_rmsnorm_bwd_fused. */
+PT_API int pt_add_rmsnorm_bwd_fused(const void* dy, int64_t dy_row_stride,
+                                    const void* dh, int64_t dh_row_stride,
+                                    const void* h, int64_t h_row_stride,
+                                    const void* weight,
+                                    const float* rstd,
+                                    void* dx, int64_t dx_row_stride,
+                                    void* dw,
+                                    float* workspace, int64_t workspace_floats,
+                                    int64_t rows, int64_t hidden,
+                                    int x_dtype, int w_dtype, float eps,
+                                    void* stream);
 
 /* Reads and clears this library's device-side error word of the current device
  * (synchronous: waits for the device). *code = 0 means no kernel reported a problem;

@@ -64,6 +64,17 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                 _c_ptr, _c_int, _c_i64, _c_i64, _c_int, _c_int, _c_float,
                                 _c_ptr]),
     "pt_rmsnorm_dw_reduce": (_c_int, [_c_ptr, _c_int, _c_i64, _c_ptr, _c_int, _c_ptr]),
+    "pt_rmsnorm_bwd_fused_workspace": (_c_int, [_c_i64, _c_i64, _c_int, _c_int,
+                                                ctypes.POINTER(_c_i64)]),
+    "pt_rmsnorm_bwd_fused": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_ptr,
+                                      _c_i64, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_int,
+                                      _c_int, _c_float, _c_ptr]),
+    "pt_add_rmsnorm_bwd_fused_workspace": (_c_int, [_c_i64, _c_i64, _c_int, _c_int,
+                                                    ctypes.POINTER(_c_i64)]),
+    "pt_add_rmsnorm_bwd_fused": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_i64,
+                                          _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_ptr, _c_ptr,
+                                          _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_float,
+                                          _c_ptr]),
     "pt_swiglu_gemm_fwd": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64, _c_ptr, _c_i64,
                                     _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_int,
                                     _c_ptr]),
@@ -229,6 +240,56 @@ def rmsnorm_dw_reduce(dw_partials: int, num_partials: int, hidden: int, dw: int,
     status = library().pt_rmsnorm_dw_reduce(dw_partials, num_partials, hidden, dw, dw_dtype,
                                             stream)
     _check("pt_rmsnorm_dw_reduce", status, error_type)
+
+
+def rmsnorm_bwd_fused_workspace(rows: int, hidden: int, x_dtype: int, w_dtype: int,
+                                error_type: type[Exception] | None = None) -> int:
+    """Floats of workspace that pt_rmsnorm_bwd_fused needs."""
+
+    out = _c_i64(0)
+    status = library().pt_rmsnorm_bwd_fused_workspace(rows, hidden, x_dtype, w_dtype,
+                                                      ctypes.byref(out))
+    _check("pt_rmsnorm_bwd_fused_workspace", status, error_type)
+    return out.value
+
+
+def rmsnorm_bwd_fused(dy: int, dy_row_stride: int, x: int, x_row_stride: int, weight: int,
+                      rstd: int | None, dx: int, dx_row_stride: int, dw: int, workspace: int,
+                      workspace_floats: int, rows: int, hidden: int, x_dtype: int,
+                      w_dtype: int, eps: float, stream: int,
+                      error_type: type[Exception] | None = None) -> None:
+    """RMSNorm backward with the dweight reduction in the same launch (pt_rmsnorm_bwd_fused)."""
+
+    status = library().pt_rmsnorm_bwd_fused(dy, dy_row_stride, x, x_row_stride, weight, rstd,
+                                            dx, dx_row_stride, dw, workspace, workspace_floats,
+                                            rows, hidden, x_dtype, w_dtype, eps, stream)
+    _check("pt_rmsnorm_bwd_fused", status, error_type)
+
+
+def add_rmsnorm_bwd_fused_workspace(rows: int, hidden: int, x_dtype: int, w_dtype: int,
+                                    error_type: type[Exception] | None = None) -> int:
+    """Floats of workspace that pt_add_rmsnorm_bwd_fused needs."""
+
+    out = _c_i64(0)
+    status = library().pt_add_rmsnorm_bwd_fused_workspace(rows, hidden, x_dtype, w_dtype,
+                                                          ctypes.byref(out))
+    _check("pt_add_rmsnorm_bwd_fused_workspace", status, error_type)
+    return out.value
+
+
+def add_rmsnorm_bwd_fused(dy: int, dy_row_stride: int, dh: int | None, dh_row_stride: int,
+                          h: int, h_row_stride: int, weight: int, rstd: int | None, dx: int,
+                          dx_row_stride: int, dw: int, workspace: int, workspace_floats: int,
+                          rows: int, hidden: int, x_dtype: int, w_dtype: int, eps: float,
+                          stream: int, error_type: type[Exception] | None = None) -> None:
+    """Fused residual add + RMSNorm backward with the dweight reduction in the same launch
+    (pt_add_rmsnorm_bwd_fused)."""
+
+    status = library().pt_add_rmsnorm_bwd_fused(dy, dy_row_stride, dh, dh_row_stride, h,
+                                                h_row_stride, weight, rstd, dx, dx_row_stride,
+                                                dw, workspace, workspace_floats, rows, hidden,
+                                                x_dtype, w_dtype, eps, stream)
+    _check("pt_add_rmsnorm_bwd_fused", status, error_type)
 
 
 def rmsnorm_bwd_noalloc(dy: int, dy_row_stride: int, x: int, x_row_stride: int, weight: int,

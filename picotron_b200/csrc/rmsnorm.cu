@@ -150,13 +150,89 @@ __device__ __forceinline__ void record_timeout() {
   atomicExch(&g_device_error, kDeviceErrWaitTimeout);
 }
 
+// ------------------------------------------------------ deterministic dweight sums --
+// The second stage of the dweight reduction, shared by the standalone reduce kernel and
+// the tail of the fused backward so that both give the same bits: column c of dw is the
+// sum of partial rows p = 0 .. P-1, formed as 64 group sums (group g adds rows g, g + 64,
+// g + 128, ... in that order, in fp64), which a fixed shuffle tree then adds; one rounding
+// at the end. The order depends only on P.
+constexpr int kReduceCols = 16;   // columns per chunk (a half-warp of 64-byte loads)
+constexpr int kReduceGroups = 64; // row groups per column
+constexpr int kReduceBatch = 8;   // partial rows loaded per group at once
+constexpr int kReduceItems = kReduceCols * kReduceGroups;
+
+// Reduces the 16-column chunk `chunk` of a [P, hidden] fp32 partial buffer into dw with
+// all threads of the CTA. `s` is a CTA-shared [kReduceCols][kReduceGroups + 1] scratch.
+// Partial rows written by other CTAs of the same grid are read through L2 (ld.global.cg),
+// so a grid barrier before the call is enough to see them. Ends with a CTA barrier.
+template <typename TW>
+__device__ __forceinline__ void dw_reduce_chunk(const float* partials, int P, int64_t hidden,
+                                                int64_t chunk, TW* dw,
+                                                double (*s)[kReduceGroups + 1]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  for (int item = threadIdx.x; item < kReduceItems; item += blockDim.x) {
+    const int col = item & (kReduceCols - 1), group = item >> 4;
+    const int64_t c = chunk * kReduceCols + col;
+    double t = 0.0;
+    if (c < hidden) {
+      for (int p0 = group; p0 < P; p0 += kReduceGroups * kReduceBatch) {
+        float v[kReduceBatch];
+#pragma unroll
+        for (int u = 0; u < kReduceBatch; ++u) {
+          const int p = p0 + u * kReduceGroups;
+          v[u] = p < P ? __ldcg(partials + (int64_t)p * hidden + c) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < kReduceBatch; ++u) t += (double)v[u];
+      }
+    }
+    s[col][group] = t;
+  }
+  __syncthreads();
+  for (int col = warp; col < kReduceCols; col += nwarps) {
+    const int64_t c = chunk * kReduceCols + col;
+    double v = s[col][lane] + s[col][lane + 32];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_down_sync(0xffffffffu, v, off);
+    if (lane == 0 && c < hidden) dw[c] = from_float<TW>((float)v);
+  }
+  __syncthreads();
+}
+
+// Grid-wide barrier of a cooperative launch (all CTAs resident), taken by one thread per
+// CTA after a CTA barrier. `bar` is a word whose low 31 bits are zero between barriers:
+// CTA 0 adds 2^31 - (G - 1) and every other CTA adds 1, so the last arrival flips bit 31
+// and leaves the low bits at zero again; each CTA waits for the flip of the bit it saw.
+// Works for any G and any value of bit 31, so the word never needs resetting. The
+// fences make every CTA's earlier global writes visible to every CTA after the barrier.
+// Bounded like every wait here: false after `limit` SM cycles.
+__device__ __forceinline__ bool grid_barrier(unsigned int* bar, unsigned int nblocks,
+                                             long long limit = kWaitLimitCycles) {
+  __threadfence();
+  const unsigned int add = blockIdx.x == 0 ? 0x80000000u - (nblocks - 1u) : 1u;
+  const unsigned int old = atomicAdd(bar, add);
+  const long long t0 = clock64();
+  for (;;) {
+    unsigned int cur;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(cur) : "l"(bar) : "memory");
+    if ((cur ^ old) & 0x80000000u) break;
+    if (clock64() - t0 > limit) return false;
+  }
+  __threadfence();
+  return true;
+}
+
 // ------------------------------------------------------------ fast fwd / bwd -------
 // Warp roles: warps [0, C) own columns, warps [C, C + RW) reduce rows, warp C + RW is the
 // TMA producer.
 // kAdd (fused residual add): the forward normalizes h = x + aux (aux = the branch output,
 // h rounded to T and written to h_out); the backward adds aux (the gradient that reaches h
 // from its other uses) to dx.
-template <typename T, typename TW, int VPT, bool kBwd, bool kHasRstd, bool kAdd, int kMaxWarps>
+// kFused (backward only, cooperative launch): after writing its partial rows every CTA
+// meets the others at a grid barrier on `grid_bar`, then reduces 16-column chunks of the
+// partials into dw_out (chunk b, b + G, ...) with dw_reduce_chunk: dx and dw in one launch.
+template <typename T, typename TW, int VPT, bool kBwd, bool kHasRstd, bool kAdd, int kMaxWarps,
+          bool kFused>
 __global__ void __launch_bounds__(kMaxWarps * 32,
                                   kMaxWarps <= 16 ? (kBwd ? PT_RMS_MIN_BLOCKS_BWD
                                                           : PT_RMS_MIN_BLOCKS_FWD)
@@ -167,7 +243,9 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
            float* __restrict__ partials_lo, float* __restrict__ zero_row,
            const T* __restrict__ aux, int64_t as, T* __restrict__ h_out, int64_t hs,
            int64_t rows, int nvec, int hidden, int stages, int C, int RW, float hidden_f,
-           float eps) {
+           float eps, unsigned int* __restrict__ grid_bar, TW* __restrict__ dw_out,
+           int num_partials) {
+  static_assert(kBwd || !kFused, "only the backward reduces its dweight in the kernel");
   constexpr int V = Vec16<T>::N;
   // Slot layout: x | dy (backward) | aux (kAdd).
   constexpr int kRowsPerSlot = (kBwd ? 2 : 1) + (kAdd ? 1 : 0);
@@ -237,21 +315,18 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
         pos.advance(1, stages);
       }
     }
-    return;
-  }
-
+  } else if (warp >= C) {
   // ----------------------------------------------------------------- reducer warps --
   // Reducer r owns local rows r, r + RW, ...: it reads the whole row from its slot
   // (lane l takes vectors l, l + 32, ...), forms sum(x^2) (and sum(dy * w * x)), and
   // publishes r = rsqrt(mean(x^2) + eps) (and c = r^2 * mean(dy * w * x)) for the slot.
-  if (warp >= C) {
     const int rid = warp - C;
     RingPos pos;
     pos.advance(rid, stages);
     for (int64_t j = rid; j < n_local; j += RW) {
       if (!mbar_wait_bounded(&full[pos.slot], pos.phase)) {
         record_timeout();
-        return;
+        break;
       }
       const T* sx = slots + (int64_t)(kRowsPerSlot * pos.slot) * row_elems;
       // Four independent paired accumulators (one per vector of an unrolled group of four).
@@ -331,9 +406,7 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
       if (lane == 0) mbar_arrive(&stats[pos.slot]);
       pos.advance(RW, stages);
     }
-    return;
-  }
-
+  } else {
   // ------------------------------------------------------------------ owner warps --
   // Forward: the owners' weights live in registers. Backward: they are read from the
   // staged fp32 copy, leaving the registers to the fp64 dweight accumulators (two CTAs per
@@ -461,10 +534,7 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
       mbar_wait_bounded(&full[pos.slot], pos.phase);
       pos.advance(1, stages);
     }
-    return;
-  }
-
-  if constexpr (kBwd) {
+  } else if constexpr (kBwd) {
     // This CTA's dweight partial rows (zeros when it owned no rows): the running sums in
     // row blockIdx.x of `partials` and their accumulated errors in row blockIdx.x of
     // `partials_lo`, or, without a lo row, their fp32-rounded total.
@@ -500,6 +570,21 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
         if (dz != nullptr) dz[q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       }
     }
+  }
+  }  // owner warps
+
+  if constexpr (kFused) {
+    // Every CTA's partial rows are written: meet at the grid barrier (a cooperative launch
+    // keeps all CTAs resident), then reduce this CTA's chunks of columns in the ring's
+    // shared memory, which no copy uses any more.
+    __syncwarp();
+    __syncthreads();
+    if (threadIdx.x == 0 && !grid_barrier(grid_bar, gridDim.x)) record_timeout();
+    __syncthreads();
+    auto* s = reinterpret_cast<double (*)[kReduceGroups + 1]>(smem);
+    const int64_t chunks = (hidden + kReduceCols - 1) / kReduceCols;
+    for (int64_t chunk = blockIdx.x; chunk < chunks; chunk += gridDim.x)
+      dw_reduce_chunk<TW>(partials, num_partials, hidden, chunk, dw_out, s);
   }
 }
 
@@ -614,48 +699,15 @@ rmsnorm_bwd_generic(const T* __restrict__ dy, int64_t dys, const T* __restrict__
   }
 }
 
-constexpr int kReduceWarps = 32;
-constexpr int kReduceCols = 16;                    // columns per CTA (half a warp)
-constexpr int kReduceGroups = kReduceWarps * 2;    // row groups per CTA (half-warps)
-constexpr int kReduceBatch = 8;                    // partial rows loaded per group at once
+constexpr int kReduceThreads = kReduceItems;  // one (column, group) item per thread
 
 template <typename TW>
-__global__ void __launch_bounds__(kReduceWarps * 32)
+__global__ void __launch_bounds__(kReduceThreads)
 rmsnorm_dw_reduce_kernel(const float* __restrict__ partials, int num_partials, int64_t hidden,
                          TW* __restrict__ dw) {
-  // 16 columns per CTA: each half-warp covers them (64-byte loads) and the 64 half-warps of
-  // the CTA split the partial rows: group g adds rows g, g + 64, g + 128, ... in that order
-  // in fp64, loading kReduceBatch of them at a time. Warp w < 16 then adds the 64 group sums
-  // of column w with a fixed shuffle tree, and the result is rounded once. The order depends
-  // only on num_partials, so the result is deterministic; the fp64 sums of the fp32 partial
-  // pairs (rounded sum, rounded remainder) are exact to far below the output's precision.
+  // One 16-column chunk per CTA (64-byte half-warp loads); dw_reduce_chunk fixes the order.
   __shared__ double s[kReduceCols][kReduceGroups + 1];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int col = lane & (kReduceCols - 1);
-  const int group = warp * 2 + (lane >> 4);
-  const int64_t c = (int64_t)blockIdx.x * kReduceCols + col;
-  double t = 0.0;
-  if (c < hidden) {
-    for (int p0 = group; p0 < num_partials; p0 += kReduceGroups * kReduceBatch) {
-      float v[kReduceBatch];
-#pragma unroll
-      for (int u = 0; u < kReduceBatch; ++u) {
-        const int p = p0 + u * kReduceGroups;
-        v[u] = p < num_partials ? partials[(int64_t)p * hidden + c] : 0.0f;
-      }
-#pragma unroll
-      for (int u = 0; u < kReduceBatch; ++u) t += (double)v[u];
-    }
-  }
-  s[col][group] = t;
-  __syncthreads();
-  if (warp < kReduceCols) {
-    const int64_t cw = (int64_t)blockIdx.x * kReduceCols + warp;
-    double v = s[warp][lane] + s[warp][lane + 32];
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) v += __shfl_down_sync(0xffffffffu, v, off);
-    if (lane == 0 && cw < hidden) dw[cw] = from_float<TW>((float)v);
-  }
+  dw_reduce_chunk<TW>(partials, num_partials, hidden, blockIdx.x, dw, s);
 }
 
 // ------------------------------------------------------------------ host helpers ---
@@ -789,13 +841,20 @@ bool rows_aligned(const void* p, int64_t stride) {
 // Kernel instance for a plan: CTAs of up to kSmallConsumers consumer warps (rows of up to
 // 4 * 32 * kElemsPerThread elements) use any of the three vectors-per-thread shapes under
 // a 5-warp launch bound; bigger CTAs use the full shape under a 17-warp bound.
-#define PT_WS(VPT_, MAXW_) rmsnorm_ws<T, TW, VPT_, kBwd, kHasRstd, kAdd, MAXW_>
+#define PT_WS(VPT_, MAXW_) rmsnorm_ws<T, TW, VPT_, kBwd, kHasRstd, kAdd, MAXW_, kFused>
 template <bool kBwd> constexpr int small_warps() { return kSmallConsumers(kBwd) + kReducers + 1; }
 constexpr int kBigWarps = kMaxConsumers + kReducers + 1;
 inline int ws_threads(const FastPlan& plan) {
   return (plan.consumers + plan.reducers + 1) * 32;
 }
-template <typename T, typename TW, bool kBwd, bool kHasRstd, bool kAdd = false>
+// Dynamic shared memory of a launch: the ring and staged weight, and for the fused
+// backward at least the dweight reduction's scratch, which reuses the ring.
+constexpr int kReduceSmem = (int)sizeof(double) * kReduceCols * (kReduceGroups + 1);
+inline int ws_smem(const FastPlan& plan, bool fused) {
+  return fused ? std::max(plan.smem, kReduceSmem) : plan.smem;
+}
+template <typename T, typename TW, bool kBwd, bool kHasRstd, bool kAdd = false,
+          bool kFused = false>
 const void* ws_kernel(const FastPlan& plan) {
   constexpr int SW = small_warps<kBwd>();
   if (plan.consumers > kSmallConsumers(kBwd))
@@ -805,26 +864,41 @@ const void* ws_kernel(const FastPlan& plan) {
   return (const void*)PT_WS((vpt_quarter<T, kBwd>()), SW);
 }
 
-template <typename T, typename TW, bool kBwd, bool kHasRstd, bool kAdd = false>
-void ws_launch(const FastPlan& plan, int grid, cudaStream_t stream, const T* x, int64_t xs,
-               const T* dy, int64_t dys, const TW* w, const float* rstd_in, T* out, int64_t os,
-               float* rstd_out, float* partials, float* partials_lo, float* zero_row,
-               int64_t rows, int hidden, float eps, const T* aux = nullptr, int64_t as = 0,
-               T* h_out = nullptr, int64_t hs = 0) {
+// Launches the plan's instance on `stream`; kFused launches are cooperative (all CTAs
+// resident at once, which the grid barrier of the fused dweight needs: `grid` must not
+// exceed the resident CTAs of the kernel).
+template <typename T, typename TW, bool kBwd, bool kHasRstd, bool kAdd = false,
+          bool kFused = false>
+cudaError_t ws_launch(const FastPlan& plan, int grid, cudaStream_t stream, const T* x, int64_t xs,
+                      const T* dy, int64_t dys, const TW* w, const float* rstd_in, T* out,
+                      int64_t os, float* rstd_out, float* partials, float* partials_lo,
+                      float* zero_row, int64_t rows, int hidden, float eps,
+                      const T* aux = nullptr, int64_t as = 0, T* h_out = nullptr, int64_t hs = 0,
+                      unsigned int* grid_bar = nullptr, TW* dw_out = nullptr,
+                      int num_partials = 0) {
   constexpr int SW = small_warps<kBwd>();
-  const int threads = ws_threads(plan);
   const float hf = (float)hidden;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((unsigned)ws_threads(plan));
+  cfg.dynamicSmemBytes = (size_t)ws_smem(plan, kFused);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = kFused ? 1 : 0;
 #define PT_WS_ARGS                                                                         \
   x, xs, dy, dys, w, rstd_in, out, os, rstd_out, partials, partials_lo, zero_row, aux, as,  \
-      h_out, hs, rows, plan.nvec, hidden, plan.stages, plan.consumers, plan.reducers, hf, eps
+      h_out, hs, rows, plan.nvec, hidden, plan.stages, plan.consumers, plan.reducers, hf, eps, \
+      grid_bar, dw_out, num_partials
   if (plan.consumers > kSmallConsumers(kBwd))
-    PT_WS((vpt_max<T, kBwd>()), kBigWarps)<<<grid, threads, plan.smem, stream>>>(PT_WS_ARGS);
-  else if (plan.vpt == vpt_max<T, kBwd>())
-    PT_WS((vpt_max<T, kBwd>()), SW)<<<grid, threads, plan.smem, stream>>>(PT_WS_ARGS);
-  else if (plan.vpt == vpt_half<T, kBwd>())
-    PT_WS((vpt_half<T, kBwd>()), SW)<<<grid, threads, plan.smem, stream>>>(PT_WS_ARGS);
-  else
-    PT_WS((vpt_quarter<T, kBwd>()), SW)<<<grid, threads, plan.smem, stream>>>(PT_WS_ARGS);
+    return cudaLaunchKernelEx(&cfg, PT_WS((vpt_max<T, kBwd>()), kBigWarps), PT_WS_ARGS);
+  if (plan.vpt == vpt_max<T, kBwd>())
+    return cudaLaunchKernelEx(&cfg, PT_WS((vpt_max<T, kBwd>()), SW), PT_WS_ARGS);
+  if (plan.vpt == vpt_half<T, kBwd>())
+    return cudaLaunchKernelEx(&cfg, PT_WS((vpt_half<T, kBwd>()), SW), PT_WS_ARGS);
+  return cudaLaunchKernelEx(&cfg, PT_WS((vpt_quarter<T, kBwd>()), SW), PT_WS_ARGS);
 #undef PT_WS_ARGS
 }
 #undef PT_WS
@@ -873,9 +947,14 @@ int num_partials_impl(int64_t rows, int64_t hidden, int* out) {
   if (int st = current_device_info(&dev, &sms)) return st;
   FastPlan plan = plan_fast<T, true, kAdd>(hidden);
   int occ = 0;
-  if (plan.ok)
-    occ = blocks_per_sm(ws_kernel<T, TW, true, false, kAdd>(plan), ws_threads(plan),
-                        plan.smem);
+  if (plan.ok) {
+    // The fused backward launches one CTA per pair of partial rows, all resident at once:
+    // take the smaller occupancy of the two instances so that both can use this count.
+    occ = std::min(blocks_per_sm(ws_kernel<T, TW, true, false, kAdd>(plan), ws_threads(plan),
+                                 plan.smem),
+                   blocks_per_sm(ws_kernel<T, TW, true, false, kAdd, true>(plan),
+                                 ws_threads(plan), ws_smem(plan, true)));
+  }
   int64_t n;
   if (occ > 0) {
     n = (int64_t)sms * occ;
@@ -942,6 +1021,80 @@ int bwd_impl(const void* dy_, int64_t dys, const void* x_, int64_t xs, const voi
         eps, aux, as);
   }
   return check_launch(kAdd ? "pt_add_rmsnorm_bwd" : "pt_rmsnorm_bwd");
+}
+
+// Workspace of the fused backward (pt_rmsnorm_bwd_fused): a 256-byte header whose first
+// word is the grid barrier, then num_partials rows of hidden floats.
+constexpr int64_t kWsHeaderFloats = 64;
+
+template <typename T, typename TW, bool kAdd = false>
+int fused_workspace_impl(int64_t rows, int64_t hidden, int64_t* floats) {
+  int P = 0;
+  if (int st = num_partials_impl<T, TW, kAdd>(rows, hidden, &P)) return st;
+  *floats = kWsHeaderFloats + (int64_t)P * hidden;
+  return ok();
+}
+
+// dx and dw in one cooperative launch of the pipeline (its CTAs reduce the dweight
+// partials among themselves after a grid barrier), for the same partial count
+// (num_partials_impl) and the same summation order as bwd_impl + pt_rmsnorm_dw_reduce, so
+// the results are bit-identical to that pair. Rows the pipeline cannot take (misaligned,
+// hidden not a multiple of 16 bytes) run the generic kernel and the reduce kernel instead.
+template <typename T, typename TW, bool kAdd = false>
+int fused_bwd_impl(const void* dy_, int64_t dys, const void* x_, int64_t xs, const void* w_,
+                   const float* rstd, void* dx_, int64_t dxs, void* dw_, float* ws,
+                   int64_t ws_floats, int64_t rows, int64_t hidden, float eps,
+                   cudaStream_t stream, const void* aux_ = nullptr, int64_t as = 0) {
+  const char* what = kAdd ? "pt_add_rmsnorm_bwd_fused" : "pt_rmsnorm_bwd_fused";
+  const T* dy = static_cast<const T*>(dy_);
+  const T* x = static_cast<const T*>(x_);
+  const TW* w = static_cast<const TW*>(w_);
+  T* dx = static_cast<T*>(dx_);
+  TW* dw = static_cast<TW*>(dw_);
+  const T* aux = static_cast<const T*>(aux_);
+  int dev = 0, sms = 0;
+  if (int st = current_device_info(&dev, &sms)) return st;
+  int P = 0;
+  if (int st = num_partials_impl<T, TW, kAdd>(rows, hidden, &P)) return st;
+  const int64_t need = kWsHeaderFloats + (int64_t)P * hidden;
+  if (ws_floats < need)
+    return set_error(PT_ERR_SHAPE, "%s: workspace of %lld floats is smaller than the %lld this "
+                     "call needs", what, (long long)ws_floats, (long long)need);
+  unsigned int* bar = reinterpret_cast<unsigned int*>(ws);
+  float* partials = ws + kWsHeaderFloats;
+  FastPlan plan = plan_fast<T, true, kAdd>(hidden);
+  bool fast = plan.ok && rows_aligned<T>(x, xs) && rows_aligned<T>(dy, dys) &&
+              rows_aligned<T>(dx, dxs) && aligned16(w) && aligned16(partials);
+  if (kAdd) fast = fast && rows_aligned<T>(aux, as);
+  const bool hr = rstd != nullptr;
+  const PartialLayout lay = partial_layout(partials, P, hidden);
+  if (fast) {
+    const void* fn = hr ? ws_kernel<T, TW, true, true, kAdd, true>(plan)
+                        : ws_kernel<T, TW, true, false, kAdd, true>(plan);
+    fast = (int64_t)sms * blocks_per_sm(fn, ws_threads(plan), ws_smem(plan, true)) >= lay.grid;
+  }
+  if (fast) {
+    const cudaError_t e =
+        hr ? ws_launch<T, TW, true, true, kAdd, true>(
+                 plan, lay.grid, stream, x, xs, dy, dys, w, rstd, dx, dxs, nullptr, partials,
+                 lay.lo, lay.zero_row, rows, (int)hidden, eps, aux, as, nullptr, 0, bar, dw, P)
+           : ws_launch<T, TW, true, false, kAdd, true>(
+                 plan, lay.grid, stream, x, xs, dy, dys, w, nullptr, dx, dxs, nullptr, partials,
+                 lay.lo, lay.zero_row, rows, (int)hidden, eps, aux, as, nullptr, 0, bar, dw, P);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return set_error(PT_ERR_CUDA, "%s: cooperative launch failed: %s", what,
+                       cudaGetErrorString(e));
+    }
+    return check_launch(what);
+  }
+  rmsnorm_bwd_generic<T, TW><<<lay.grid, kGenericThreads, 0, stream>>>(
+      dy, dys, x, xs, w, rstd, dx, dxs, partials, lay.lo, lay.zero_row, rows, (int)hidden, eps,
+      aux, as);
+  if (int st = check_launch(what)) return st;
+  const int grid = (int)((hidden + kReduceCols - 1) / kReduceCols);
+  rmsnorm_dw_reduce_kernel<TW><<<grid, kReduceThreads, 0, stream>>>(partials, P, hidden, dw);
+  return check_launch(what);
 }
 
 // Dispatch on the (x, w) dtype pair. Returns PT_ERR_UNSUPPORTED_DTYPE for pairs that
@@ -1042,6 +1195,48 @@ int pt_rmsnorm_bwd(const void* dy, int64_t dy_row_stride, const void* x, int64_t
   });
 }
 
+int pt_rmsnorm_bwd_fused_workspace(int64_t rows, int64_t hidden, int x_dtype, int w_dtype,
+                                   int64_t* floats) {
+  if (floats == nullptr) return set_error(PT_ERR_INVALID_ARGUMENT, "floats is NULL");
+  if (int st = check_shape(rows, hidden)) return st;
+  return dispatch_xw(x_dtype, w_dtype, [&](auto* tx, auto* tw) {
+    using T = std::remove_pointer_t<decltype(tx)>;
+    using TW = std::remove_pointer_t<decltype(tw)>;
+    return fused_workspace_impl<T, TW>(rows, hidden, floats);
+  });
+}
+
+int pt_rmsnorm_bwd_fused(const void* dy, int64_t dy_row_stride, const void* x,
+                         int64_t x_row_stride, const void* weight, const float* rstd, void* dx,
+                         int64_t dx_row_stride, void* dw, float* workspace,
+                         int64_t workspace_floats, int64_t rows, int64_t hidden, int x_dtype,
+                         int w_dtype, float eps, void* stream) {
+  if (int st = check_shape(rows, hidden)) return st;
+  if (!(eps >= 0.0f)) return set_error(PT_ERR_INVALID_ARGUMENT, "eps must be >= 0");
+  if (int st = check_device_ptr(weight, "weight")) return st;
+  if (int st = check_device_ptr(dw, "dw")) return st;
+  if (int st = check_device_ptr(workspace, "workspace")) return st;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return set_error(PT_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+  if (rows > 0) {
+    if (int st = check_row_stride(dy_row_stride, hidden, "dy_row_stride")) return st;
+    if (int st = check_row_stride(x_row_stride, hidden, "x_row_stride")) return st;
+    if (int st = check_row_stride(dx_row_stride, hidden, "dx_row_stride")) return st;
+    if (int st = check_device_ptr(dy, "dy")) return st;
+    if (int st = check_device_ptr(x, "x")) return st;
+    if (int st = check_device_ptr(dx, "dx")) return st;
+    if (rstd)
+      if (int st = check_device_ptr(rstd, "rstd")) return st;
+  }
+  return dispatch_xw(x_dtype, w_dtype, [&](auto* tx, auto* tw) {
+    using T = std::remove_pointer_t<decltype(tx)>;
+    using TW = std::remove_pointer_t<decltype(tw)>;
+    return fused_bwd_impl<T, TW>(dy, dy_row_stride, x, x_row_stride, weight, rstd, dx,
+                                 dx_row_stride, dw, workspace, workspace_floats, rows, hidden,
+                                 eps, as_stream(stream));
+  });
+}
+
 int pt_add_rmsnorm_fwd(const void* residual, int64_t residual_row_stride, const void* branch,
                        int64_t branch_row_stride, const void* weight, void* h_out,
                        int64_t h_row_stride, void* y, int64_t y_row_stride, float* rstd,
@@ -1123,6 +1318,57 @@ int pt_add_rmsnorm_bwd(const void* dy, int64_t dy_row_stride, const void* dh,
   });
 }
 
+int pt_add_rmsnorm_bwd_fused_workspace(int64_t rows, int64_t hidden, int x_dtype, int w_dtype,
+                                       int64_t* floats) {
+  if (floats == nullptr) return set_error(PT_ERR_INVALID_ARGUMENT, "floats is NULL");
+  if (int st = check_shape(rows, hidden)) return st;
+  return dispatch_xw(x_dtype, w_dtype, [&](auto* tx, auto* tw) {
+    using T = std::remove_pointer_t<decltype(tx)>;
+    using TW = std::remove_pointer_t<decltype(tw)>;
+    return fused_workspace_impl<T, TW, true>(rows, hidden, floats);
+  });
+}
+
+int pt_add_rmsnorm_bwd_fused(const void* dy, int64_t dy_row_stride, const void* dh,
+                             int64_t dh_row_stride, const void* h, int64_t h_row_stride,
+                             const void* weight, const float* rstd, void* dx,
+                             int64_t dx_row_stride, void* dw, float* workspace,
+                             int64_t workspace_floats, int64_t rows, int64_t hidden,
+                             int x_dtype, int w_dtype, float eps, void* stream) {
+  if (dh == nullptr)
+    return pt_rmsnorm_bwd_fused(dy, dy_row_stride, h, h_row_stride, weight, rstd, dx,
+                                dx_row_stride, dw, workspace, workspace_floats, rows, hidden,
+                                x_dtype, w_dtype, eps, stream);
+  if (int st = check_shape(rows, hidden)) return st;
+  if (!(eps >= 0.0f)) return set_error(PT_ERR_INVALID_ARGUMENT, "eps must be >= 0");
+  if (int st = check_device_ptr(weight, "weight")) return st;
+  if (int st = check_device_ptr(dw, "dw")) return st;
+  if (int st = check_device_ptr(workspace, "workspace")) return st;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return set_error(PT_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+  if (rows > 0) {
+    if (int st = check_row_stride(dy_row_stride, hidden, "dy_row_stride")) return st;
+    if (int st = check_row_stride(dh_row_stride, hidden, "dh_row_stride")) return st;
+    if (int st = check_row_stride(h_row_stride, hidden, "h_row_stride")) return st;
+    if (int st = check_row_stride(dx_row_stride, hidden, "dx_row_stride")) return st;
+    if (int st = check_device_ptr(dy, "dy")) return st;
+    if (int st = check_device_ptr(dh, "dh")) return st;
+    if (int st = check_device_ptr(h, "h")) return st;
+    if (int st = check_device_ptr(dx, "dx")) return st;
+    if (rstd)
+      if (int st = check_device_ptr(rstd, "rstd")) return st;
+    if (dx == dy || dx == h)
+      return set_error(PT_ERR_INVALID_ARGUMENT, "dx may alias dh only");
+  }
+  return dispatch_xw(x_dtype, w_dtype, [&](auto* tx, auto* tw) {
+    using T = std::remove_pointer_t<decltype(tx)>;
+    using TW = std::remove_pointer_t<decltype(tw)>;
+    return fused_bwd_impl<T, TW, true>(dy, dy_row_stride, h, h_row_stride, weight, rstd, dx,
+                                       dx_row_stride, dw, workspace, workspace_floats, rows,
+                                       hidden, eps, as_stream(stream), dh, dh_row_stride);
+  });
+}
+
 int pt_rmsnorm_dw_reduce(const float* dw_partials, int num_partials, int64_t hidden, void* dw,
                          int dw_dtype, void* stream) {
   if (num_partials < 1)
@@ -1132,7 +1378,7 @@ int pt_rmsnorm_dw_reduce(const float* dw_partials, int num_partials, int64_t hid
   if (int st = check_device_ptr(dw_partials, "dw_partials")) return st;
   if (int st = check_device_ptr(dw, "dw")) return st;
   const int grid = (int)((hidden + kReduceCols - 1) / kReduceCols);
-  const int threads = kReduceWarps * 32;
+  const int threads = kReduceThreads;
   cudaStream_t s = as_stream(stream);
   switch (dw_dtype) {
     case PT_FLOAT32:

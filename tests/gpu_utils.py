@@ -221,3 +221,40 @@ def rope_qk(direction: str, q, k, cos, sin, layout: str = "interleaved"):
                   sin.data_ptr(), cos.stride(0), code[layout], DTYPE_CODES[q.dtype],
                   DTYPE_CODES[cos.dtype], stream())
     return qo, ko
+
+
+def fused_workspace(rows: int, hidden: int, x_dtype, w_dtype, add: bool = False):
+    """A zeroed workspace of the size pt_(add_)rmsnorm_bwd_fused asks for."""
+
+    query = _capi.add_rmsnorm_bwd_fused_workspace if add else _capi.rmsnorm_bwd_fused_workspace
+    floats = query(rows, hidden, DTYPE_CODES[x_dtype], DTYPE_CODES[w_dtype])
+    return torch.zeros(floats, dtype=torch.float32, device=DEV)
+
+
+def rmsnorm_bwd_fused(dy2d, x2d, w, eps, rstd=None, ws=None):
+    rows, hidden = x2d.shape
+    if ws is None:
+        ws = fused_workspace(rows, hidden, x2d.dtype, w.dtype)
+    dx = torch.empty((rows, hidden), dtype=x2d.dtype, device=x2d.device)
+    dw = torch.full((hidden,), float("nan"), dtype=w.dtype, device=x2d.device)
+    _capi.rmsnorm_bwd_fused(dy2d.data_ptr(), dy2d.stride(0), x2d.data_ptr(), x2d.stride(0),
+                            w.data_ptr(), rstd.data_ptr() if rstd is not None else None,
+                            dx.data_ptr(), dx.stride(0), dw.data_ptr(), ws.data_ptr(),
+                            ws.numel(), rows, hidden, DTYPE_CODES[x2d.dtype],
+                            DTYPE_CODES[w.dtype], eps, stream())
+    return dx, dw
+
+
+def add_rmsnorm_bwd_fused(dy2d, dh2d, h2d, w, eps, ws=None):
+    rows, hidden = h2d.shape
+    if ws is None:
+        ws = fused_workspace(rows, hidden, h2d.dtype, w.dtype, add=True)
+    dx = torch.empty_like(h2d)
+    dw = torch.full((hidden,), float("nan"), dtype=w.dtype, device=h2d.device)
+    _capi.add_rmsnorm_bwd_fused(dy2d.data_ptr(), dy2d.stride(0),
+                                dh2d.data_ptr() if dh2d is not None else None,
+                                dh2d.stride(0) if dh2d is not None else 0, h2d.data_ptr(),
+                                h2d.stride(0), w.data_ptr(), None, dx.data_ptr(), dx.stride(0),
+                                dw.data_ptr(), ws.data_ptr(), ws.numel(), rows, hidden,
+                                DTYPE_CODES[h2d.dtype], DTYPE_CODES[w.dtype], eps, stream())
+    return dx, dw
