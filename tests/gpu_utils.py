@@ -35,12 +35,17 @@ def stream() -> int:
 # ulp of the result only when |result| < about 2^-16 of the terms: a few elements in 10^5
 # for these distributions, which the tolerance's 2^-16 max floor admits. Those are counted
 # (floor_only) and bounded here.
+# A GEMM output is a sum of K products accumulated in fp32: its error is about
+# sqrt(K) * 2^-24 of the sum of |terms|, so at K = 4096 the outputs smaller than about
+# 2^-10 of that sum (about one in 10^4 for these inputs) exceed 2 ulp, inside the floor.
 MAX_ULP_ROUNDED_ONCE = 1.0
 MAX_FRAC_OVER_2ULP_CANCELLING = 1e-4
+MAX_FRAC_OVER_2ULP_GEMM_K4096 = 1e-3
 
 
 def full_size_parity(out: torch.Tensor, exact: torch.Tensor, what: str, cancels: bool,
-                     dtype: torch.dtype | None = None):
+                     dtype: torch.dtype | None = None,
+                     max_frac_over_2ulp: float = MAX_FRAC_OVER_2ULP_CANCELLING):
     """assert_close plus the ulp statistics of a full-size output: asserts the bounds above
     for 16-bit outputs and appends one JSON line per output to $PT_PARITY_LOG when set."""
 
@@ -60,7 +65,7 @@ def full_size_parity(out: torch.Tensor, exact: torch.Tensor, what: str, cancels:
             fh.write(json.dumps(rec) + "\n")
     if dt != torch.float32:
         if cancels:
-            assert r.frac_over_2ulp <= MAX_FRAC_OVER_2ULP_CANCELLING, f"{what}: {r}"
+            assert r.frac_over_2ulp <= max_frac_over_2ulp, f"{what}: {r}"
         else:
             assert r.max_ulp <= MAX_ULP_ROUNDED_ONCE and r.floor_only == 0, f"{what}: {r}"
     return r

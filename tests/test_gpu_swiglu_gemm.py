@@ -129,8 +129,10 @@ def test_llama_mlp_shape_against_library_gemm():
     torch.cuda.synchronize()
     rows = torch.arange(0, m, 61, device=gu.DEV)
     ge, ue, _ = po.gate_up_forward(x[rows], wg, wu, "exact")
-    gu.full_size_parity(g[rows], ge, "llama gate_up gemm gate (row sample)", cancels=True)
-    gu.full_size_parity(u[rows], ue, "llama gate_up gemm up (row sample)", cancels=True)
+    gu.full_size_parity(g[rows], ge, "llama gate_up gemm gate (row sample)", cancels=True,
+                        max_frac_over_2ulp=gu.MAX_FRAC_OVER_2ULP_GEMM_K4096)
+    gu.full_size_parity(u[rows], ue, "llama gate_up gemm up (row sample)", cancels=True,
+                        max_frac_over_2ulp=gu.MAX_FRAC_OVER_2ULP_GEMM_K4096)
     del ge, ue
     gu.full_size_parity(act[rows], po.swiglu_forward(g[rows], u[rows], "exact"),
                         "llama gate_up gemm act (row sample)", cancels=False)
