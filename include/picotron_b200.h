@@ -177,10 +177,14 @@ PT_API int pt_rmsnorm_bwd_fused(const void* dy, int64_t dy_row_stride,
  * training step that must not pay cudaMalloc/cudaFree's implicit device synchronisation,
  * or a thin FFI binding with no allocator to size and keep a dw_partials buffer. Computes
  * dx (x dtype) and dw (w_dtype) directly. It has no counterpart in the reference.
- * The dweight partials go to a scratch array inside the library (2^21 floats = 8 MiB per
- * device, kept until the process exits); hidden above 2^21 is rejected with PT_ERR_SHAPE.
+ * The dweight partials go to a scratch array inside the library (2^22 floats = 16 MiB per
+ * device, kept until the process exits); hidden above 2^22 is rejected with PT_ERR_SHAPE.
+ * The array holds the partial rows of every CTA pt_rmsnorm_bwd would use on a B200 up to
+ * hidden 7085; for wider rows the call runs fewer CTAs than pt_rmsnorm_bwd (as many as
+ * the array has rows for) and may be slower, with the same kind of result.
  * The first call on a device looks up that array's address (cudaGetSymbolAddress), so
- * make it before any stream capture. All calls share the one array: calls whose work
+ * make it before any stream capture; the address is kept for the life of the process, so
+ * do not call this entry point after cudaDeviceReset. All calls share the one array: calls whose work
  * overlaps on the GPU (different streams, or different host threads on one device without
  * ordering) race on it and must be serialised by the caller. Nothing in the array needs
  * to start at zero: each call writes every partial it later reads. */

@@ -161,33 +161,61 @@ constexpr int kReduceGroups = 64; // row groups per column
 constexpr int kReduceBatch = 8;   // partial rows loaded per group at once
 constexpr int kReduceItems = kReduceCols * kReduceGroups;
 
-// Reduces the 16-column chunk `chunk` of a [P, hidden] fp32 partial buffer into dw with
-// all threads of the CTA. `s` is a CTA-shared [kReduceCols][kReduceGroups + 1] scratch.
-// Partial rows written by other CTAs of the same grid are read through L2 (ld.global.cg),
-// so a grid barrier before the call is enough to see them. Ends with a CTA barrier.
-template <typename TW>
+// Group sums of one 16-column chunk of a [P, hidden] fp32 partial buffer: this thread's
+// items (column, group) = item & 15, item >> 4 for item = first + threadIdx.x + k *
+// blockDim.x, k < kItems, each the fp64 sum of rows group, group + 64, ... in that order,
+// written to s[column][group]. The loads of all of a thread's items are issued together,
+// kReduceBatch rows per item at a time, so a thread waits for L2 once per batch, not once
+// per item and batch. Partial rows written by other CTAs of the same grid are read
+// through L2 (ld.global.cg), so a grid barrier before the call is enough to see them.
+template <int kItems>
+__device__ __forceinline__ void dw_group_sums(const float* partials, int P, int64_t hidden,
+                                              int64_t chunk, int first,
+                                              double (*s)[kReduceGroups + 1]) {
+  double t[kItems];
+  const float* base[kItems];
+  int group[kItems];
+#pragma unroll
+  for (int k = 0; k < kItems; ++k) {
+    const int item = first + threadIdx.x + k * blockDim.x;
+    const int64_t c = chunk * kReduceCols + (item & (kReduceCols - 1));
+    t[k] = 0.0;
+    // Items past the chunk or past the last column read nothing (group = P).
+    group[k] = (item < kReduceItems && c < hidden) ? (item >> 4) : P;
+    base[k] = partials + c;
+  }
+  for (int p0 = 0; p0 < P; p0 += kReduceGroups * kReduceBatch) {
+    float v[kItems][kReduceBatch];
+#pragma unroll
+    for (int k = 0; k < kItems; ++k)
+#pragma unroll
+      for (int u = 0; u < kReduceBatch; ++u) {
+        const int p = p0 + group[k] + u * kReduceGroups;
+        v[k][u] = p < P ? __ldcg(base[k] + (int64_t)p * hidden) : 0.0f;
+      }
+#pragma unroll
+    for (int k = 0; k < kItems; ++k)
+#pragma unroll
+      for (int u = 0; u < kReduceBatch; ++u) t[k] += (double)v[k][u];
+  }
+#pragma unroll
+  for (int k = 0; k < kItems; ++k) {
+    const int item = first + threadIdx.x + k * blockDim.x;
+    if (item < kReduceItems) s[item & (kReduceCols - 1)][item >> 4] = t[k];
+  }
+}
+
+// Reduces the 16-column chunk `chunk` into dw with all threads of the CTA, kItems items
+// per thread per pass (as many passes as the CTA's size needs): the group sums, then a
+// fixed shuffle tree per column. `s` is a CTA-shared [kReduceCols][kReduceGroups + 1]
+// scratch. Ends with a CTA barrier.
+template <typename TW, int kItems>
 __device__ __forceinline__ void dw_reduce_chunk(const float* partials, int P, int64_t hidden,
                                                 int64_t chunk, TW* dw,
                                                 double (*s)[kReduceGroups + 1]) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-  for (int item = threadIdx.x; item < kReduceItems; item += blockDim.x) {
-    const int col = item & (kReduceCols - 1), group = item >> 4;
-    const int64_t c = chunk * kReduceCols + col;
-    double t = 0.0;
-    if (c < hidden) {
-      for (int p0 = group; p0 < P; p0 += kReduceGroups * kReduceBatch) {
-        float v[kReduceBatch];
-#pragma unroll
-        for (int u = 0; u < kReduceBatch; ++u) {
-          const int p = p0 + u * kReduceGroups;
-          v[u] = p < P ? __ldcg(partials + (int64_t)p * hidden + c) : 0.0f;
-        }
-#pragma unroll
-        for (int u = 0; u < kReduceBatch; ++u) t += (double)v[u];
-      }
-    }
-    s[col][group] = t;
-  }
+  for (int first = 0; first < kReduceItems; first += kItems * blockDim.x)
+    dw_group_sums<kItems>(partials, P, hidden, chunk, first, s);
   __syncthreads();
   for (int col = warp; col < kReduceCols; col += nwarps) {
     const int64_t c = chunk * kReduceCols + col;
@@ -584,7 +612,7 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
     auto* s = reinterpret_cast<double (*)[kReduceGroups + 1]>(smem);
     const int64_t chunks = (hidden + kReduceCols - 1) / kReduceCols;
     for (int64_t chunk = blockIdx.x; chunk < chunks; chunk += gridDim.x)
-      dw_reduce_chunk<TW>(partials, num_partials, hidden, chunk, dw_out, s);
+      dw_reduce_chunk<TW, 3>(partials, num_partials, hidden, chunk, dw_out, s);
   }
 }
 
@@ -707,7 +735,7 @@ rmsnorm_dw_reduce_kernel(const float* __restrict__ partials, int num_partials, i
                          TW* __restrict__ dw) {
   // One 16-column chunk per CTA (64-byte half-warp loads); dw_reduce_chunk fixes the order.
   __shared__ double s[kReduceCols][kReduceGroups + 1];
-  dw_reduce_chunk<TW>(partials, num_partials, hidden, blockIdx.x, dw, s);
+  dw_reduce_chunk<TW, 1>(partials, num_partials, hidden, blockIdx.x, dw, s);
 }
 
 // ------------------------------------------------------------------ host helpers ---
@@ -1401,12 +1429,15 @@ int pt_rmsnorm_dw_reduce(const float* dw_partials, int num_partials, int64_t hid
 
 // ------------------------------------------------------- allocation-free backward --
 // Scratch for pt_rmsnorm_bwd_noalloc: the dweight partials live in this file-scope device
-// array (kNoAllocFloats floats = 8 MiB, held by every device that loads the library until
-// the process exits). Host code must not use the symbol itself as a device address: its
-// address on a device comes from cudaGetSymbolAddress, taken once per device.
+// array (kNoAllocFloats floats = 16 MiB, held by every device that loads the library until
+// the process exits): room for the full partial count of a B200 (two rows for each of 296
+// CTAs) up to hidden 7085; wider rows run the backward with fewer CTAs. Host code must not
+// use the symbol itself as a device address: its address on a device comes from
+// cudaGetSymbolAddress, taken once per device and kept for the life of the process (it is
+// not looked up again after cudaDeviceReset).
 namespace pt {
 namespace {
-constexpr int64_t kNoAllocFloats = int64_t(1) << 21;
+constexpr int64_t kNoAllocFloats = int64_t(1) << 22;
 constexpr int kNoAllocMaxDevices = 64;
 __device__ __align__(256) float g_noalloc_partials[kNoAllocFloats];
 std::mutex g_noalloc_mu;

@@ -104,23 +104,6 @@ class _OnDevice:
             torch.cuda.set_device(self.previous)
 
 
-# Workspaces of the fused RMSNorm backwards (pt_rmsnorm_bwd_fused), one per (device, stream).
-# The C ABI wants the workspace zeroed once and leaves it reusable by every call; calls on
-# one stream never overlap on the GPU, and no two streams share a workspace. A call that
-# needs more than the cached one gets a new, larger one (the old one is freed in stream
-# order by the caching allocator).
-_workspaces: dict[tuple[int, int], Tensor] = {}
-
-
-def _workspace(device: torch.device, stream: int, floats: int) -> Tensor:
-    index = device.index if device.index is not None else torch.cuda.current_device()
-    ws = _workspaces.get((index, stream))
-    if ws is None or ws.numel() < floats:
-        ws = torch.zeros(floats, dtype=torch.float32, device=device)
-        _workspaces[(index, stream)] = ws
-    return ws
-
-
 def _dtype_code(t: Tensor, error_type: type[Exception]) -> int:
     code = DTYPE_CODES.get(t.dtype)
     if code is None:
@@ -193,7 +176,7 @@ def rms_norm_backward(dy: Tensor, x: Tensor, weight: Tensor, eps: float) -> tupl
         dy = dy.to(x.dtype)
     w = _rms_weight(x, weight)
     dx = torch.empty(x.shape, dtype=x.dtype, device=x.device)
-    dw = torch.empty(weight.shape, dtype=w.dtype, device=x.device)
+    dw = torch.empty(weight.shape, dtype=weight.dtype, device=x.device)
     xr = _as_rows(x, hidden)
     dyr = _as_rows(dy, hidden)
     dxr = dx.view(-1, hidden)
@@ -201,15 +184,17 @@ def rms_norm_backward(dy: Tensor, x: Tensor, weight: Tensor, eps: float) -> tupl
     x_code, w_code = DTYPE_CODES[x.dtype], DTYPE_CODES[w.dtype]
     with _OnDevice(x.device):
         stream = _stream(x.device)
-        floats = _capi.rmsnorm_bwd_fused_workspace(rows, hidden, x_code, w_code,
-                                                   TritonRMSNormUnavailable)
-        ws = _workspace(x.device, stream, floats)
-        _capi.rmsnorm_bwd_fused(
+        num_partials = _capi.rmsnorm_bwd_num_partials(rows, hidden, x_code, w_code,
+                                                      TritonRMSNormUnavailable)
+        partials = torch.empty((num_partials, hidden), dtype=torch.float32, device=x.device)
+        _capi.rmsnorm_bwd(
             dyr.data_ptr(), dyr.stride(0), xr.data_ptr(), xr.stride(0), w.data_ptr(), None,
-            dxr.data_ptr(), dxr.stride(0), dw.data_ptr(), ws.data_ptr(), ws.numel(), rows,
-            hidden, x_code, w_code, float(eps), stream, TritonRMSNormUnavailable,
+            dxr.data_ptr(), dxr.stride(0), partials.data_ptr(), num_partials, rows, hidden,
+            x_code, w_code, float(eps), stream, TritonRMSNormUnavailable,
         )
-    return dx, dw.to(weight.dtype)
+        _capi.rmsnorm_dw_reduce(partials.data_ptr(), num_partials, hidden, dw.data_ptr(),
+                                DTYPE_CODES[dw.dtype], stream, TritonRMSNormUnavailable)
+    return dx, dw
 
 
 @rms_norm_backward.register_fake
@@ -282,23 +267,25 @@ def add_rms_norm_backward(dy: Tensor, dh: Tensor | None, h: Tensor, weight: Tens
         dh = dh.to(h.dtype)
     w = _rms_weight(h, weight)
     dx = torch.empty(h.shape, dtype=h.dtype, device=h.device)
-    dw = torch.empty(weight.shape, dtype=w.dtype, device=h.device)
+    dw = torch.empty(weight.shape, dtype=weight.dtype, device=h.device)
     hr, dyr, dxr = _as_rows(h, hidden), _as_rows(dy, hidden), dx.view(-1, hidden)
     dhr = _as_rows(dh, hidden) if dh is not None else None
     rows = hr.size(0)
     x_code, w_code = DTYPE_CODES[h.dtype], DTYPE_CODES[w.dtype]
     with _OnDevice(h.device):
         stream = _stream(h.device)
-        floats = _capi.add_rmsnorm_bwd_fused_workspace(rows, hidden, x_code, w_code,
-                                                       TritonRMSNormUnavailable)
-        ws = _workspace(h.device, stream, floats)
-        _capi.add_rmsnorm_bwd_fused(
+        num_partials = _capi.add_rmsnorm_bwd_num_partials(rows, hidden, x_code, w_code,
+                                                          TritonRMSNormUnavailable)
+        partials = torch.empty((num_partials, hidden), dtype=torch.float32, device=h.device)
+        _capi.add_rmsnorm_bwd(
             dyr.data_ptr(), dyr.stride(0), dhr.data_ptr() if dhr is not None else None,
             dhr.stride(0) if dhr is not None else 0, hr.data_ptr(), hr.stride(0), w.data_ptr(),
-            None, dxr.data_ptr(), dxr.stride(0), dw.data_ptr(), ws.data_ptr(), ws.numel(),
-            rows, hidden, x_code, w_code, float(eps), stream, TritonRMSNormUnavailable,
+            None, dxr.data_ptr(), dxr.stride(0), partials.data_ptr(), num_partials, rows,
+            hidden, x_code, w_code, float(eps), stream, TritonRMSNormUnavailable,
         )
-    return dx, dw.to(weight.dtype)
+        _capi.rmsnorm_dw_reduce(partials.data_ptr(), num_partials, hidden, dw.data_ptr(),
+                                DTYPE_CODES[dw.dtype], stream, TritonRMSNormUnavailable)
+    return dx, dw
 
 
 @add_rms_norm_backward.register_fake
