@@ -138,16 +138,22 @@ def time_library_mlpup(work, stream: int, steps: int) -> float:
     return a.elapsed_time(b) / steps
 
 
-def dram_traffic_per_launch(kernel: str, tokens: int) -> float | None:
-    """Per-launch DRAM bytes of ``kernel`` from the committed ncu summary, scaled to
-    ``tokens`` rows (the traffic of these kernels grows in proportion to the rows)."""
+def traffic_per_launch(kernel: str, units: int) -> tuple[float | None, float | None]:
+    """(traffic bytes of one launch of ``kernel`` at ``units`` tokens (parameters for AdamW),
+    traffic / algorithmic bytes) from the committed ncu table profiles/traffic.json, where
+    traffic = DRAM reads + the bytes the SMs store into L2 of one captured launch. The
+    table's launch is scaled by units: every kernel's bytes grow in proportion, except the
+    gate/up GEMM's two weights, which are read once whatever the tokens."""
 
     path = ROOT / "profiles" / "traffic.json"
     try:
-        entry = json.loads(path.read_text())[kernel]
-        return float(entry["dram_bytes_per_launch"]) * tokens / float(entry["tokens"])
+        entry = json.loads(path.read_text())["kernels"][kernel]
+        t = float(entry["traffic_bytes_per_launch"])
+        scale = units / float(entry["params"] if "params" in entry else entry["tokens"])
+        fixed = 2 * INTER * HIDDEN * BF16 if kernel == "swiglu_gemm" else 0.0
+        return (t - fixed) * scale + fixed, float(entry["traffic_over_algorithmic"])
     except Exception:
-        return None
+        return None, None
 
 
 class ClockSampler:
@@ -465,6 +471,47 @@ class Stack:
         b.record()
         timer.setdefault(name, []).append((a, b))
 
+    def step_launches(self, stream: int) -> dict:
+        """The launches of one step grouped by kernel, in step order, each a callable that
+        returns the C ABI status (no collectives)."""
+
+        lib, L, T = self.lib, self.layers, self.tokens
+        f32, b16 = self.capi.PT_FLOAT32, self.capi.PT_BFLOAT16
+        y, act = self.y.data_ptr(), self.act.data_ptr()
+        part, P = self.partials.data_ptr(), self.num_partials
+        ws, ws_floats = self.workspace.data_ptr(), self.workspace.numel()
+        out: dict = {}
+
+        def add(name, fn):
+            out.setdefault(name, []).append(fn)
+
+        for l in range(L):
+            for k in range(2):
+                add("rmsnorm_fwd", lambda l=l, k=k: lib.pt_rmsnorm_fwd(
+                    self.x[l, k].data_ptr(), HIDDEN, self.w[l, k].data_ptr(), y, HIDDEN, None,
+                    T, HIDDEN, b16, f32, EPS, stream))
+            add("swiglu_fwd", lambda l=l: lib.pt_swiglu_fwd(
+                self.gate[l].data_ptr(), self.up[l].data_ptr(), act, T * INTER, b16, stream))
+        for l in reversed(range(L)):
+            add("swiglu_bwd", lambda l=l: lib.pt_swiglu_bwd(
+                self.dout[l].data_ptr(), self.gate[l].data_ptr(), self.up[l].data_ptr(),
+                self.dg.data_ptr(), self.du.data_ptr(), T * INTER, b16, stream))
+            for k in (1, 0):
+                if self.fused_dw:
+                    add("rmsnorm_bwd", lambda l=l, k=k: lib.pt_rmsnorm_bwd_fused(
+                        self.dy[l, k].data_ptr(), HIDDEN, self.x[l, k].data_ptr(), HIDDEN,
+                        self.w[l, k].data_ptr(), None, self.dx.data_ptr(), HIDDEN,
+                        self.bucket.slot(2 * l + k).data_ptr(), ws, ws_floats, T, HIDDEN, b16,
+                        f32, EPS, stream))
+                    continue
+                add("rmsnorm_bwd", lambda l=l, k=k: lib.pt_rmsnorm_bwd(
+                    self.dy[l, k].data_ptr(), HIDDEN, self.x[l, k].data_ptr(), HIDDEN,
+                    self.w[l, k].data_ptr(), None, self.dx.data_ptr(), HIDDEN, part, P, T,
+                    HIDDEN, b16, f32, EPS, stream))
+                add("rmsnorm_dw_reduce", lambda l=l, k=k: lib.pt_rmsnorm_dw_reduce(
+                    part, P, HIDDEN, self.bucket.slot(2 * l + k).data_ptr(), f32, stream))
+        return out
+
     def step(self, stream: int, world: int, swiglu_bwd_events: list | None = None,
              timer: dict | None = None) -> None:
         """One forward + backward of the stack. ``swiglu_bwd_events``: (start, end) event
@@ -524,7 +571,7 @@ class OpWorkload:
     measurement and for small ncu captures; the default workload is the stack."""
 
     def __init__(self, op: str, tokens: int, device: torch.device, seed: int,
-                 fused_dw: bool = False) -> None:
+                 fused_dw: bool = False, adamw_layers: int = 4) -> None:
         from picotron_b200 import _capi
 
         self.capi, self.lib, self.op, self.tokens, self.device = _capi, _capi.library(), op, tokens, device
@@ -602,7 +649,7 @@ class OpWorkload:
             # (q, k, v, o, gate, up, down projections and the two norm weights per layer:
             # 218 M parameters a layer), lr 3e-4, betas (0.9, 0.95), eps 1e-8, wd 0.1.
             shapes = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096),
-                      (14336, 4096), (4096, 14336), (4096,), (4096,)] * 4
+                      (14336, 4096), (4096, 14336), (4096,), (4096,)] * adamw_layers
             self.params = [torch.randn(s_, generator=gen, device=device) for s_ in shapes]
             self.grads = [torch.randn(s_, generator=gen, device=device) for s_ in shapes]
             self.m = [torch.zeros(s_, device=device) for s_ in shapes]
@@ -765,28 +812,35 @@ class OpWorkload:
 
 
 def per_kernel_block(stack: Stack, stream: int, world: int, steps: int, peak: float) -> dict:
-    """Mean CUDA-event duration of every kernel of the stack's step, from ``steps``
-    instrumented steps run after the timed region (events around every launch, which the
-    timed steps do not carry), max over ranks."""
+    """Mean duration of every kernel of the stack's step, after the timed region: for each
+    kernel, its launches of one step (over the stack's own inputs, in step order) run back
+    to back between one pair of CUDA events, ``steps`` times; max over ranks. One event pair
+    per kernel keeps event overhead out of the per-launch figure."""
 
-    timer: dict = {}
-    for _ in range(steps):
-        stack.step(stream, world, timer=timer)
-    torch.cuda.synchronize()
     out = {}
     total_us = 0.0
-    for name, pairs in timer.items():
-        us = statistics.fmean(a.elapsed_time(b) for a, b in pairs) * 1e3
+    for name, fns in stack.step_launches(stream).items():
+        for fn in fns[:2]:
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            for fn in fns:
+                stack._check(fn(), name)
+        b.record()
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1e3 / (steps * len(fns))
         us = max_over_ranks(us, world, stack.device)
-        per_step = len(pairs) // steps
         nbytes = stack.kernel_bytes[name]
         gbs = nbytes / (us * 1e-6) / 1e9
-        out[name] = {"launches_per_step": per_step, "mean_us": us, "bytes_per_launch": nbytes,
+        out[name] = {"launches_per_step": len(fns), "mean_us": us, "bytes_per_launch": nbytes,
                      "gbs": gbs, "frac_of_hbm_peak": gbs / peak}
-        total_us += us * per_step
+        total_us += us * len(fns)
     out["sum_us_per_step"] = total_us
-    out["how"] = (f"{steps} instrumented steps after the timed region, CUDA events around "
-                  "every launch, mean per kernel, max over ranks")
+    out["how"] = (f"after the timed region: each kernel's launches of one step, over the "
+                  f"stack's inputs, back to back between one event pair, {steps} times; mean "
+                  "per launch, max over ranks")
     return out
 
 
@@ -990,6 +1044,8 @@ def main() -> None:
     ap.add_argument("--rms-bwd", choices=["fused", "pair"], default="pair",
                     help="RMSNorm backward: dweight reduced by a second kernel (pair, the "
                          "faster on B200) or in the same cooperative launch (fused)")
+    ap.add_argument("--adamw-layers", type=int, default=4,
+                    help="adamw: Llama-3-8B decoder layers whose parameters are stepped")
     ap.add_argument("--no-extras", action="store_true",
                     help="stack: skip the config-4 RoPE block and the reference GPU path")
     ap.add_argument("--cpu-tokens", type=int, default=16384,
@@ -1019,7 +1075,8 @@ def main() -> None:
              "addnorm": "fused residual add + RMSNorm fwd+bwd bf16 h4096 (config 2 shapes)",
              "mlpup": "gate/up GEMMs + SwiGLU epilogue fwd bf16 4096->14336 (config 3/5 shapes)",
              "ce": "cross-entropy fwd+bwd bf16, vocab 128256 (Llama-3 head)",
-             "adamw": "AdamW step, fp32 params of 4 Llama-3-8B decoder layers (873 M)"}
+             "adamw": (f"AdamW step, fp32 params of {args.adamw_layers} Llama-3-8B decoder "
+                       f"layers ({218.2 * args.adamw_layers:.0f} M)")}
     config = {
         "workload": names[args.workload],
         "layers": args.layers,
@@ -1076,7 +1133,7 @@ def main() -> None:
                      fused_dw=args.rms_bwd == "fused")
     else:
         work = OpWorkload(args.workload, args.tokens, device, seed=1234 + rank,
-                          fused_dw=args.rms_bwd == "fused")
+                          fused_dw=args.rms_bwd == "fused", adamw_layers=args.adamw_layers)
     stream = torch.cuda.current_stream(device).cuda_stream
     torch.cuda.synchronize()
 
@@ -1112,7 +1169,8 @@ def main() -> None:
     bytes_step = work.bytes_per_step()
     dom_name, dom_bytes = work.dominant
     achieved = dom_bytes / (dom_ms / 1e3) / 1e9
-    traffic = dram_traffic_per_launch(work.traffic_key, work.tokens)
+    traffic, traffic_ratio = traffic_per_launch(
+        work.traffic_key, work.nparams if args.workload == "adamw" else work.tokens)
     tensor_bound = args.workload == "mlpup"
     library_ms = None
     library_what = None
@@ -1176,6 +1234,8 @@ def main() -> None:
                 "unit": "GB/s",
                 "frac": achieved / peak,
                 "traffic": traffic,
+                "traffic_over_algorithmic": traffic_ratio,
+                "traffic_source": "profiles/traffic.json: ncu DRAM reads + SM-issued L2 writes",
                 "algorithmic_bytes_per_launch": dom_bytes,
                 "mean_launch_us": dom_ms * 1e3,
             } if not tensor_bound else {
@@ -1187,6 +1247,8 @@ def main() -> None:
                 "unit": "TFLOP/s",
                 "frac": achieved / tpeak,
                 "traffic": traffic,
+                "traffic_over_algorithmic": traffic_ratio,
+                "traffic_source": "profiles/traffic.json: ncu DRAM reads + SM-issued L2 writes",
                 "algorithmic_flops_per_launch": dom_bytes,
                 "mean_launch_us": dom_ms * 1e3,
             },
