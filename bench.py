@@ -43,9 +43,51 @@ import sys
 import time
 from pathlib import Path
 
+# Under torchrun NCCL logs its INIT lines (communicator size, rank, channels, NVLS) into a
+# per-process file, which each rank copies to stderr once its communicator exists; set
+# before torch loads NCCL, since NCCL reads these once.
+if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+    os.environ.setdefault("NCCL_DEBUG", "INFO")
+    os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+    os.environ.setdefault("NCCL_DEBUG_FILE", f"/tmp/pt_nccl_{os.getpid()}.log")
+
 import torch
 
 ROOT = Path(__file__).resolve().parent
+
+# The contract is one JSON line on stdout from rank 0. Libraries may print to stdout (NCCL's
+# version banner does), so file descriptor 1 points at stderr for the whole run and the
+# result line goes to the real stdout, kept here.
+_RESULT_OUT = None
+
+
+def _claim_stdout() -> None:
+    global _RESULT_OUT
+    if _RESULT_OUT is None:
+        sys.stdout.flush()
+        _RESULT_OUT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
+
+
+def emit(line: dict) -> None:
+    """Writes the result line to the real stdout."""
+
+    out = _RESULT_OUT if _RESULT_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
+def copy_nccl_log_to_stderr(rank: int) -> None:
+    path = os.environ.get("NCCL_DEBUG_FILE", "")
+    if not path.startswith("/tmp/pt_nccl_"):
+        return
+    try:
+        text = Path(path).read_text()
+        Path(path).unlink()
+    except OSError:
+        return
+    for line in text.splitlines():
+        print(f"[rank {rank}] {line}", file=sys.stderr)
 METRIC = "RMSNorm+SwiGLU fwd+bwd tokens/s & HBM GB/s (bf16, h4096/i14336) at 1–8 B200"
 HIDDEN, INTER = 4096, 14336
 EPS = 1e-5
@@ -175,6 +217,13 @@ class ClockSampler:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+            # The first sample can take a second or more on an 8-GPU host: let it land
+            # before the timed region starts (at most 5 s).
+            deadline = time.monotonic() + 5.0
+            while time.monotonic() < deadline and self.proc.poll() is None:
+                if Path(self.out_path).stat().st_size > 0:
+                    break
+                time.sleep(0.05)
         except Exception:
             self.proc = None
         return self
@@ -229,15 +278,11 @@ def init_distributed(gpus: int):
     if world > 1:
         import torch.distributed as dist
 
-        # NCCL's INIT log (communicator size, rank, channels, NVLS) goes to stderr so the
-        # rank count can be checked, while rank 0 prints exactly one line on stdout (NCCL
-        # writes to stdout unless NCCL_DEBUG_FILE says otherwise).
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
+        dist.barrier()  # the communicator exists (and has logged its INIT lines) after this
+        copy_nccl_log_to_stderr(rank)
     return world, rank, local
 
 
@@ -436,6 +481,9 @@ class Stack:
         # from the last layer down, so each bucket's all-reduce overlaps the backward of the
         # layers below it; only layer 0's small one is left at the end of the step.
         self.bucket_starts = sorted({0, 1} | set(range(0, layers, 8)) - {layers})
+        # When a list, each step appends the (start, end) events around its final waits for
+        # the all-reduces: the collective time the backward did not hide.
+        self.wait_events: list | None = None
         self.events_per_step = layers  # one (start, end) pair per SwiGLU backward launch
         self.dominant = ("swiglu_bwd_vec (SwiGLU backward)", 5 * tokens * INTER * BF16)
         self.traffic_key = "swiglu_bwd"
@@ -561,8 +609,14 @@ class Stack:
                 i = starts.index(l)
                 stop = starts[i + 1] if i + 1 < len(starts) else L
                 pending.append(self.bucket.all_reduce_async(2 * l, 2 * stop))
+        if self.wait_events is not None:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
         for p in pending:
             p.wait()
+        if self.wait_events is not None:
+            b.record()
+            self.wait_events.append((a, b))
 
 
 class OpWorkload:
@@ -1060,6 +1114,7 @@ def main() -> None:
                          "ce = cross-entropy forward + backward over a 128256 vocabulary; "
                          "adamw = one fused AdamW step over 4 Llama-3-8B layers of parameters")
     args = ap.parse_args()
+    _claim_stdout()
     if args.workload != "stack":
         args.no_e2e = True
         args.no_cpu_baseline = True
@@ -1115,7 +1170,7 @@ def main() -> None:
             "e2e": {"value": ref["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
         return
 
     world, rank, local = init_distributed(args.gpus)
@@ -1150,6 +1205,8 @@ def main() -> None:
             uuids.append(str(torch.cuda.get_device_properties(i).uuid))
         except Exception:
             pass
+    if args.workload == "stack" and world > 1:
+        work.wait_events = []
     barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(uuids if rank == 0 else []) as clocks:
@@ -1162,6 +1219,11 @@ def main() -> None:
         barrier(world)
     elapsed = start.elapsed_time(end)
     ms = max_over_ranks(elapsed, world, device) / args.steps
+    exposed_us = None
+    if getattr(work, "wait_events", None):
+        exposed_us = max_over_ranks(
+            statistics.fmean(a.elapsed_time(b) for a, b in work.wait_events) * 1e3, world, device)
+        work.wait_events = None
     dom_ms = statistics.fmean(a.elapsed_time(b) for a, b in ev)
     dom_ms = max_over_ranks(dom_ms, world, device)
 
@@ -1259,13 +1321,21 @@ def main() -> None:
                 "unit": getattr(work, "unit", "tokens/s"),
             },
             "per_kernel": per_kernel,
+            "dweight_allreduce": None if args.workload != "stack" or world == 1 else {
+                "buckets_per_step": len(work.bucket_starts),
+                "last_bucket": "layer 0 (2 norms, 32 KB)",
+                "exposed_us_per_step": exposed_us,
+                "how": "CUDA events around the step's final waits for its all-reduces (the "
+                       "time the compute stream waits for NCCL after its last kernel), mean "
+                       "over the timed steps, max over ranks",
+            },
             "rope_cfg4": rope_cfg4,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": work.launches_per_step * args.steps,
             "clocks": clocks.summary() if rank == 0 else None,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
 
     if world > 1:
         import torch.distributed as dist
