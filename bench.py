@@ -47,9 +47,10 @@ from pathlib import Path
 # per-process file, which each rank copies to stderr once its communicator exists; set
 # before torch loads NCCL, since NCCL reads these once.
 if int(os.environ.get("WORLD_SIZE", "1")) > 1:
-    os.environ.setdefault("NCCL_DEBUG", "INFO")
+    if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION", "WARN"):
+        os.environ["NCCL_DEBUG"] = "INFO"
     os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
-    os.environ.setdefault("NCCL_DEBUG_FILE", f"/tmp/pt_nccl_{os.getpid()}.log")
+    os.environ["NCCL_DEBUG_FILE"] = f"/tmp/pt_nccl_{os.getpid()}.log"
 
 import torch
 
@@ -228,6 +229,14 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def mark(self) -> None:
+        """Only samples taken after this call count (the timed region starts here)."""
+
+        try:
+            self.skip = len(Path(self.out_path).read_text().splitlines())
+        except (OSError, TypeError):
+            self.skip = 0
+
     def __exit__(self, *exc):
         if self.proc is not None:
             self.proc.terminate()
@@ -242,7 +251,7 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         sm, sm_max, reasons, power = [], [], set(), []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in Path(self.out_path).read_text().splitlines():
+        for line in Path(self.out_path).read_text().splitlines()[getattr(self, "skip", 0):]:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -269,7 +278,7 @@ class ClockSampler:
                 "reasons": sorted(reasons)}
 
 
-def init_distributed(gpus: int):
+def init_distributed(gpus: int, high_priority_nccl: bool = True):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -278,9 +287,12 @@ def init_distributed(gpus: int):
     if world > 1:
         import torch.distributed as dist
 
+        from picotron_b200.dist import nccl_options
+
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device("cuda", local))
+                                device_id=torch.device("cuda", local),
+                                pg_options=nccl_options() if high_priority_nccl else None)
         dist.barrier()  # the communicator exists (and has logged its INIT lines) after this
         copy_nccl_log_to_stderr(rank)
     return world, rank, local
@@ -1098,6 +1110,8 @@ def main() -> None:
     ap.add_argument("--rms-bwd", choices=["fused", "pair"], default="pair",
                     help="RMSNorm backward: dweight reduced by a second kernel (pair, the "
                          "faster on B200) or in the same cooperative launch (fused)")
+    ap.add_argument("--nccl-stream", choices=["high", "normal"], default="high",
+                    help="priority of the NCCL stream that runs the dweight all-reduces")
     ap.add_argument("--adamw-layers", type=int, default=4,
                     help="adamw: Llama-3-8B decoder layers whose parameters are stepped")
     ap.add_argument("--no-extras", action="store_true",
@@ -1143,6 +1157,7 @@ def main() -> None:
         "parallelism": f"dp{args.gpus}",
         "eps": EPS,
         "weight_dtype": "float32",
+        "nccl_stream": f"{args.nccl_stream} priority",
         "rmsnorm_backward": ("dweight reduced in the same launch" if args.rms_bwd == "fused"
                              else "dweight reduced by a second kernel"),
         "l2": "no flush: every layer has its own inputs, each larger than the 126 MB L2",
@@ -1173,7 +1188,7 @@ def main() -> None:
         emit(line)
         return
 
-    world, rank, local = init_distributed(args.gpus)
+    world, rank, local = init_distributed(args.gpus, args.nccl_stream == "high")
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     import picotron_b200  # noqa: F401  (loads the library; fails loudly if it is missing)
@@ -1210,6 +1225,7 @@ def main() -> None:
     barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(uuids if rank == 0 else []) as clocks:
+        clocks.mark()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
         for s in range(args.steps):

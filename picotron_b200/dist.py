@@ -21,6 +21,17 @@ import torch.distributed as dist
 from torch import Tensor
 
 
+def nccl_options():
+    """Options for a NCCL process group whose collectives overlap the hot-path kernels: its
+    stream has high priority. Every kernel of the backward fills the GPU (persistent grids
+    sized to the SMs), so on a normal-priority stream NCCL's all-reduce kernels wait for free
+    SMs behind the compute stream's queued kernels and run only after the backward's last
+    kernel; with high priority their CTAs are dispatched first as SMs free up.
+    Pass as ``dist.init_process_group("nccl", pg_options=nccl_options(), ...)``."""
+
+    return dist.ProcessGroupNCCL.Options(is_high_priority_stream=True)
+
+
 class PendingAllReduce:
     """An all-reduce issued by ``DWeightBucket.all_reduce_async``; ``wait`` completes it.
 
