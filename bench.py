@@ -132,6 +132,37 @@ def time_library_adamw(work, steps: int) -> float:
     return ms
 
 
+def time_library_mlpact(work, stream: int, steps: int) -> float:
+    """ms per step of the unfused path the two fused GEMMs replace: cuBLAS (torch.matmul) for
+    gate, up and d_act = dy @ w_down, and this library's SwiGLU forward and backward kernels."""
+
+    c = work.capi
+    n = work.tokens * INTER
+    d_act = torch.empty_like(work.act)
+
+    def step(i: int) -> None:
+        x, dy = work.x[i % 2], work.dy[i % 2]
+        torch.matmul(x, work.wg.t(), out=work.g)
+        torch.matmul(x, work.wu.t(), out=work.u)
+        c.swiglu_fwd(work.g.data_ptr(), work.u.data_ptr(), work.act.data_ptr(), n,
+                     c.PT_BFLOAT16, stream)
+        torch.matmul(dy, work.wd, out=d_act)
+        c.swiglu_bwd(d_act.data_ptr(), work.g.data_ptr(), work.u.data_ptr(), work.dg.data_ptr(),
+                     work.du.data_ptr(), n, c.PT_BFLOAT16, stream)
+
+    for i in range(3):
+        step(i)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(steps):
+        step(i)
+    b.record()
+    torch.cuda.synchronize()
+    del d_act
+    return a.elapsed_time(b) / steps
+
+
 def time_library_ce(work, steps: int) -> float:
     """ms per step of PyTorch's own cross-entropy forward + backward on the same logits."""
 
@@ -696,6 +727,31 @@ class OpWorkload:
             self.bytes = (tokens * k + 2 * INTER * k + 3 * tokens * INTER) * BF16
             self.launches_per_step = 1
             self.dominant = ("swiglu_gemm_kernel", self.flops)
+        elif op == "mlpact":
+            # The MLP's activation in training, both directions on the tensor cores: the gate/up
+            # GEMMs with the SwiGLU epilogue (act, gate, up written), then the down
+            # projection's input gradient d_act = dy @ w_down with the SwiGLU backward in its
+            # epilogue (dgate, dup written), w_down transposed once per step for it.
+            k = HIDDEN
+            self.x = [torch.randn((tokens, k), generator=gen, device=device, dtype=bf)
+                      for _ in range(2)]
+            self.dy = [torch.randn((tokens, k), generator=gen, device=device, dtype=bf)
+                       for _ in range(2)]
+            self.wg = torch.randn((INTER, k), generator=gen, device=device, dtype=bf) * 2 * k ** -0.5
+            self.wu = torch.randn((INTER, k), generator=gen, device=device, dtype=bf) * 2 * k ** -0.5
+            self.wd = torch.randn((k, INTER), generator=gen, device=device, dtype=bf) * 2 * INTER ** -0.5
+            self.wdt = torch.empty((INTER, k), device=device, dtype=bf)
+            self.act = torch.empty((tokens, INTER), device=device, dtype=bf)
+            self.g, self.u = torch.empty_like(self.act), torch.empty_like(self.act)
+            self.dg, self.du = torch.empty_like(self.act), torch.empty_like(self.act)
+            self.flops = 2 * 2 * tokens * INTER * k + 2 * tokens * INTER * k
+            # fwd: x, w_gate, w_up in, act, gate, up out; w_down transposed (in + out); bwd:
+            # dy, w_down^T, gate, up in, dgate, dup out.
+            self.bytes = ((tokens * k + 2 * INTER * k + 3 * tokens * INTER) + 2 * INTER * k
+                          + (tokens * k + INTER * k + 4 * tokens * INTER)) * BF16
+            self.launches_per_step = 2
+            self.dominant = ("swiglu_gemm_bwd_pair_kernel (d_act GEMM + SwiGLU backward)",
+                             2 * tokens * INTER * k)
         elif op == "ce":
             # Cross-entropy forward + backward over a Llama-3 vocabulary (the next-step row):
             # logits [tokens, 128256] bf16 ~ N(0, 2^2), uniform targets.
@@ -766,6 +822,7 @@ class OpWorkload:
             self.units, self.unit = self.tokens, "tokens/s"
         self.traffic_key = {"rmsnorm": "rmsnorm_bwd", "swiglu": "swiglu_bwd", "rope": "rope_fwd",
                             "addnorm": "add_rmsnorm_bwd", "mlpup": "swiglu_gemm",
+                            "mlpact": "swiglu_gemm_bwd",
                             "ce": "ce_bwd", "adamw": "adamw"}[op]
 
     def bytes_per_step(self) -> int:
@@ -827,6 +884,17 @@ class OpWorkload:
             c.swiglu_gemm_fwd(x.data_ptr(), HIDDEN, self.wg.data_ptr(), self.wu.data_ptr(), HIDDEN,
                               self.act.data_ptr(), INTER, self.g.data_ptr(), self.u.data_ptr(),
                               INTER, T, INTER, HIDDEN, c.PT_BFLOAT16, stream)
+            if ev: ev[1].record()
+        elif self.op == "mlpact":
+            x, dy = self.x[i % 2], self.dy[i % 2]
+            c.swiglu_gemm_fwd(x.data_ptr(), HIDDEN, self.wg.data_ptr(), self.wu.data_ptr(), HIDDEN,
+                              self.act.data_ptr(), INTER, self.g.data_ptr(), self.u.data_ptr(),
+                              INTER, T, INTER, HIDDEN, c.PT_BFLOAT16, stream)
+            self.wdt.copy_(self.wd.t())
+            if ev: ev[0].record()
+            c.swiglu_gemm_bwd(dy.data_ptr(), HIDDEN, self.wdt.data_ptr(), HIDDEN, self.g.data_ptr(),
+                              self.u.data_ptr(), INTER, self.dg.data_ptr(), self.du.data_ptr(),
+                              INTER, None, 0, T, INTER, HIDDEN, c.PT_BFLOAT16, stream)
             if ev: ev[1].record()
         elif self.op == "ce":
             lg = self.logits[i % 2]
@@ -1119,7 +1187,7 @@ def main() -> None:
     ap.add_argument("--cpu-tokens", type=int, default=16384,
                     help="tokens of the one layer the CPU reference path times")
     ap.add_argument("--workload", choices=["stack", "rmsnorm", "swiglu", "rope", "rope_rh", "addnorm", "mlpup",
-                                           "ce", "adamw"],
+                                           "mlpact", "ce", "adamw"],
                     default="stack",
                     help="stack = BASELINE config 5 (the headline); rmsnorm, swiglu, rope are "
                          "configs 2, 3 and 4, one op forward+backward per step, for per-kernel "
@@ -1143,6 +1211,8 @@ def main() -> None:
              "rope_rh": "RoPE q+k fwd+bwd bf16 (BASELINE config 4), rotate-half pairs",
              "addnorm": "fused residual add + RMSNorm fwd+bwd bf16 h4096 (config 2 shapes)",
              "mlpup": "gate/up GEMMs + SwiGLU epilogue fwd bf16 4096->14336 (config 3/5 shapes)",
+             "mlpact": ("MLP activation fwd+bwd on the tensor cores bf16 (config 3/5 shapes): "
+                        "gate/up GEMMs + SwiGLU epilogue, d_act GEMM + SwiGLU backward epilogue"),
              "ce": "cross-entropy fwd+bwd bf16, vocab 128256 (Llama-3 head)",
              "adamw": (f"AdamW step, fp32 params of {args.adamw_layers} Llama-3-8B decoder "
                        f"layers ({218.2 * args.adamw_layers:.0f} M)")}
@@ -1249,7 +1319,7 @@ def main() -> None:
     achieved = dom_bytes / (dom_ms / 1e3) / 1e9
     traffic, traffic_ratio = traffic_per_launch(
         work.traffic_key, work.nparams if args.workload == "adamw" else work.tokens)
-    tensor_bound = args.workload == "mlpup"
+    tensor_bound = args.workload in ("mlpup", "mlpact")
     library_ms = None
     library_what = None
     if args.workload == "adamw":
@@ -1264,8 +1334,13 @@ def main() -> None:
         # A tensor-core contraction: FLOPs per launch over the cuBLAS bf16 burst peak.
         achieved = dom_bytes / (dom_ms / 1e3) / 1e12
         tpeak, tpeak_kind = measured_peaks("bf16_tflops")
-        library_ms = time_library_mlpup(work, stream, args.steps)
-        library_what = "cuBLAS gate and up GEMMs (torch.matmul) + this library's SwiGLU kernel"
+        if args.workload == "mlpup":
+            library_ms = time_library_mlpup(work, stream, args.steps)
+            library_what = "cuBLAS gate and up GEMMs (torch.matmul) + this library's SwiGLU kernel"
+        else:
+            library_ms = time_library_mlpact(work, stream, args.steps)
+            library_what = ("cuBLAS gate, up and d_act GEMMs (torch.matmul) + this library's "
+                            "SwiGLU forward and backward kernels")
 
     per_kernel = rope_cfg4 = reference_gpu = None
     if args.workload == "stack":

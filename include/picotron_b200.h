@@ -309,6 +309,27 @@ PT_API int pt_swiglu_gemm_fwd(const void* x, int64_t x_row_stride,
                               int64_t m, int64_t n, int64_t k, int dtype,
                               void* stream);
 
+/* The training backward of the MLP's activation, fused into the GEMM that produces its input
+ * gradient: d_act = dy @ w_down (dy [m, k] the down projection's output gradient, w_down the
+ * nn.Linear weight [k, n]) on the tensor cores, and in the epilogue, from gate and up [m, n]
+ * as the forward saved them:
+ *   dgate = (d_act * up) * (s * (1 + gate * (1 - s))),  dup = d_act * (gate * s),
+ *   s = sigmoid(gate), fp32 math on d_act rounded to the dtype, results in the dtype.
+ * d_act is stored too when dact_out is not NULL. w_down_t is w_down transposed, [n, k]
+ * row-major (both GEMM operands are then read along k). Replaces the autograd of
+ * down_projection plus _SwiGLUAutogradFunction.backward (src/picotron/nn/feedforward.py:
+ * 27-43, src/picotron/nn/triton_kernels/swiglu.py:71-81): d_act never goes through HBM and
+ * the activation backward needs no launch of its own. n (the intermediate size) a multiple of
+ * 64, k a multiple of 8, 16-byte aligned pointers and row strides of 8 elements; outputs
+ * alias no input. bf16 or fp16. */
+PT_API int pt_swiglu_gemm_bwd(const void* dy, int64_t dy_row_stride,
+                              const void* w_down_t, int64_t w_row_stride,
+                              const void* gate, const void* up, int64_t pre_row_stride,
+                              void* dgate, void* dup, int64_t grad_row_stride,
+                              void* dact_out, int64_t dact_row_stride,
+                              int64_t m, int64_t n, int64_t k, int dtype,
+                              void* stream);
+
 /* ---------------------------------------------------------- cross-entropy ------- */
 
 /* Mean cross-entropy over rows of `vocab` logits (class stride 1). Rows form an

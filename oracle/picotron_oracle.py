@@ -141,6 +141,23 @@ def gate_up_forward(x: Tensor, w_gate: Tensor, w_up: Tensor, mode: str = "eager"
     return g, u, swiglu_forward(g, u, "eager")
 
 
+def down_swiglu_backward(dy: Tensor, w_down: Tensor, gate: Tensor, up: Tensor,
+                         mode: str = "eager"):
+    """Returns (d_act, dgate, dup): the gradient that reaches the activation through
+    SwiGLU.down_projection (src/picotron/nn/feedforward.py:43, an nn.Linear without bias, so
+    d_act = dy @ w_down), then the activation's backward (swiglu_backward below).
+    eager: the matmul in the input dtype (what autograd of F.linear computes) and the
+    reference's backward op for op. exact: d_act in float64, then the float64 backward."""
+
+    _check_mode(mode)
+    if mode == "exact":
+        d_act = dy.double() @ w_down.double()
+    else:
+        d_act = dy @ w_down
+    dgate, dup = swiglu_backward(gate, up, d_act, mode)
+    return d_act, dgate, dup
+
+
 def swiglu_backward(gate: Tensor, up: Tensor, dout: Tensor, mode: str = "eager"):
     """Returns (dgate, dup).
 

@@ -78,6 +78,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pt_swiglu_gemm_fwd": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64, _c_ptr, _c_i64,
                                     _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_int,
                                     _c_ptr]),
+    "pt_swiglu_gemm_bwd": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64,
+                                    _c_ptr, _c_ptr, _c_i64, _c_ptr, _c_i64, _c_i64, _c_i64,
+                                    _c_i64, _c_int, _c_ptr]),
     "pt_cross_entropy_fwd": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_ptr,
                                       _c_i64, _c_i64, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_int,
                                       _c_ptr]),
@@ -351,6 +354,19 @@ def swiglu_gemm_fwd(x: int, x_row_stride: int, w_gate: int, w_up: int, w_row_str
                                           act_row_stride, gate_out, up_out, pre_row_stride, m,
                                           n, k, dtype, stream)
     _check("pt_swiglu_gemm_fwd", status, error_type)
+
+
+def swiglu_gemm_bwd(dy: int, dy_row_stride: int, w_down_t: int, w_row_stride: int, gate: int,
+                    up: int, pre_row_stride: int, dgate: int, dup: int, grad_row_stride: int,
+                    dact_out: int | None, dact_row_stride: int, m: int, n: int, k: int,
+                    dtype: int, stream: int, error_type: type[Exception] | None = None) -> None:
+    """The down projection's input gradient with the SwiGLU backward in its epilogue
+    (pt_swiglu_gemm_bwd)."""
+
+    status = library().pt_swiglu_gemm_bwd(dy, dy_row_stride, w_down_t, w_row_stride, gate, up,
+                                          pre_row_stride, dgate, dup, grad_row_stride, dact_out,
+                                          dact_row_stride, m, n, k, dtype, stream)
+    _check("pt_swiglu_gemm_bwd", status, error_type)
 
 
 def cross_entropy_fwd(logits: int, vocab: int, outer: int, inner: int, logits_strides,

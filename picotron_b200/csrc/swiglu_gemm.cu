@@ -60,7 +60,12 @@ constexpr long long kWaitCycles = 2000000000LL;  // about one second of SM clock
 constexpr int kEpiCols = 32;
 constexpr int kStageOut = 32 * kEpiCols * 2;               // one 32 x 32 16-bit tile: 2 KB
 constexpr int kEpiBufs = 2;  // double-buffered: a chunk is staged while the last one is stored
-constexpr int kStagingBytes = kEpiWarps * kEpiBufs * 3 * kStageOut;  // per warp: (act, gate, up)
+// Staged 32 x 32 tiles per warp and buffer: forward (act, gate, up); backward (gate and up
+// loaded, dgate, dup and optionally d_act stored).
+template <bool kBwd> constexpr int staged_tiles() { return kBwd ? 5 : 3; }
+template <bool kBwd> constexpr int staging_bytes() {
+  return kEpiWarps * kEpiBufs * staged_tiles<kBwd>() * kStageOut;
+}
 
 // Two shapes of the same pipeline:
 //  * single CTA (kPair = false): a 128 x 128 tile per CTA; each stage holds the x tile and
@@ -74,16 +79,22 @@ constexpr int kStagingBytes = kEpiWarps * kEpiBufs * 3 * kStageOut;  // per warp
 #ifndef PT_GEMM_PAIR_STAGES
 #define PT_GEMM_PAIR_STAGES 5
 #endif
-template <bool kPair> struct Shape {
-  static constexpr int kStages = kPair ? PT_GEMM_PAIR_STAGES : 3;
+// kBwd (the down projection's data gradient with the SwiGLU backward in the epilogue) uses
+// the same stages, 4 for CTA pairs to make room for its larger epilogue staging.
+template <bool kPair, bool kBwd = false> struct Shape {
+  static constexpr int kStages = kPair ? (kBwd ? 4 : PT_GEMM_PAIR_STAGES) : 3;
   static constexpr int kStageBytes = kATileBytes + (kPair ? 1 : 2) * kWTileBytes;
   static constexpr int kTileM = kPair ? 2 * kBM : kBM;
   static constexpr int kCtas = kPair ? 2 : 1;
+  static constexpr int kStagingBytes = staging_bytes<kBwd>();
   static constexpr int kSmemBytes =
       1024 /* alignment slack */ + kStages * kStageBytes + kStagingBytes + 256;
 };
-static_assert(Shape<false>::kStages <= kMaxStages && Shape<true>::kStages <= kMaxStages, "");
-static_assert(Shape<false>::kSmemBytes <= 227 * 1024 && Shape<true>::kSmemBytes <= 227 * 1024,
+static_assert(Shape<false>::kStages <= kMaxStages && Shape<true>::kStages <= kMaxStages &&
+                  Shape<true, true>::kStages <= kMaxStages, "");
+static_assert(Shape<false>::kSmemBytes <= 227 * 1024 && Shape<true>::kSmemBytes <= 227 * 1024 &&
+                  Shape<false, true>::kSmemBytes <= 227 * 1024 &&
+                  Shape<true, true>::kSmemBytes <= 227 * 1024,
               "stage ring + epilogue staging must fit the 227 KB of shared memory per CTA");
 
 struct GemmBarriers {
@@ -92,6 +103,7 @@ struct GemmBarriers {
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
   uint64_t drain;
+  uint64_t epi_full[kEpiWarps][kEpiBufs];  // backward: the epilogue's gate/up tiles landed
   uint32_t tmem_base;
 };
 static_assert(sizeof(GemmBarriers) <= 256, "barrier block must fit its reserved space");
@@ -353,21 +365,167 @@ struct TileGrid {
   }
 };
 
+// Epilogue of the backward GEMM (kBwd): per tile, each epilogue warp owns 32 rows (tensor
+// memory lanes [32q, 32q + 32)) and walks 8 chunks of 32 columns, 4 in each accumulator half
+// (columns c of d_act, then n_half + c). Per chunk, lane 0 loads the gate and up 32 x 32
+// tiles with TMA (64-byte swizzle, the next chunk's while this one computes), the warp reads
+// its 32 d_act values from tensor memory, rounds them to T (the d_act a separate GEMM would
+// store), forms dgate = (d_act * up) * (s * (1 + gate * (1 - s))) and dup = d_act * (gate * s)
+// with s = sigmoid(gate) in fp32 (the operation order of swiglu_bwd_vec), stages them and
+// stores them with TMA. Chunks past n_half (a last tile column narrower than 128) are
+// skipped. Every wait is bounded; after a timeout the warp stops, records the error word and
+// waits (bounded) for its own loads in flight.
 template <typename T, bool kPair>
+__device__ __forceinline__ void bwd_epilogue(GemmBarriers* bars, unsigned char* staging,
+                                             uint32_t tmem_base, const TileGrid& grid, int unit,
+                                             int units, uint32_t rank,
+                                             const CUtensorMap* map_da, const CUtensorMap* map_dg,
+                                             const CUtensorMap* map_du,
+                                             const CUtensorMap* map_gin,
+                                             const CUtensorMap* map_uin, int save_da,
+                                             int n_half) {
+  using S = Shape<kPair, true>;
+  constexpr int kTiles = staged_tiles<true>();  // gate, up in; dgate, dup, d_act out
+  constexpr int kChunks = 2 * kBN / kEpiCols;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q = warp & 3, wi = warp - kEpiWarp0;
+  const uint32_t empty_addr0 = kPair ? peer_addr(&bars->tmem_empty[0], 0)
+                                     : smem_addr(&bars->tmem_empty[0]);
+  const uint64_t policy = evict_first_policy();
+  unsigned char* st0 = staging + (size_t)wi * kEpiBufs * kTiles * kStageOut;
+  uint32_t g = 0;              // chunks this warp has loaded: buffer g & 1, phase (g >> 1) & 1
+  // Loads not yet waited for: bit bb of pending_mask, with their chunk numbers.
+  uint32_t pending_mask = 0, pending_gc0 = 0, pending_gc1 = 0;
+  bool ok = true;
+  int i = 0;
+  auto issue = [&](uint32_t gc, int row, int col) {
+    const int bb = gc & 1;
+    unsigned char* st = st0 + bb * kTiles * kStageOut;
+    uint64_t* bar = &bars->epi_full[wi][bb];
+    if (lane == 0) {
+      mbar_arrive_expect_tx(bar, 2 * kStageOut);
+      tma_load_2d<false>(smem_addr(st), map_gin, col, row, smem_addr(bar));
+      tma_load_2d<false>(smem_addr(st + kStageOut), map_uin, col, row, smem_addr(bar));
+    }
+    pending_mask |= 1u << bb;
+    if (bb) pending_gc1 = gc; else pending_gc0 = gc;
+  };
+  for (int t = unit; ok && t < grid.count(); t += units, ++i) {
+    const int b = i & 1;
+    int mb, nb;
+    grid.coords(t, mb, nb);
+    const int row0 = mb * S::kTileM + (int)rank * kBM + q * 32;  // this warp's rows
+    // Live chunks: the first `per_half` of each half (all 4 unless the tile column is the
+    // last, narrower one); live chunk li is chunk j = li of the first half or 4 + (li -
+    // per_half) of the second.
+    const int per_half = min(kChunks / 2, (n_half - nb * kBN) / kEpiCols);
+    const int nl = 2 * per_half;
+    auto chunk_of = [&](int li) { return li < per_half ? li : kChunks / 2 + (li - per_half); };
+    auto col_of = [&](int j) { return (j >> 2) * n_half + nb * kBN + (j & 3) * kEpiCols; };
+    if (nl > 0) issue(g, row0, col_of(chunk_of(0)));
+    if (!wait_bounded(&bars->tmem_full[b], (i >> 1) & 1)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    const uint32_t tg = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * kAccCols);
+#pragma unroll 1
+    for (int li = 0; li < nl; ++li) {
+      const int j = chunk_of(li);
+      const uint32_t gc = g + li;
+      const int bb = gc & 1;
+      // The other buffer was last read by the previous chunk (fenced below): refill it.
+      if (li + 1 < nl) issue(gc + 1, row0, col_of(chunk_of(li + 1)));
+      if (!wait_bounded(&bars->epi_full[wi][bb], (gc >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      pending_mask &= ~(1u << bb);
+      unsigned char* st = st0 + bb * kTiles * kStageOut;
+      uint32_t ar[32];
+      tmem_ld32(tg + (j >> 2) * kBN + (j & 3) * kEpiCols, ar);
+      tmem_wait_ld();
+      reg_fence32(ar);
+      // The TMA stores that last used this buffer's output tiles must have read them.
+      if (lane == 0) bulk_wait_read<kEpiBufs - 1>();
+      __syncwarp();
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {  // 16-byte chunk v of this thread's row
+        const uint32_t off = swz64(lane, v);
+        float g8[8], u8[8], dg8[8], du8[8], da8[8];
+        unpack<T>(lds128(st + off), g8);
+        unpack<T>(lds128(st + kStageOut + off), u8);
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          const float2 a2 = round2<T>(make_float2(__uint_as_float(ar[v * 8 + e]),
+                                                  __uint_as_float(ar[v * 8 + e + 1])));
+          da8[e] = a2.x;
+          da8[e + 1] = a2.y;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float sg = sigmoid_f32(g8[e]);
+          dg8[e] = (da8[e] * u8[e]) * (sg * (1.0f + g8[e] * (1.0f - sg)));
+          du8[e] = da8[e] * (g8[e] * sg);
+        }
+        *reinterpret_cast<uint4*>(st + 2 * kStageOut + off) = pack<T>(dg8);
+        *reinterpret_cast<uint4*>(st + 3 * kStageOut + off) = pack<T>(du8);
+        if (save_da) *reinterpret_cast<uint4*>(st + 4 * kStageOut + off) = pack<T>(da8);
+      }
+      // Orders this chunk's shared-memory reads (before the buffer is refilled by TMA) and
+      // writes (before the TMA stores read them) with the async proxy.
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int col = col_of(j);
+        const uint32_t sa = smem_addr(st);
+        tma_store_2d(map_dg, sa + 2 * kStageOut, col, row0, policy);
+        tma_store_2d(map_du, sa + 3 * kStageOut, col, row0, policy);
+        if (save_da) tma_store_2d(map_da, sa + 4 * kStageOut, col, row0, policy);
+        bulk_commit();
+      }
+    }
+    if (!ok) break;
+    g += nl;
+    tc_fence_before();
+    __syncwarp();
+    // Release this accumulator buffer to the MMA issuer (on the even CTA of a pair).
+    if (lane == 0) mbar_arrive_cluster(empty_addr0 + (uint32_t)(b * sizeof(uint64_t)));
+  }
+  if (!ok) {
+    record_gemm_error();
+    // Loads still in flight must land before this CTA's shared memory is released.
+    if (pending_mask & 1u) wait_bounded(&bars->epi_full[wi][0], (pending_gc0 >> 1) & 1);
+    if (pending_mask & 2u) wait_bounded(&bars->epi_full[wi][1], (pending_gc1 >> 1) & 1);
+  }
+  // The staging tiles must stay valid until this warp's last TMA stores have completed.
+  if (lane == 0) bulk_wait_all();
+  __syncwarp();
+}
+
+// Forward: A = x, B = (w_gate | w_up), epilogue act = silu(gate) * up (+ gate, up stored).
+// kBwd: A = dy (the down projection's output gradient), B = the two halves of w_down^T
+// (rows [0, n) and [n, 2n) of the [2n, k] transposed down weight), so the accumulator holds
+// d_act for columns c and n + c of a tile; the epilogue (bwd_epilogue) reads gate and up at
+// those columns and stores dgate and dup (+ d_act when save_pre). map_act/map_gate/map_up
+// are then the d_act, dgate and dup outputs and map_gin/map_uin the gate and up inputs.
+template <typename T, bool kPair, bool kBwd>
 __device__ __forceinline__ void swiglu_gemm_body(const CUtensorMap* map_x,
                                                  const CUtensorMap* map_wg,
                                                  const CUtensorMap* map_wu,
                                                  const CUtensorMap* map_act,
                                                  const CUtensorMap* map_gate,
-                                                 const CUtensorMap* map_up, int save_pre, int m,
+                                                 const CUtensorMap* map_up,
+                                                 const CUtensorMap* map_gin,
+                                                 const CUtensorMap* map_uin, int save_pre, int m,
                                                  int n, int k) {
-  using S = Shape<kPair>;
+  using S = Shape<kPair, kBwd>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   const uint32_t pad = ((raw + 1023u) & ~1023u) - raw;
   unsigned char* tiles = smem_raw + pad;
   unsigned char* staging = tiles + S::kStages * S::kStageBytes;  // 1024-byte aligned
-  GemmBarriers* bars = reinterpret_cast<GemmBarriers*>(staging + kStagingBytes);
+  GemmBarriers* bars = reinterpret_cast<GemmBarriers*>(staging + S::kStagingBytes);
   const uint32_t tiles_addr = raw + pad;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -387,6 +545,8 @@ __device__ __forceinline__ void swiglu_gemm_body(const CUtensorMap* map_x,
       mbar_init(&bars->tmem_empty[b], kEpiWarps * S::kCtas);
     }
     mbar_init(&bars->drain, 1);
+    for (int w = 0; w < kEpiWarps; ++w)
+      for (int b = 0; b < kEpiBufs; ++b) mbar_init(&bars->epi_full[w][b], 1);
     fence_mbar_init();
   }
   if (warp == 2) tmem_alloc<kPair>(&bars->tmem_base);
@@ -481,6 +641,9 @@ __device__ __forceinline__ void swiglu_gemm_body(const CUtensorMap* map_x,
       wait_bounded(&bars->drain, 0);
     }
     __syncwarp();
+  } else if (warp >= kEpiWarp0 && kBwd) {
+    bwd_epilogue<T, kPair>(bars, staging, tmem_base, grid, unit, units, rank, map_act, map_gate,
+                           map_up, map_gin, map_uin, save_pre, n);
   } else if (warp >= kEpiWarp0) {
     // ---------------------------------------------------------------- epilogue --
     const int q = warp & 3;  // this warp may read tensor-memory lanes [32q, 32q + 32)
@@ -574,8 +737,8 @@ swiglu_gemm_kernel(const __grid_constant__ CUtensorMap map_x,
                    const __grid_constant__ CUtensorMap map_act,
                    const __grid_constant__ CUtensorMap map_gate,
                    const __grid_constant__ CUtensorMap map_up, int save_pre, int m, int n, int k) {
-  swiglu_gemm_body<T, false>(&map_x, &map_wg, &map_wu, &map_act, &map_gate, &map_up, save_pre,
-                             m, n, k);
+  swiglu_gemm_body<T, false, false>(&map_x, &map_wg, &map_wu, &map_act, &map_gate, &map_up,
+                                    &map_gate, &map_up, save_pre, m, n, k);
 }
 
 template <typename T>
@@ -587,8 +750,41 @@ swiglu_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_x,
                         const __grid_constant__ CUtensorMap map_gate,
                         const __grid_constant__ CUtensorMap map_up, int save_pre, int m, int n,
                         int k) {
-  swiglu_gemm_body<T, true>(&map_x, &map_wg, &map_wu, &map_act, &map_gate, &map_up, save_pre, m,
-                            n, k);
+  swiglu_gemm_body<T, true, false>(&map_x, &map_wg, &map_wu, &map_act, &map_gate, &map_up,
+                                   &map_gate, &map_up, save_pre, m, n, k);
+}
+
+// The down projection's data gradient with the SwiGLU backward in the epilogue (see
+// swiglu_gemm_body, kBwd): map_dy [m, k], map_w0 / map_w1 the two [n, k] halves of w_down^T,
+// outputs map_da (optional d_act), map_dg, map_du [m, 2n], inputs map_gin, map_uin [m, 2n].
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+swiglu_gemm_bwd_kernel(const __grid_constant__ CUtensorMap map_dy,
+                       const __grid_constant__ CUtensorMap map_w0,
+                       const __grid_constant__ CUtensorMap map_w1,
+                       const __grid_constant__ CUtensorMap map_da,
+                       const __grid_constant__ CUtensorMap map_dg,
+                       const __grid_constant__ CUtensorMap map_du,
+                       const __grid_constant__ CUtensorMap map_gin,
+                       const __grid_constant__ CUtensorMap map_uin, int save_da, int m, int n,
+                       int k) {
+  swiglu_gemm_body<T, false, true>(&map_dy, &map_w0, &map_w1, &map_da, &map_dg, &map_du,
+                                   &map_gin, &map_uin, save_da, m, n, k);
+}
+
+template <typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+swiglu_gemm_bwd_pair_kernel(const __grid_constant__ CUtensorMap map_dy,
+                            const __grid_constant__ CUtensorMap map_w0,
+                            const __grid_constant__ CUtensorMap map_w1,
+                            const __grid_constant__ CUtensorMap map_da,
+                            const __grid_constant__ CUtensorMap map_dg,
+                            const __grid_constant__ CUtensorMap map_du,
+                            const __grid_constant__ CUtensorMap map_gin,
+                            const __grid_constant__ CUtensorMap map_uin, int save_da, int m,
+                            int n, int k) {
+  swiglu_gemm_body<T, true, true>(&map_dy, &map_w0, &map_w1, &map_da, &map_dg, &map_du,
+                                  &map_gin, &map_uin, save_da, m, n, k);
 }
 
 // ------------------------------------------------------------------------ host ------
@@ -698,6 +894,58 @@ int gemm_impl(const void* x, int64_t xs, const void* wg, const void* wu, int64_t
   return check_launch("pt_swiglu_gemm_fwd");
 }
 
+// d_act = dy @ w_down (computed as dy against w_down_t = w_down^T, [n, k] row-major, split
+// into its two n/2-row halves) with dgate / dup from gate and up in the epilogue; d_act is
+// stored only when dact_out is given.
+template <typename T>
+int gemm_bwd_impl(const void* dy, int64_t dys, const void* wdt, int64_t wds, const void* gate,
+                  const void* up, int64_t ps, void* dgate, void* dup, int64_t gs, void* dact,
+                  int64_t das, int64_t m, int64_t n, int64_t k, cudaStream_t stream) {
+  const CUtensorMapDataType type = std::is_same<T, __nv_bfloat16>::value
+                                       ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const int64_t nh = n / 2;
+  const void* wdt1 = static_cast<const unsigned char*>(wdt) + nh * wds * (int64_t)sizeof(T);
+  constexpr auto sw64 = CU_TENSOR_MAP_SWIZZLE_64B;
+  CUtensorMap mdy, mw0, mw1, mgi, mui, mdg, mdu, mda;
+  if (int st = make_map(&mdy, dy, m, k, dys, kBM, type, "dy")) return st;
+  if (int st = make_map(&mw0, wdt, nh, k, wds, kBN, type, "w_down_t")) return st;
+  if (int st = make_map(&mw1, wdt1, nh, k, wds, kBN, type, "w_down_t (second half)")) return st;
+  if (int st = make_map(&mgi, gate, m, n, ps, 32, type, "gate", kEpiCols, sw64)) return st;
+  if (int st = make_map(&mui, up, m, n, ps, 32, type, "up", kEpiCols, sw64)) return st;
+  if (int st = make_map(&mdg, dgate, m, n, gs, 32, type, "dgate", kEpiCols, sw64)) return st;
+  if (int st = make_map(&mdu, dup, m, n, gs, 32, type, "dup", kEpiCols, sw64)) return st;
+  const int save_da = dact != nullptr;
+  if (save_da) {
+    if (int st = make_map(&mda, dact, m, n, das, 32, type, "dact_out", kEpiCols, sw64)) return st;
+  } else {
+    mda = mdg;  // never used
+  }
+  int dev = 0, sms = 0;
+  if (int st = current_device_info(&dev, &sms)) return st;
+  const int64_t tiles_n = (nh + kBN - 1) / kBN;
+  if (m > kBM && sms >= 2) {
+    using S = Shape<true, true>;
+    const void* fn = (const void*)swiglu_gemm_bwd_pair_kernel<T>;
+    if (!allow_smem(fn, S::kSmemBytes, dev))
+      return set_error(PT_ERR_CUDA, "cannot raise the shared memory limit of the GEMM kernel");
+    const int64_t tiles = ((m + S::kTileM - 1) / S::kTileM) * tiles_n;
+    const int pairs = (int)std::min<int64_t>(tiles, sms / 2);
+    swiglu_gemm_bwd_pair_kernel<T><<<2 * pairs, kThreads, S::kSmemBytes, stream>>>(
+        mdy, mw0, mw1, mda, mdg, mdu, mgi, mui, save_da, (int)m, (int)nh, (int)k);
+  } else {
+    using S = Shape<false, true>;
+    const void* fn = (const void*)swiglu_gemm_bwd_kernel<T>;
+    if (!allow_smem(fn, S::kSmemBytes, dev))
+      return set_error(PT_ERR_CUDA, "cannot raise the shared memory limit of the GEMM kernel");
+    const int64_t tiles = ((m + S::kTileM - 1) / S::kTileM) * tiles_n;
+    const int grid = (int)std::min<int64_t>(tiles, sms);
+    swiglu_gemm_bwd_kernel<T><<<grid, kThreads, S::kSmemBytes, stream>>>(
+        mdy, mw0, mw1, mda, mdg, mdu, mgi, mui, save_da, (int)m, (int)nh, (int)k);
+  }
+  return check_launch("pt_swiglu_gemm_bwd");
+}
+
 }  // namespace
 
 // Reads and clears this file's device error word (called by pt_take_device_error).
@@ -763,6 +1011,54 @@ int pt_swiglu_gemm_fwd(const void* x, int64_t x_row_stride, const void* w_gate,
     default:
       return set_error(PT_ERR_UNSUPPORTED_DTYPE,
                        "pt_swiglu_gemm_fwd supports bfloat16 and float16 (got dtype %d)", dtype);
+  }
+}
+
+int pt_swiglu_gemm_bwd(const void* dy, int64_t dy_row_stride, const void* w_down_t,
+                       int64_t w_row_stride, const void* gate, const void* up,
+                       int64_t pre_row_stride, void* dgate, void* dup, int64_t grad_row_stride,
+                       void* dact_out, int64_t dact_row_stride, int64_t m, int64_t n, int64_t k,
+                       int dtype, void* stream) {
+  if (m < 0 || n < 0 || k < 0)
+    return set_error(PT_ERR_SHAPE, "m, n, k must be >= 0 (got %lld, %lld, %lld)", (long long)m,
+                     (long long)n, (long long)k);
+  if (m == 0 || n == 0) return ok();
+  if (k == 0) return set_error(PT_ERR_SHAPE, "k must be >= 1");
+  if (m > INT32_MAX / 2 || n > INT32_MAX / 2 || k > INT32_MAX / 2)
+    return set_error(PT_ERR_SHAPE, "m, n and k must each be below 2^30");
+  if (n % 64 != 0 || k % 8 != 0)
+    return set_error(PT_ERR_SHAPE, "n must be a multiple of 64 and k of 8 (got n=%lld, k=%lld)",
+                     (long long)n, (long long)k);
+  if (dy_row_stride < k || w_row_stride < k || pre_row_stride < n || grad_row_stride < n ||
+      (dact_out != nullptr && dact_row_stride < n))
+    return set_error(PT_ERR_SHAPE, "a row stride is smaller than its row");
+  if (dy_row_stride % 8 || w_row_stride % 8 || pre_row_stride % 8 || grad_row_stride % 8 ||
+      (dact_out != nullptr && dact_row_stride % 8))
+    return set_error(PT_ERR_SHAPE, "row strides must be multiples of 8 elements");
+  const void* ptrs[7] = {dy, w_down_t, gate, up, dgate, dup, dact_out};
+  const char* names[7] = {"dy", "w_down_t", "gate", "up", "dgate", "dup", "dact_out"};
+  for (int i = 0; i < 7; ++i) {
+    if (ptrs[i] == nullptr && i == 6) continue;
+    if (int st = check_device_ptr(ptrs[i], names[i])) return st;
+    if (!aligned16(ptrs[i]))
+      return set_error(PT_ERR_INVALID_ARGUMENT, "%s must be 16-byte aligned", names[i]);
+  }
+  for (int o = 4; o < 7; ++o)
+    for (int i = 0; i < 4; ++i)
+      if (ptrs[o] != nullptr && ptrs[o] == ptrs[i])
+        return set_error(PT_ERR_INVALID_ARGUMENT, "%s must not alias %s", names[o], names[i]);
+  switch (dtype) {
+    case PT_BFLOAT16:
+      return gemm_bwd_impl<__nv_bfloat16>(dy, dy_row_stride, w_down_t, w_row_stride, gate, up,
+                                          pre_row_stride, dgate, dup, grad_row_stride, dact_out,
+                                          dact_row_stride, m, n, k, as_stream(stream));
+    case PT_FLOAT16:
+      return gemm_bwd_impl<__half>(dy, dy_row_stride, w_down_t, w_row_stride, gate, up,
+                                   pre_row_stride, dgate, dup, grad_row_stride, dact_out,
+                                   dact_row_stride, m, n, k, as_stream(stream));
+    default:
+      return set_error(PT_ERR_UNSUPPORTED_DTYPE,
+                       "pt_swiglu_gemm_bwd supports bfloat16 and float16 (got dtype %d)", dtype);
   }
 }
 

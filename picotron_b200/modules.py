@@ -109,10 +109,16 @@ class SwiGLU(nn.Module):
         if (self.fuse_gate_up and hidden_states.is_cuda
                 and self._compute_dtype(hidden_states) in (torch.bfloat16, torch.float16)):
             dtype = self._compute_dtype(hidden_states)
-            activated = torch.ops.picotron_b200.swiglu_gate_up(
-                hidden_states.to(dtype), self.gate_projection.weight.to(dtype),
-                self.up_projection.weight.to(dtype))[0]
-            return self.down_projection(activated)
+            x = hidden_states.to(dtype)
+            w_gate = self.gate_projection.weight.to(dtype)
+            w_up = self.up_projection.weight.to(dtype)
+            down = self.down_projection
+            if down.bias is None and ops.fused_down_backward_supported(x, down.weight):
+                # Both activation passes inside tensor-core GEMMs: the forward's epilogue and
+                # the backward's (the down projection's input gradient never reaches HBM).
+                return ops.swiglu_mlp(x, w_gate, w_up, down.weight.to(dtype))
+            activated = torch.ops.picotron_b200.swiglu_gate_up(x, w_gate, w_up)[0]
+            return down(activated)
         gate = self.gate_projection(hidden_states)
         up = self.up_projection(hidden_states)
         return self.down_projection(self.activation(gate, up))

@@ -452,6 +452,84 @@ def _gate_up_backward(ctx, d_act, d_gate, d_up):
 swiglu_gate_up.register_autograd(_gate_up_backward, setup_context=_gate_up_setup)
 
 
+def fused_down_backward_supported(x: Tensor, w_down: Tensor) -> bool:
+    """True when pt_swiglu_gemm_bwd takes the MLP's shapes (intermediate size a multiple of
+    64, hidden size a multiple of 8)."""
+
+    return w_down.dim() == 2 and w_down.size(1) % 64 == 0 and w_down.size(0) % 8 == 0
+
+
+@torch.library.custom_op("picotron_b200::swiglu_down_backward", mutates_args=())
+def swiglu_down_backward(d_out: Tensor, w_down: Tensor, gate: Tensor,
+                         up: Tensor) -> tuple[Tensor, Tensor]:
+    """(dgate, dup) from the down projection's output gradient: d_act = d_out @ w_down and
+    the SwiGLU backward in one tcgen05 GEMM (pt_swiglu_gemm_bwd); d_act stays on chip."""
+
+    check_device(d_out.device, TritonSwiGLUUnavailable)
+    if not (d_out.dtype == w_down.dtype == gate.dtype == up.dtype) or d_out.dtype not in (
+            torch.bfloat16, torch.float16):
+        raise TritonSwiGLUUnavailable("the fused down-projection backward takes one dtype, "
+                                      "bfloat16 or float16")
+    k, n = w_down.shape
+    if (d_out.size(-1) != k or gate.shape != up.shape or gate.size(-1) != n
+            or gate.shape[:-1] != d_out.shape[:-1]):
+        raise TritonSwiGLUUnavailable("expected d_out [..., k], w_down [k, n], gate, up [..., n]")
+    dgate = torch.empty(gate.shape, dtype=gate.dtype, device=gate.device)
+    dup = torch.empty(gate.shape, dtype=gate.dtype, device=gate.device)
+    if dgate.numel() == 0:
+        return dgate, dup
+    d2 = _as_rows(d_out, k)
+    if d2.stride(0) % 8 or d2.data_ptr() % 16:
+        d2 = d2.contiguous()
+    g2, u2 = gate.reshape(-1, n).contiguous(), up.reshape(-1, n).contiguous()
+    wdt = w_down.t().contiguous()  # [n, k]: both GEMM operands read along k
+    with _OnDevice(d_out.device):
+        _capi.swiglu_gemm_bwd(
+            d2.data_ptr(), d2.stride(0), wdt.data_ptr(), k, g2.data_ptr(), u2.data_ptr(), n,
+            dgate.data_ptr(), dup.data_ptr(), n, None, 0, d2.size(0), n, k,
+            DTYPE_CODES[d_out.dtype], _stream(d_out.device), TritonSwiGLUUnavailable,
+        )
+    return dgate, dup
+
+
+@swiglu_down_backward.register_fake
+def _swiglu_down_backward_fake(d_out, w_down, gate, up):
+    return (torch.empty(gate.shape, dtype=gate.dtype, device=gate.device),
+            torch.empty(gate.shape, dtype=gate.dtype, device=gate.device))
+
+
+class _SwiGLUMLP(torch.autograd.Function):
+    """down_projection(silu(gate_projection(x)) * up_projection(x)) without biases (reference
+    SwiGLU.forward, feedforward.py:27-43). Forward: the gate/up GEMMs with the activation in
+    their epilogue, then the down projection (library GEMM). Backward: the down projection's
+    weight gradient (library GEMM), its input gradient with the activation's backward in the
+    epilogue (pt_swiglu_gemm_bwd), then the gate/up projections' gradients (library GEMMs)."""
+
+    @staticmethod
+    def forward(ctx, x, w_gate, w_up, w_down):
+        act, gate, up = torch.ops.picotron_b200.swiglu_gate_up(x, w_gate, w_up)
+        ctx.save_for_backward(x, w_gate, w_up, w_down, act, gate, up)
+        return torch.nn.functional.linear(act, w_down)
+
+    @staticmethod
+    def backward(ctx, d_out):
+        x, w_gate, w_up, w_down, act, gate, up = ctx.saved_tensors
+        n, k = w_gate.shape
+        d_out = d_out.to(x.dtype)
+        d2 = d_out.reshape(-1, w_down.size(0))
+        dw_down = d2.t() @ act.reshape(-1, n)
+        dg, du = torch.ops.picotron_b200.swiglu_down_backward(d_out, w_down, gate, up)
+        x2, dg2, du2 = x.reshape(-1, k), dg.reshape(-1, n), du.reshape(-1, n)
+        dx = (dg2 @ w_gate).addmm_(du2, w_up).reshape(x.shape)
+        return dx, dg2.t() @ x2, du2.t() @ x2, dw_down
+
+
+def swiglu_mlp(x: Tensor, w_gate: Tensor, w_up: Tensor, w_down: Tensor) -> Tensor:
+    """The SwiGLU MLP with both activation passes fused into tensor-core GEMMs."""
+
+    return _SwiGLUMLP.apply(x, w_gate, w_up, w_down)
+
+
 # --------------------------------------------------------------------- cross-entropy --
 
 

@@ -266,6 +266,9 @@ def test_fake_implementations_of_next_step_ops():
     wg = torch.empty(96, 64, device="meta", dtype=torch.bfloat16)
     act, g, u = torch.ops.picotron_b200.swiglu_gate_up(x, wg, wg)
     assert act.shape == (3, 5, 96) and g.shape == act.shape and u.dtype == torch.bfloat16
+    wd = torch.empty(64, 96, device="meta", dtype=torch.bfloat16)
+    dg, du = torch.ops.picotron_b200.swiglu_down_backward(x, wd, g, u)
+    assert dg.shape == g.shape and du.shape == u.shape and dg.dtype == torch.bfloat16
     logits = torch.empty(2, 1000, 7, device="meta", dtype=torch.bfloat16)
     targets = torch.empty(2, 7, device="meta", dtype=torch.long)
     loss, lse, mean = torch.ops.picotron_b200.cross_entropy(logits, targets, -100)
