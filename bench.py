@@ -87,8 +87,9 @@ def copy_nccl_log_to_stderr(rank: int) -> None:
         Path(path).unlink()
     except OSError:
         return
-    for line in text.splitlines():
-        print(f"[rank {rank}] {line}", file=sys.stderr)
+    block = "".join(f"[rank {rank}] {line}\n" for line in text.splitlines())
+    sys.stderr.write(block)  # one write per rank, so ranks do not interleave within a line
+    sys.stderr.flush()
 METRIC = "RMSNorm+SwiGLU fwd+bwd tokens/s & HBM GB/s (bf16, h4096/i14336) at 1–8 B200"
 HIDDEN, INTER = 4096, 14336
 EPS = 1e-5
