@@ -750,7 +750,7 @@ class OpWorkload:
             # dy, w_down^T, gate, up in, dgate, dup out.
             self.bytes = ((tokens * k + 2 * INTER * k + 3 * tokens * INTER) + 2 * INTER * k
                           + (tokens * k + INTER * k + 4 * tokens * INTER)) * BF16
-            self.launches_per_step = 2
+            self.launches_per_step = 3
             self.dominant = ("swiglu_gemm_bwd_pair_kernel (d_act GEMM + SwiGLU backward)",
                              2 * tokens * INTER * k)
         elif op == "ce":
@@ -891,7 +891,8 @@ class OpWorkload:
             c.swiglu_gemm_fwd(x.data_ptr(), HIDDEN, self.wg.data_ptr(), self.wu.data_ptr(), HIDDEN,
                               self.act.data_ptr(), INTER, self.g.data_ptr(), self.u.data_ptr(),
                               INTER, T, INTER, HIDDEN, c.PT_BFLOAT16, stream)
-            self.wdt.copy_(self.wd.t())
+            c.transpose_2d(self.wd.data_ptr(), INTER, self.wdt.data_ptr(), HIDDEN, HIDDEN, INTER,
+                           c.PT_BFLOAT16, stream)
             if ev: ev[0].record()
             c.swiglu_gemm_bwd(dy.data_ptr(), HIDDEN, self.wdt.data_ptr(), HIDDEN, self.g.data_ptr(),
                               self.u.data_ptr(), INTER, self.dg.data_ptr(), self.du.data_ptr(),

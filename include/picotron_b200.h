@@ -330,6 +330,14 @@ PT_API int pt_swiglu_gemm_bwd(const void* dy, int64_t dy_row_stride,
                               int64_t m, int64_t n, int64_t k, int dtype,
                               void* stream);
 
+/* dst[c, r] = src[r, c] for a [rows, cols] matrix (row strides in elements), in 64 x 64 tiles
+ * through shared memory: w_down as [k, n] into the w_down_t that pt_swiglu_gemm_bwd reads.
+ * bf16, fp16 or fp32; dst must not alias src. No reference counterpart (the reference's
+ * backward multiplies by w_down through autograd without a transposed copy). */
+PT_API int pt_transpose_2d(const void* src, int64_t src_row_stride,
+                           void* dst, int64_t dst_row_stride,
+                           int64_t rows, int64_t cols, int dtype, void* stream);
+
 /* ---------------------------------------------------------- cross-entropy ------- */
 
 /* Mean cross-entropy over rows of `vocab` logits (class stride 1). Rows form an

@@ -81,6 +81,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pt_swiglu_gemm_bwd": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64,
                                     _c_ptr, _c_ptr, _c_i64, _c_ptr, _c_i64, _c_i64, _c_i64,
                                     _c_i64, _c_int, _c_ptr]),
+    "pt_transpose_2d": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_i64, _c_i64, _c_int, _c_ptr]),
     "pt_cross_entropy_fwd": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_ptr,
                                       _c_i64, _c_i64, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_int,
                                       _c_ptr]),
@@ -367,6 +368,16 @@ def swiglu_gemm_bwd(dy: int, dy_row_stride: int, w_down_t: int, w_row_stride: in
                                           pre_row_stride, dgate, dup, grad_row_stride, dact_out,
                                           dact_row_stride, m, n, k, dtype, stream)
     _check("pt_swiglu_gemm_bwd", status, error_type)
+
+
+def transpose_2d(src: int, src_row_stride: int, dst: int, dst_row_stride: int, rows: int,
+                 cols: int, dtype: int, stream: int,
+                 error_type: type[Exception] | None = None) -> None:
+    """dst = src transposed (pt_transpose_2d)."""
+
+    status = library().pt_transpose_2d(src, src_row_stride, dst, dst_row_stride, rows, cols,
+                                       dtype, stream)
+    _check("pt_transpose_2d", status, error_type)
 
 
 def cross_entropy_fwd(logits: int, vocab: int, outer: int, inner: int, logits_strides,

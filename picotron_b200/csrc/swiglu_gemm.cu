@@ -61,8 +61,8 @@ constexpr int kEpiCols = 32;
 constexpr int kStageOut = 32 * kEpiCols * 2;               // one 32 x 32 16-bit tile: 2 KB
 constexpr int kEpiBufs = 2;  // double-buffered: a chunk is staged while the last one is stored
 // Staged 32 x 32 tiles per warp and buffer: forward (act, gate, up); backward (gate and up
-// loaded, dgate, dup and optionally d_act stored).
-template <bool kBwd> constexpr int staged_tiles() { return kBwd ? 5 : 3; }
+// loaded, dgate and dup stored; the optional d_act is staged in the consumed gate tile).
+template <bool kBwd> constexpr int staged_tiles() { return kBwd ? 4 : 3; }
 template <bool kBwd> constexpr int staging_bytes() {
   return kEpiWarps * kEpiBufs * staged_tiles<kBwd>() * kStageOut;
 }
@@ -80,9 +80,9 @@ template <bool kBwd> constexpr int staging_bytes() {
 #define PT_GEMM_PAIR_STAGES 5
 #endif
 // kBwd (the down projection's data gradient with the SwiGLU backward in the epilogue) uses
-// the same stages, 4 for CTA pairs to make room for its larger epilogue staging.
+// the same stages and a third more epilogue staging.
 template <bool kPair, bool kBwd = false> struct Shape {
-  static constexpr int kStages = kPair ? (kBwd ? 4 : PT_GEMM_PAIR_STAGES) : 3;
+  static constexpr int kStages = kPair ? PT_GEMM_PAIR_STAGES : 3;
   static constexpr int kStageBytes = kATileBytes + (kPair ? 1 : 2) * kWTileBytes;
   static constexpr int kTileM = kPair ? 2 * kBM : kBM;
   static constexpr int kCtas = kPair ? 2 : 1;
@@ -385,7 +385,7 @@ __device__ __forceinline__ void bwd_epilogue(GemmBarriers* bars, unsigned char* 
                                              const CUtensorMap* map_uin, int save_da,
                                              int n_half) {
   using S = Shape<kPair, true>;
-  constexpr int kTiles = staged_tiles<true>();  // gate, up in; dgate, dup, d_act out
+  constexpr int kTiles = staged_tiles<true>();  // gate, up in; dgate, dup out
   constexpr int kChunks = 2 * kBN / kEpiCols;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = warp & 3, wi = warp - kEpiWarp0;
@@ -403,6 +403,8 @@ __device__ __forceinline__ void bwd_epilogue(GemmBarriers* bars, unsigned char* 
     unsigned char* st = st0 + bb * kTiles * kStageOut;
     uint64_t* bar = &bars->epi_full[wi][bb];
     if (lane == 0) {
+      // With d_act staged in the gate tile, its TMA store must have read it first.
+      if (save_da) bulk_wait_read<0>();
       mbar_arrive_expect_tx(bar, 2 * kStageOut);
       tma_load_2d<false>(smem_addr(st), map_gin, col, row, smem_addr(bar));
       tma_load_2d<false>(smem_addr(st + kStageOut), map_uin, col, row, smem_addr(bar));
@@ -470,7 +472,8 @@ __device__ __forceinline__ void bwd_epilogue(GemmBarriers* bars, unsigned char* 
         }
         *reinterpret_cast<uint4*>(st + 2 * kStageOut + off) = pack<T>(dg8);
         *reinterpret_cast<uint4*>(st + 3 * kStageOut + off) = pack<T>(du8);
-        if (save_da) *reinterpret_cast<uint4*>(st + 4 * kStageOut + off) = pack<T>(da8);
+        // The gate values at `off` were read above by this thread alone: reuse the slot.
+        if (save_da) *reinterpret_cast<uint4*>(st + off) = pack<T>(da8);
       }
       // Orders this chunk's shared-memory reads (before the buffer is refilled by TMA) and
       // writes (before the TMA stores read them) with the async proxy.
@@ -481,7 +484,7 @@ __device__ __forceinline__ void bwd_epilogue(GemmBarriers* bars, unsigned char* 
         const uint32_t sa = smem_addr(st);
         tma_store_2d(map_dg, sa + 2 * kStageOut, col, row0, policy);
         tma_store_2d(map_du, sa + 3 * kStageOut, col, row0, policy);
-        if (save_da) tma_store_2d(map_da, sa + 4 * kStageOut, col, row0, policy);
+        if (save_da) tma_store_2d(map_da, sa, col, row0, policy);
         bulk_commit();
       }
     }

@@ -482,8 +482,11 @@ def swiglu_down_backward(d_out: Tensor, w_down: Tensor, gate: Tensor,
     if d2.stride(0) % 8 or d2.data_ptr() % 16:
         d2 = d2.contiguous()
     g2, u2 = gate.reshape(-1, n).contiguous(), up.reshape(-1, n).contiguous()
-    wdt = w_down.t().contiguous()  # [n, k]: both GEMM operands read along k
+    wd = w_down.contiguous()
+    wdt = torch.empty((n, k), dtype=wd.dtype, device=wd.device)  # both operands read along k
     with _OnDevice(d_out.device):
+        _capi.transpose_2d(wd.data_ptr(), wd.stride(0), wdt.data_ptr(), k, k, n,
+                           DTYPE_CODES[wd.dtype], _stream(d_out.device), TritonSwiGLUUnavailable)
         _capi.swiglu_gemm_bwd(
             d2.data_ptr(), d2.stride(0), wdt.data_ptr(), k, g2.data_ptr(), u2.data_ptr(), n,
             dgate.data_ptr(), dup.data_ptr(), n, None, 0, d2.size(0), n, k,

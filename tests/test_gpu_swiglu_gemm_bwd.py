@@ -114,3 +114,19 @@ def test_rejects_unsupported_shapes_and_aliasing():
                               up.data_ptr(), 128, gate.data_ptr(), out.data_ptr(), 128, None, 0,
                               128, 128, 64, code, gu.stream())
     assert info.value.status == _capi.PT_ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32], ids=str)
+@pytest.mark.parametrize("rows,cols,pad", [(4096, 1536, 0), (130, 70, 0), (64, 8, 3), (1, 1, 0)],
+                         ids=str)
+def test_transpose_is_exact(dtype, rows, cols, pad):
+    # pad > 0 gives row strides that are not multiples of 8 (the element-wise path).
+    src = gu.randn((rows, cols + pad), 51, dtype)[:, :cols]
+    dst_buf = torch.full((cols, rows + pad), -7.0, dtype=dtype, device=gu.DEV)
+    dst = dst_buf[:, :rows]
+    _capi.transpose_2d(src.data_ptr(), src.stride(0), dst.data_ptr(), dst.stride(0), rows, cols,
+                       DTYPE_CODES[dtype], gu.stream())
+    torch.cuda.synchronize()
+    assert torch.equal(dst, src.t())
+    if pad:
+        assert torch.equal(dst_buf[:, rows:], torch.full_like(dst_buf[:, rows:], -7.0))
