@@ -60,11 +60,14 @@ constexpr long long kWaitCycles = 2000000000LL;  // about one second of SM clock
 constexpr int kEpiCols = 32;
 constexpr int kStageOut = 32 * kEpiCols * 2;               // one 32 x 32 16-bit tile: 2 KB
 constexpr int kEpiBufs = 2;  // double-buffered: a chunk is staged while the last one is stored
-// Staged 32 x 32 tiles per warp and buffer: forward (act, gate, up); backward (gate and up
-// loaded, dgate and dup stored; the optional d_act is staged in the consumed gate tile).
-template <bool kBwd> constexpr int staged_tiles() { return kBwd ? 4 : 3; }
+// Epilogue staging per warp: forward, kEpiBufs buffers of (act, gate, up); backward, a ring of
+// kEpiInBufs buffers of (gate, up) loaded ahead and kEpiBufs of (dgate, dup) to store (the
+// optional d_act is staged in the consumed gate tile).
+constexpr int kEpiInBufs = 4;
+constexpr int kBarrierBytes = 512;  // shared memory reserved for GemmBarriers
+constexpr int kBwdWarpStaging = (kEpiInBufs * 2 + kEpiBufs * 2) * kStageOut;
 template <bool kBwd> constexpr int staging_bytes() {
-  return kEpiWarps * kEpiBufs * staged_tiles<kBwd>() * kStageOut;
+  return kBwd ? kEpiWarps * kBwdWarpStaging : kEpiWarps * kEpiBufs * 3 * kStageOut;
 }
 
 // Two shapes of the same pipeline:
@@ -79,16 +82,16 @@ template <bool kBwd> constexpr int staging_bytes() {
 #ifndef PT_GEMM_PAIR_STAGES
 #define PT_GEMM_PAIR_STAGES 5
 #endif
-// kBwd (the down projection's data gradient with the SwiGLU backward in the epilogue) uses
-// the same stages and a third more epilogue staging.
+// kBwd (the down projection's data gradient with the SwiGLU backward in the epilogue) gives
+// one pipeline stage (two for single CTAs, used only for m <= 128) to its deeper epilogue.
 template <bool kPair, bool kBwd = false> struct Shape {
-  static constexpr int kStages = kPair ? PT_GEMM_PAIR_STAGES : 3;
+  static constexpr int kStages = kPair ? (kBwd ? 4 : PT_GEMM_PAIR_STAGES) : (kBwd ? 2 : 3);
   static constexpr int kStageBytes = kATileBytes + (kPair ? 1 : 2) * kWTileBytes;
   static constexpr int kTileM = kPair ? 2 * kBM : kBM;
   static constexpr int kCtas = kPair ? 2 : 1;
   static constexpr int kStagingBytes = staging_bytes<kBwd>();
   static constexpr int kSmemBytes =
-      1024 /* alignment slack */ + kStages * kStageBytes + kStagingBytes + 256;
+      1024 /* alignment slack */ + kStages * kStageBytes + kStagingBytes + kBarrierBytes;
 };
 static_assert(Shape<false>::kStages <= kMaxStages && Shape<true>::kStages <= kMaxStages &&
                   Shape<true, true>::kStages <= kMaxStages, "");
@@ -103,10 +106,10 @@ struct GemmBarriers {
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
   uint64_t drain;
-  uint64_t epi_full[kEpiWarps][kEpiBufs];  // backward: the epilogue's gate/up tiles landed
+  uint64_t epi_full[kEpiWarps][kEpiInBufs];  // backward: the epilogue's gate/up tiles landed
   uint32_t tmem_base;
 };
-static_assert(sizeof(GemmBarriers) <= 256, "barrier block must fit its reserved space");
+static_assert(sizeof(GemmBarriers) <= kBarrierBytes, "barrier block must fit its space");
 
 __device__ __forceinline__ void record_gemm_error() {
   atomicExch(&g_gemm_error, kDeviceErrWaitTimeout);
@@ -367,14 +370,16 @@ struct TileGrid {
 
 // Epilogue of the backward GEMM (kBwd): per tile, each epilogue warp owns 32 rows (tensor
 // memory lanes [32q, 32q + 32)) and walks 8 chunks of 32 columns, 4 in each accumulator half
-// (columns c of d_act, then n_half + c). Per chunk, lane 0 loads the gate and up 32 x 32
-// tiles with TMA (64-byte swizzle, the next chunk's while this one computes), the warp reads
-// its 32 d_act values from tensor memory, rounds them to T (the d_act a separate GEMM would
-// store), forms dgate = (d_act * up) * (s * (1 + gate * (1 - s))) and dup = d_act * (gate * s)
-// with s = sigmoid(gate) in fp32 (the operation order of swiglu_bwd_vec), stages them and
-// stores them with TMA. Chunks past n_half (a last tile column narrower than 128) are
-// skipped. Every wait is bounded; after a timeout the warp stops, records the error word and
-// waits (bounded) for its own loads in flight.
+// (columns c of d_act, then n_half + c); chunks past n_half (a last tile column narrower than
+// 128) are skipped. Lane 0 loads the gate and up 32 x 32 tiles of the chunks with TMA (64-byte
+// swizzle) into a ring of kEpiInBufs buffers, up to kEpiInBufs - 1 chunks ahead of the one
+// being computed and across tile boundaries, so the loads' latency hides behind the work of
+// the chunks before them. Per chunk the warp reads its 32 d_act values from tensor memory,
+// rounds them to T (the d_act a separate GEMM would store), forms
+// dgate = (d_act * up) * (s * (1 + gate * (1 - s))) and dup = d_act * (gate * s) with
+// s = sigmoid(gate) in fp32 (the operation order of swiglu_bwd_vec), stages them and stores
+// them with TMA. Every wait is bounded; after a timeout the warp stops, records the error
+// word and waits (bounded) for its own loads in flight.
 template <typename T, bool kPair>
 __device__ __forceinline__ void bwd_epilogue(GemmBarriers* bars, unsigned char* staging,
                                              uint32_t tmem_base, const TileGrid& grid, int unit,
@@ -385,46 +390,60 @@ __device__ __forceinline__ void bwd_epilogue(GemmBarriers* bars, unsigned char* 
                                              const CUtensorMap* map_uin, int save_da,
                                              int n_half) {
   using S = Shape<kPair, true>;
-  constexpr int kTiles = staged_tiles<true>();  // gate, up in; dgate, dup out
   constexpr int kChunks = 2 * kBN / kEpiCols;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = warp & 3, wi = warp - kEpiWarp0;
   const uint32_t empty_addr0 = kPair ? peer_addr(&bars->tmem_empty[0], 0)
                                      : smem_addr(&bars->tmem_empty[0]);
   const uint64_t policy = evict_first_policy();
-  unsigned char* st0 = staging + (size_t)wi * kEpiBufs * kTiles * kStageOut;
-  uint32_t g = 0;              // chunks this warp has loaded: buffer g & 1, phase (g >> 1) & 1
-  // Loads not yet waited for: bit bb of pending_mask, with their chunk numbers.
-  uint32_t pending_mask = 0, pending_gc0 = 0, pending_gc1 = 0;
-  bool ok = true;
-  int i = 0;
-  auto issue = [&](uint32_t gc, int row, int col) {
-    const int bb = gc & 1;
-    unsigned char* st = st0 + bb * kTiles * kStageOut;
+  unsigned char* in0 = staging + (size_t)wi * kBwdWarpStaging;  // kEpiInBufs x (gate, up)
+  unsigned char* out0 = in0 + kEpiInBufs * 2 * kStageOut;        // kEpiBufs x (dgate, dup)
+  // Live chunks of a tile: the first per_half of each half; live chunk li is chunk j = li of
+  // the first half or kChunks / 2 + (li - per_half) of the second.
+  auto per_half_of = [&](int nb) { return min(kChunks / 2, (n_half - nb * kBN) / kEpiCols); };
+  auto col_of = [&](int nb, int j) { return (j >> 2) * n_half + nb * kBN + (j & 3) * kEpiCols; };
+  // Load cursor: this CTA's tile lt and its live chunk lli; L loads issued, C chunks consumed.
+  int lt = unit, lli = 0;
+  uint32_t L = 0, C = 0;
+  auto issue_next = [&]() -> bool {
+    if (lt >= grid.count()) return false;
+    int mb, nb;
+    grid.coords(lt, mb, nb);
+    const int ph = per_half_of(nb);
+    const int j = lli < ph ? lli : kChunks / 2 + (lli - ph);
+    const int row = mb * S::kTileM + (int)rank * kBM + q * 32;
+    const int bb = (int)(L % kEpiInBufs);
+    unsigned char* st = in0 + bb * 2 * kStageOut;
     uint64_t* bar = &bars->epi_full[wi][bb];
     if (lane == 0) {
-      // With d_act staged in the gate tile, its TMA store must have read it first.
+      // With d_act staged in a gate tile, its TMA store must have read it first.
       if (save_da) bulk_wait_read<0>();
       mbar_arrive_expect_tx(bar, 2 * kStageOut);
-      tma_load_2d<false>(smem_addr(st), map_gin, col, row, smem_addr(bar));
-      tma_load_2d<false>(smem_addr(st + kStageOut), map_uin, col, row, smem_addr(bar));
+      tma_load_2d<false>(smem_addr(st), map_gin, col_of(nb, j), row, smem_addr(bar));
+      tma_load_2d<false>(smem_addr(st + kStageOut), map_uin, col_of(nb, j), row, smem_addr(bar));
     }
-    pending_mask |= 1u << bb;
-    if (bb) pending_gc1 = gc; else pending_gc0 = gc;
+    ++L;
+    if (++lli == 2 * ph) {
+      lli = 0;
+      lt += units;
+    }
+    return true;
   };
+  // Up to kEpiInBufs loads in flight, counting the chunk being computed; the buffer a new load
+  // fills was last read by chunk L - kEpiInBufs < C, already consumed and fenced.
+  auto prefetch = [&]() {
+    while (L < C + kEpiInBufs && issue_next()) {
+    }
+  };
+  bool ok = true;
+  int i = 0;
   for (int t = unit; ok && t < grid.count(); t += units, ++i) {
     const int b = i & 1;
     int mb, nb;
     grid.coords(t, mb, nb);
     const int row0 = mb * S::kTileM + (int)rank * kBM + q * 32;  // this warp's rows
-    // Live chunks: the first `per_half` of each half (all 4 unless the tile column is the
-    // last, narrower one); live chunk li is chunk j = li of the first half or 4 + (li -
-    // per_half) of the second.
-    const int per_half = min(kChunks / 2, (n_half - nb * kBN) / kEpiCols);
-    const int nl = 2 * per_half;
-    auto chunk_of = [&](int li) { return li < per_half ? li : kChunks / 2 + (li - per_half); };
-    auto col_of = [&](int j) { return (j >> 2) * n_half + nb * kBN + (j & 3) * kEpiCols; };
-    if (nl > 0) issue(g, row0, col_of(chunk_of(0)));
+    const int ph = per_half_of(nb);
+    prefetch();
     if (!wait_bounded(&bars->tmem_full[b], (i >> 1) & 1)) {
       ok = false;
       break;
@@ -432,23 +451,21 @@ __device__ __forceinline__ void bwd_epilogue(GemmBarriers* bars, unsigned char* 
     tc_fence_after();
     const uint32_t tg = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * kAccCols);
 #pragma unroll 1
-    for (int li = 0; li < nl; ++li) {
-      const int j = chunk_of(li);
-      const uint32_t gc = g + li;
-      const int bb = gc & 1;
-      // The other buffer was last read by the previous chunk (fenced below): refill it.
-      if (li + 1 < nl) issue(gc + 1, row0, col_of(chunk_of(li + 1)));
-      if (!wait_bounded(&bars->epi_full[wi][bb], (gc >> 1) & 1)) {
+    for (int li = 0; li < 2 * ph; ++li) {
+      prefetch();
+      const int j = li < ph ? li : kChunks / 2 + (li - ph);
+      const int bb = (int)(C % kEpiInBufs);
+      if (!wait_bounded(&bars->epi_full[wi][bb], (C / kEpiInBufs) & 1)) {
         ok = false;
         break;
       }
-      pending_mask &= ~(1u << bb);
-      unsigned char* st = st0 + bb * kTiles * kStageOut;
+      unsigned char* st = in0 + bb * 2 * kStageOut;
+      unsigned char* so = out0 + (C & 1) * 2 * kStageOut;
       uint32_t ar[32];
       tmem_ld32(tg + (j >> 2) * kBN + (j & 3) * kEpiCols, ar);
       tmem_wait_ld();
       reg_fence32(ar);
-      // The TMA stores that last used this buffer's output tiles must have read them.
+      // The TMA stores that last used this output buffer must have read it.
       if (lane == 0) bulk_wait_read<kEpiBufs - 1>();
       __syncwarp();
 #pragma unroll
@@ -470,26 +487,25 @@ __device__ __forceinline__ void bwd_epilogue(GemmBarriers* bars, unsigned char* 
           dg8[e] = (da8[e] * u8[e]) * (sg * (1.0f + g8[e] * (1.0f - sg)));
           du8[e] = da8[e] * (g8[e] * sg);
         }
-        *reinterpret_cast<uint4*>(st + 2 * kStageOut + off) = pack<T>(dg8);
-        *reinterpret_cast<uint4*>(st + 3 * kStageOut + off) = pack<T>(du8);
+        *reinterpret_cast<uint4*>(so + off) = pack<T>(dg8);
+        *reinterpret_cast<uint4*>(so + kStageOut + off) = pack<T>(du8);
         // The gate values at `off` were read above by this thread alone: reuse the slot.
         if (save_da) *reinterpret_cast<uint4*>(st + off) = pack<T>(da8);
       }
-      // Orders this chunk's shared-memory reads (before the buffer is refilled by TMA) and
-      // writes (before the TMA stores read them) with the async proxy.
+      // Orders this chunk's shared-memory reads (before TMA refills the buffer) and writes
+      // (before the TMA stores read them) with the async proxy.
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        const int col = col_of(j);
-        const uint32_t sa = smem_addr(st);
-        tma_store_2d(map_dg, sa + 2 * kStageOut, col, row0, policy);
-        tma_store_2d(map_du, sa + 3 * kStageOut, col, row0, policy);
-        if (save_da) tma_store_2d(map_da, sa, col, row0, policy);
+        const int col = col_of(nb, j);
+        tma_store_2d(map_dg, smem_addr(so), col, row0, policy);
+        tma_store_2d(map_du, smem_addr(so + kStageOut), col, row0, policy);
+        if (save_da) tma_store_2d(map_da, smem_addr(st), col, row0, policy);
         bulk_commit();
       }
+      ++C;
     }
     if (!ok) break;
-    g += nl;
     tc_fence_before();
     __syncwarp();
     // Release this accumulator buffer to the MMA issuer (on the even CTA of a pair).
@@ -498,8 +514,8 @@ __device__ __forceinline__ void bwd_epilogue(GemmBarriers* bars, unsigned char* 
   if (!ok) {
     record_gemm_error();
     // Loads still in flight must land before this CTA's shared memory is released.
-    if (pending_mask & 1u) wait_bounded(&bars->epi_full[wi][0], (pending_gc0 >> 1) & 1);
-    if (pending_mask & 2u) wait_bounded(&bars->epi_full[wi][1], (pending_gc1 >> 1) & 1);
+    for (uint32_t c = C; c < L; ++c)
+      wait_bounded(&bars->epi_full[wi][c % kEpiInBufs], (c / kEpiInBufs) & 1);
   }
   // The staging tiles must stay valid until this warp's last TMA stores have completed.
   if (lane == 0) bulk_wait_all();
@@ -549,7 +565,7 @@ __device__ __forceinline__ void swiglu_gemm_body(const CUtensorMap* map_x,
     }
     mbar_init(&bars->drain, 1);
     for (int w = 0; w < kEpiWarps; ++w)
-      for (int b = 0; b < kEpiBufs; ++b) mbar_init(&bars->epi_full[w][b], 1);
+      for (int b = 0; b < kEpiInBufs; ++b) mbar_init(&bars->epi_full[w][b], 1);
     fence_mbar_init();
   }
   if (warp == 2) tmem_alloc<kPair>(&bars->tmem_base);
