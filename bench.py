@@ -502,11 +502,13 @@ class Stack:
         self.dout = torch.randn((layers, tokens, INTER), generator=gen, device=device, dtype=bf)
         self.w = 1 + 0.02 * torch.randn((layers, 2, HIDDEN), generator=gen, device=device)
         # outputs are write-only here; their consumers (GEMMs) are outside this path
-        self.y = torch.empty((tokens, HIDDEN), device=device, dtype=bf)
-        self.dx = torch.empty((tokens, HIDDEN), device=device, dtype=bf)
-        self.act = torch.empty((tokens, INTER), device=device, dtype=bf)
-        self.dg = torch.empty((tokens, INTER), device=device, dtype=bf)
-        self.du = torch.empty((tokens, INTER), device=device, dtype=bf)
+        # Two buffers per output, alternated by layer (dx by norm): consecutive kernels never
+        # write the same addresses, so no kernel's stores can merge in L2 with the last one's.
+        self.y = [torch.empty((tokens, HIDDEN), device=device, dtype=bf) for _ in range(2)]
+        self.dx = [torch.empty((tokens, HIDDEN), device=device, dtype=bf) for _ in range(2)]
+        self.act = [torch.empty((tokens, INTER), device=device, dtype=bf) for _ in range(2)]
+        self.dg = [torch.empty((tokens, INTER), device=device, dtype=bf) for _ in range(2)]
+        self.du = [torch.empty((tokens, INTER), device=device, dtype=bf) for _ in range(2)]
         self.bucket = DWeightBucket([HIDDEN] * (2 * layers), device)
         self.num_partials = _capi.rmsnorm_bwd_num_partials(tokens, HIDDEN, _capi.PT_BFLOAT16,
                                                            _capi.PT_FLOAT32)
@@ -569,7 +571,8 @@ class Stack:
 
         lib, L, T = self.lib, self.layers, self.tokens
         f32, b16 = self.capi.PT_FLOAT32, self.capi.PT_BFLOAT16
-        y, act = self.y.data_ptr(), self.act.data_ptr()
+        y = [t.data_ptr() for t in self.y]
+        act = [t.data_ptr() for t in self.act]
         part, P = self.partials.data_ptr(), self.num_partials
         ws, ws_floats = self.workspace.data_ptr(), self.workspace.numel()
         out: dict = {}
@@ -580,25 +583,25 @@ class Stack:
         for l in range(L):
             for k in range(2):
                 add("rmsnorm_fwd", lambda l=l, k=k: lib.pt_rmsnorm_fwd(
-                    self.x[l, k].data_ptr(), HIDDEN, self.w[l, k].data_ptr(), y, HIDDEN, None,
+                    self.x[l, k].data_ptr(), HIDDEN, self.w[l, k].data_ptr(), y[k], HIDDEN, None,
                     T, HIDDEN, b16, f32, EPS, stream))
             add("swiglu_fwd", lambda l=l: lib.pt_swiglu_fwd(
-                self.gate[l].data_ptr(), self.up[l].data_ptr(), act, T * INTER, b16, stream))
+                self.gate[l].data_ptr(), self.up[l].data_ptr(), act[l % 2], T * INTER, b16, stream))
         for l in reversed(range(L)):
             add("swiglu_bwd", lambda l=l: lib.pt_swiglu_bwd(
                 self.dout[l].data_ptr(), self.gate[l].data_ptr(), self.up[l].data_ptr(),
-                self.dg.data_ptr(), self.du.data_ptr(), T * INTER, b16, stream))
+                self.dg[l % 2].data_ptr(), self.du[l % 2].data_ptr(), T * INTER, b16, stream))
             for k in (1, 0):
                 if self.fused_dw:
                     add("rmsnorm_bwd", lambda l=l, k=k: lib.pt_rmsnorm_bwd_fused(
                         self.dy[l, k].data_ptr(), HIDDEN, self.x[l, k].data_ptr(), HIDDEN,
-                        self.w[l, k].data_ptr(), None, self.dx.data_ptr(), HIDDEN,
+                        self.w[l, k].data_ptr(), None, self.dx[k].data_ptr(), HIDDEN,
                         self.bucket.slot(2 * l + k).data_ptr(), ws, ws_floats, T, HIDDEN, b16,
                         f32, EPS, stream))
                     continue
                 add("rmsnorm_bwd", lambda l=l, k=k: lib.pt_rmsnorm_bwd(
                     self.dy[l, k].data_ptr(), HIDDEN, self.x[l, k].data_ptr(), HIDDEN,
-                    self.w[l, k].data_ptr(), None, self.dx.data_ptr(), HIDDEN, part, P, T,
+                    self.w[l, k].data_ptr(), None, self.dx[k].data_ptr(), HIDDEN, part, P, T,
                     HIDDEN, b16, f32, EPS, stream))
                 add("rmsnorm_dw_reduce", lambda l=l, k=k: lib.pt_rmsnorm_dw_reduce(
                     part, P, HIDDEN, self.bucket.slot(2 * l + k).data_ptr(), f32, stream))
@@ -612,14 +615,15 @@ class Stack:
 
         lib, L, T = self.lib, self.layers, self.tokens
         f32, b16 = self.capi.PT_FLOAT32, self.capi.PT_BFLOAT16
-        y, act = self.y.data_ptr(), self.act.data_ptr()
+        y = [t.data_ptr() for t in self.y]
+        act = [t.data_ptr() for t in self.act]
         for l in range(L):
             for k in range(2):
                 self._launch("rmsnorm_fwd", timer, lambda: lib.pt_rmsnorm_fwd(
-                    self.x[l, k].data_ptr(), HIDDEN, self.w[l, k].data_ptr(), y, HIDDEN, None,
+                    self.x[l, k].data_ptr(), HIDDEN, self.w[l, k].data_ptr(), y[k], HIDDEN, None,
                     T, HIDDEN, b16, f32, EPS, stream))
             self._launch("swiglu_fwd", timer, lambda: lib.pt_swiglu_fwd(
-                self.gate[l].data_ptr(), self.up[l].data_ptr(), act, T * INTER, b16, stream))
+                self.gate[l].data_ptr(), self.up[l].data_ptr(), act[l % 2], T * INTER, b16, stream))
         part, P = self.partials.data_ptr(), self.num_partials
         ws, ws_floats = self.workspace.data_ptr(), self.workspace.numel()
         pending = []
@@ -630,20 +634,20 @@ class Stack:
                 start.record()
             self._launch("swiglu_bwd", timer, lambda: lib.pt_swiglu_bwd(
                 self.dout[l].data_ptr(), self.gate[l].data_ptr(), self.up[l].data_ptr(),
-                self.dg.data_ptr(), self.du.data_ptr(), T * INTER, b16, stream))
+                self.dg[l % 2].data_ptr(), self.du[l % 2].data_ptr(), T * INTER, b16, stream))
             if swiglu_bwd_events is not None:
                 end.record()
             for k in (1, 0):
                 if self.fused_dw:
                     self._launch("rmsnorm_bwd", timer, lambda: lib.pt_rmsnorm_bwd_fused(
                         self.dy[l, k].data_ptr(), HIDDEN, self.x[l, k].data_ptr(), HIDDEN,
-                        self.w[l, k].data_ptr(), None, self.dx.data_ptr(), HIDDEN,
+                        self.w[l, k].data_ptr(), None, self.dx[k].data_ptr(), HIDDEN,
                         self.bucket.slot(2 * l + k).data_ptr(), ws, ws_floats, T, HIDDEN, b16,
                         f32, EPS, stream))
                     continue
                 self._launch("rmsnorm_bwd", timer, lambda: lib.pt_rmsnorm_bwd(
                     self.dy[l, k].data_ptr(), HIDDEN, self.x[l, k].data_ptr(), HIDDEN,
-                    self.w[l, k].data_ptr(), None, self.dx.data_ptr(), HIDDEN, part, P, T,
+                    self.w[l, k].data_ptr(), None, self.dx[k].data_ptr(), HIDDEN, part, P, T,
                     HIDDEN, b16, f32, EPS, stream))
                 self._launch("rmsnorm_dw_reduce", timer, lambda: lib.pt_rmsnorm_dw_reduce(
                     part, P, HIDDEN, self.bucket.slot(2 * l + k).data_ptr(), f32, stream))
