@@ -273,6 +273,30 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
+// 1-D bulk copy of `bytes` from this CTA's shared memory to global memory (both addresses
+// 16-byte aligned, bytes a multiple of 16), tracked by this thread's bulk-group counter.
+__device__ __forceinline__ void bulk_store_row(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+               "r"(smem_addr(src)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until this thread's committed bulk stores have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_all_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Waits until this thread's committed bulk stores have completed.
+__device__ __forceinline__ void bulk_wait_all_done() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Orders this thread's earlier generic-proxy shared-memory writes before later async-proxy
+// (bulk copy) accesses to them.
+__device__ __forceinline__ void fence_async_proxy_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Potentially blocking test of phase `parity`: the thread may sleep until the phase
 // completes or about kSuspendHintNs nanoseconds pass (0: the hardware's default limit).
 #ifndef PT_SUSPEND_NS
