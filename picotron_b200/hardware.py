@@ -86,7 +86,8 @@ def probe_hot_path(device: int | torch.device | None = None, seed: int = 0) -> P
     errors: dict[str, float] = {}
 
     def rel(a: torch.Tensor, b: torch.Tensor) -> float:
-        return float((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-30))
+        a, b = a.detach().float(), b.detach().float()
+        return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
 
     hidden, inter, tokens = 64, 96, 48
     norm = RMSNorm(hidden, use_triton_rmsnorm=True).to(dev)
