@@ -1259,7 +1259,8 @@ def main() -> None:
         "weight_dtype": "float32",
         "nccl_stream": f"{args.nccl_stream} priority",
         "rmsnorm_backward": ("dweight reduced in the same launch" if args.rms_bwd == "fused"
-                             else "dweight reduced by a second kernel"),
+                             else "dweight reduced by a second kernel, launched as a "
+                                  "programmatic dependent of the backward"),
         "l2": "no flush: every layer has its own inputs, each larger than the 126 MB L2",
     }
 

@@ -77,6 +77,16 @@ __device__ __forceinline__ void st_stream(void* p, const uint4& v) {
                : "memory");
 }
 
+// One 32-byte store of eight floats (sm_100: a whole L2 sector per thread); p must be 32-byte
+// aligned.
+__device__ __forceinline__ void st_global_v8(float* p, const float (&v)[8]) {
+  asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};"
+               :
+               : "l"(p), "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]),
+                 "f"(v[6]), "f"(v[7])
+               : "memory");
+}
+
 // Unpack a 16-byte vector of T into fp32 values.
 template <typename T> __device__ __forceinline__ void unpack(const uint4& v, float* f);
 

@@ -637,10 +637,42 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
     // `partials_lo`, or, without a lo row, their fp32-rounded total.
     float* prow = partials + (int64_t)blockIdx.x * hidden;
     float* lrow = partials_lo != nullptr ? partials_lo + (int64_t)blockIdx.x * hidden : nullptr;
+    // 16-bit rows give each thread eight consecutive columns per vector: with 32-byte aligned
+    // partial rows each thread stores them as whole 32-byte sectors (the float4 pairs below
+    // leave every sector half-written by each of two store instructions).
+    const bool whole_sectors =
+        V == 8 && (reinterpret_cast<uintptr_t>(prow) & 31) == 0 &&
+        (lrow == nullptr || (reinterpret_cast<uintptr_t>(lrow) & 31) == 0) &&
+        (zero_row == nullptr || (reinterpret_cast<uintptr_t>(zero_row) & 31) == 0);
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       if (!valid[k]) continue;
       const int64_t col = (int64_t)(lane + 32 * (warp + C * k)) * V;
+      if constexpr (V == 8) {
+        if (whole_sectors) {
+          float hi[8], lo[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const double a = acc[k][e];
+            hi[e] = (float)a;
+            lo[e] = (float)(a - (double)hi[e]);
+          }
+          if (lrow != nullptr) {
+            st_global_v8(prow + col, hi);
+            st_global_v8(lrow + col, lo);
+          } else {
+            float t[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) t[e] = __fadd_rn(hi[e], lo[e]);
+            st_global_v8(prow + col, t);
+          }
+          if (zero_row != nullptr && blockIdx.x == 0) {
+            const float z[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+            st_global_v8(zero_row + col, z);
+          }
+          continue;
+        }
+      }
       float4* dst = reinterpret_cast<float4*>(prow + col);
       float4* dlo = lrow != nullptr ? reinterpret_cast<float4*>(lrow + col) : nullptr;
       float4* dz = zero_row != nullptr && blockIdx.x == 0

@@ -13,6 +13,8 @@ import golden_io
 import gpu_utils as gu
 from oracle import picotron_oracle as po
 from oracle import tolerance
+from picotron_b200 import _capi
+from picotron_b200.ops import DTYPE_CODES
 
 pytestmark = pytest.mark.gpu
 
@@ -110,6 +112,32 @@ def test_any_partial_count_and_determinism(num_partials):
     assert torch.equal(dx1, dx2) and torch.equal(dw1, dw2)
     _, dwe = po.rms_norm_backward(x.cpu(), w.cpu(), dy.cpu(), 1e-5, "exact")
     tolerance.assert_close(dw1, dwe, f"dw P={num_partials}")
+
+
+@pytest.mark.parametrize("num_partials", [296, 297])  # with and without the zeroed odd row
+def test_partial_rows_any_16_byte_alignment(num_partials):
+    # 16-bit rows store their partial rows as whole 32-byte sectors when the buffer is 32-byte
+    # aligned and as 16-byte halves otherwise: same partial rows, same dx and dw.
+    x = gu.randn((1000, 4096), 15, torch.bfloat16)
+    w = gu.randn(4096, 16, torch.float32, 0.02, 1.0)
+    dy = gu.randn((1000, 4096), 17, torch.bfloat16)
+    xc, wc = DTYPE_CODES[torch.bfloat16], DTYPE_CODES[torch.float32]
+    out = []
+    for offset in (0, 4):  # floats: a 32-byte aligned buffer, then one 16 bytes past it
+        buf = torch.full((num_partials * 4096 + 8,), float("nan"), device=gu.DEV)
+        part = buf[offset:offset + num_partials * 4096]
+        dx = torch.empty_like(x)
+        dw = torch.empty(4096, device=gu.DEV)
+        _capi.rmsnorm_bwd(dy.data_ptr(), 4096, x.data_ptr(), 4096, w.data_ptr(), None,
+                          dx.data_ptr(), 4096, part.data_ptr(), num_partials, 1000, 4096, xc, wc,
+                          1e-5, gu.stream())
+        _capi.rmsnorm_dw_reduce(part.data_ptr(), num_partials, 4096, dw.data_ptr(), wc,
+                                gu.stream())
+        torch.cuda.synchronize()
+        out.append((dx, dw, part.clone()))
+    assert torch.isfinite(out[0][2]).all() and torch.isfinite(out[1][2]).all()
+    for a, b in zip(out[0], out[1]):
+        assert torch.equal(a, b)
 
 
 def test_zero_rows_backward_gives_zero_dweight():
