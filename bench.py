@@ -533,7 +533,7 @@ class Stack:
         # the all-reduces: the collective time the backward did not hide.
         self.wait_events: list | None = None
         self.events_per_step = layers  # one (start, end) pair per SwiGLU backward launch
-        self.dominant = ("swiglu_bwd_vec (SwiGLU backward)", 5 * tokens * INTER * BF16)
+        self.dominant = ("swiglu_bwd_vec32 (SwiGLU backward)", 5 * tokens * INTER * BF16)
         self.traffic_key = "swiglu_bwd"
         t = tokens
         # Algorithmic bytes of one launch of each kernel of the step (inputs read once,
@@ -797,7 +797,7 @@ class OpWorkload:
             self.dg, self.du = torch.empty_like(self.out), torch.empty_like(self.out)
             self.bytes = 8 * tokens * INTER * BF16
             self.launches_per_step = 2
-            self.dominant = ("swiglu_bwd_vec", 5 * tokens * INTER * BF16)
+            self.dominant = ("swiglu_bwd_vec32", 5 * tokens * INTER * BF16)
         elif op in ("rope", "rope_rh"):
             op_name = op
             # rope: the reference's interleaved pairs; rope_rh: the rotate-half pairing that

@@ -77,6 +77,27 @@ __device__ __forceinline__ void st_stream(void* p, const uint4& v) {
                : "memory");
 }
 
+// 32-byte streaming load / store (two 16-byte vectors in one instruction, sm_100); p must be
+// 32-byte aligned.
+struct Vec32B {
+  uint4 lo, hi;
+};
+__device__ __forceinline__ Vec32B ld_stream32(const void* p) {
+  Vec32B r;
+  asm("ld.global.nc.L1::no_allocate.v8.u32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+      : "=r"(r.lo.x), "=r"(r.lo.y), "=r"(r.lo.z), "=r"(r.lo.w), "=r"(r.hi.x), "=r"(r.hi.y),
+        "=r"(r.hi.z), "=r"(r.hi.w)
+      : "l"(p));
+  return r;
+}
+__device__ __forceinline__ void st_stream32(void* p, const uint4& lo, const uint4& hi) {
+  asm volatile("st.global.cs.v8.u32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};"
+               :
+               : "l"(p), "r"(lo.x), "r"(lo.y), "r"(lo.z), "r"(lo.w), "r"(hi.x), "r"(hi.y),
+                 "r"(hi.z), "r"(hi.w)
+               : "memory");
+}
+
 // One 32-byte store of eight floats (sm_100: a whole L2 sector per thread); p must be 32-byte
 // aligned.
 __device__ __forceinline__ void st_global_v8(float* p, const float (&v)[8]) {

@@ -59,6 +59,27 @@ def test_misaligned_pointers_take_the_scalar_path():
     _check(g, u, dy, "misaligned")
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16],
+                         ids=lambda d: str(d).split(".")[-1])
+def test_32_and_16_byte_vector_paths_agree(dtype):
+    # 32-byte aligned arrays take the 32-byte vector kernels, arrays 16 bytes off it the
+    # 16-byte ones; both give the same bits, tails included.
+    n = 65_543
+    dy, g, u = (gu.randn(n, seed, dtype, 2.0) for seed in (6, 7, 8))
+    outs = []
+    for off_bytes in (0, 16):
+        off = off_bytes // dy.element_size()
+        placed = []
+        for t in (dy, g, u):  # the same values, starting off_bytes past a 256-byte boundary
+            buf = torch.empty(n + 64, dtype=dtype, device=gu.DEV)
+            buf[off:off + n].copy_(t)
+            placed.append(buf[off:off + n])
+        outs.append((gu.swiglu_fwd(placed[1], placed[2]),) + gu.swiglu_bwd(*placed))
+    torch.cuda.synchronize()
+    assert all(torch.equal(a, b) for a, b in zip(outs[0], outs[1]))
+    _check(g, u, dy, f"32-byte path {dtype}")
+
+
 def test_saturated_and_special_values():
     vals = torch.tensor([0.0, -0.0, 1.0, -1.0, 20.0, -20.0, 88.0, -88.0, 100.0, -100.0, 3e4,
                          -3e4, -1.2785, 1e-20, -1e-20, 5.0, -5.0, 0.5], dtype=torch.float32)
