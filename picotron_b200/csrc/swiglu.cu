@@ -104,8 +104,8 @@ swiglu_bwd_vec(const T* __restrict__ dout, const T* __restrict__ g, const T* __r
 // instruction): the paths for 32-byte aligned arrays. A/B of builds on B200 at config 3 inside
 // the config-5 step, where each SwiGLU kernel follows RMSNorm kernels: the 32-byte loads make
 // the backward 5 % faster there (361 against 379 us per launch; 32-byte stores alone changed
-// nothing) and the step 2 % shorter (27.09 against 27.73 ms), while back to back on their own
-// both kernels are within 1-3 % of the 16-byte ones (slower, in that setting).
+// nothing) and the step 2 % shorter (27.01 against 27.64 ms, same box), while back to back on
+// their own both kernels are within 1-3 % of the 16-byte ones (slower, in that setting).
 template <typename T, int U>
 __global__ void __launch_bounds__(kThreadsFwd)
 swiglu_fwd_vec32(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__ out,
