@@ -1315,8 +1315,10 @@ def main() -> None:
     E = work.events_per_step
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(E * args.steps)]
+    # The GPUs this job runs on (local rank r uses device r): idle GPUs of a larger box must
+    # not enter the clock record.
     uuids = []
-    for i in range(torch.cuda.device_count()):
+    for i in range(min(world, torch.cuda.device_count())):
         try:
             uuids.append(str(torch.cuda.get_device_properties(i).uuid))
         except Exception:
