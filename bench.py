@@ -36,6 +36,7 @@ from __future__ import annotations
 import argparse
 import datetime
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -1194,8 +1195,9 @@ def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None,
-                    help="timed steps (default 30; 300 for mlpup / mlpact, whose steps of a few "
-                         "ms would otherwise end before the clock sampler's first sample)")
+                    help="timed steps (default: 30 for the stack, 300 for mlpup / mlpact, and "
+                         "for the other per-op workloads as many as fill about 0.6 s, so that "
+                         "the clock sampler sees the timed region)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=32)
@@ -1224,6 +1226,7 @@ def main() -> None:
                          "ce = cross-entropy forward + backward over a 128256 vocabulary; "
                          "adamw = one fused AdamW step over 4 Llama-3-8B layers of parameters")
     args = ap.parse_args()
+    auto_steps = args.steps is None
     if args.steps is None:
         args.steps = 300 if args.workload in ("mlpup", "mlpact") else 30
     _claim_stdout()
@@ -1311,6 +1314,16 @@ def main() -> None:
     for _ in range(args.warmup):
         work.step(stream, world)
     torch.cuda.synchronize()
+    if auto_steps and world == 1 and args.workload not in ("stack", "mlpup", "mlpact"):
+        # Per-op workloads take well under a millisecond per step: without --steps, time as
+        # many as fill about 0.6 s, so that the clock sampler sees the timed region.
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(3):
+            work.step(stream, world)
+        b.record()
+        torch.cuda.synchronize()
+        args.steps = max(args.steps, int(math.ceil(600.0 / max(a.elapsed_time(b) / 3, 1e-3))))
 
     E = work.events_per_step
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))

@@ -98,6 +98,23 @@ __device__ __forceinline__ void st_stream32(void* p, const uint4& lo, const uint
                : "memory");
 }
 
+// 32-byte loads of eight floats (sm_100); p must be 32-byte aligned. The _cs form streams
+// (evict-first) data read once.
+__device__ __forceinline__ void ld_global_v8(const float* p, float (&v)[8]) {
+  asm volatile("ld.global.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]),
+                 "=f"(v[6]), "=f"(v[7])
+               : "l"(p)
+               : "memory");
+}
+__device__ __forceinline__ void ld_global_cs_v8(const float* p, float (&v)[8]) {
+  asm volatile("ld.global.cs.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]),
+                 "=f"(v[6]), "=f"(v[7])
+               : "l"(p)
+               : "memory");
+}
+
 // One 32-byte store of eight floats (sm_100: a whole L2 sector per thread); p must be 32-byte
 // aligned.
 __device__ __forceinline__ void st_global_v8(float* p, const float (&v)[8]) {
