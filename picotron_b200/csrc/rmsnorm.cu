@@ -320,10 +320,12 @@ rmsnorm_ws(const T* __restrict__ x, int64_t xs, const T* __restrict__ dy, int64_
     }
     fence_mbar_init();
   }
-  // The backward is launched as a programmatic dependent of the stream's previous kernel
-  // (ws_launch): its CTAs may take their SMs while that kernel finishes, and wait here,
-  // before their first global memory access, until it has completed.
-  if constexpr (kBwd && !kFused) asm volatile("griddepcontrol.wait;" ::: "memory");
+  // Launched as a programmatic dependent of the stream's previous kernel (ws_launch; not the
+  // cooperative fused backward): the CTAs may take their SMs while that kernel finishes, and
+  // wait here, before their first global memory access, until it has completed. The forward
+  // lets the next kernel be scheduled from here on (the backward does so below).
+  if constexpr (!kFused) asm volatile("griddepcontrol.wait;" ::: "memory");
+  if constexpr (!kBwd) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __syncthreads();
   // The producer starts filling the ring at once; the reducer and owner warps stage the
   // backward's weight meanwhile and meet at named barrier 1 (A/B on B200: 1 us less per
@@ -1041,9 +1043,10 @@ cudaError_t ws_launch(const FastPlan& plan, int grid, cudaStream_t stream, const
   cfg.blockDim = dim3((unsigned)ws_threads(plan));
   cfg.dynamicSmemBytes = (size_t)ws_smem(plan, kFused);
   cfg.stream = stream;
-  // The fused backward needs all CTAs resident (cooperative); the two-launch backward is a
-  // programmatic dependent of the previous kernel (A/B on B200 at 16384 x 4096 bf16: 68.4
-  // against 70.8 us back to back, 0.90 of the HBM peak; same bits).
+  // The fused backward needs all CTAs resident (cooperative); the forward and the two-launch
+  // backward are programmatic dependents of the previous kernel (A/B on B200 at 16384 x 4096
+  // bf16, back to back: backward 68.4 against 70.8 us, forward 44.1 against 46.0 us; the
+  // config-5 step 0.5 % shorter; same bits).
   cudaLaunchAttribute attr[1];
   if (kFused) {
     attr[0].id = cudaLaunchAttributeCooperative;
@@ -1053,7 +1056,7 @@ cudaError_t ws_launch(const FastPlan& plan, int grid, cudaStream_t stream, const
     attr[0].val.programmaticStreamSerializationAllowed = 1;
   }
   cfg.attrs = attr;
-  cfg.numAttrs = (kFused || kBwd) ? 1 : 0;
+  cfg.numAttrs = 1;
 #define PT_WS_ARGS                                                                         \
   x, xs, dy, dys, w, rstd_in, out, os, rstd_out, partials, partials_lo, zero_row, aux, as,  \
       h_out, hs, rows, plan.nvec, hidden, plan.stages, plan.consumers, plan.reducers, hf, eps, \
