@@ -52,6 +52,11 @@ if int(os.environ.get("WORLD_SIZE", "1")) > 1:
         os.environ["NCCL_DEBUG"] = "INFO"
     os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
     os.environ["NCCL_DEBUG_FILE"] = f"/tmp/pt_nccl_{os.getpid()}.log"
+    # The dweight all-reduces are 32-256 KB, latency-bound, and overlap kernels that fill
+    # every SM: without NVLink SHARP (NVLS) their exposed wait stayed at 47-147 us per step in
+    # 4 of 4 two-GPU runs, while with it about one run in three waited 1.6-2.4 ms per step
+    # throughout (B200, same box and build). The environment can still turn it back on.
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
 
 import torch
 
@@ -1261,6 +1266,7 @@ def main() -> None:
         "eps": EPS,
         "weight_dtype": "float32",
         "nccl_stream": f"{args.nccl_stream} priority",
+        "nccl_nvls": os.environ.get("NCCL_NVLS_ENABLE", "default") if args.gpus > 1 else None,
         "rmsnorm_backward": ("dweight reduced in the same launch" if args.rms_bwd == "fused"
                              else "dweight reduced by a second kernel, launched as a "
                                   "programmatic dependent of the backward"),

@@ -27,7 +27,10 @@ def nccl_options():
     sized to the SMs), so on a normal-priority stream NCCL's all-reduce kernels wait for free
     SMs behind the compute stream's queued kernels and run only after the backward's last
     kernel; with high priority their CTAs are dispatched first as SMs free up.
-    Pass as ``dist.init_process_group("nccl", pg_options=nccl_options(), ...)``."""
+    Pass as ``dist.init_process_group("nccl", pg_options=nccl_options(), ...)``. For these
+    small (32-256 KB), latency-bound all-reduces also set ``NCCL_NVLS_ENABLE=0`` before NCCL
+    loads: on B200 with NVLink SHARP enabled about one two-GPU run in three left 1.6-2.4 ms
+    of all-reduce exposed at the end of every step, without it none of four did."""
 
     return dist.ProcessGroupNCCL.Options(is_high_priority_stream=True)
 
