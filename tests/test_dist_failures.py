@@ -20,7 +20,6 @@ import os
 import socket
 import time
 
-import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 

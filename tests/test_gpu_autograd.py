@@ -12,7 +12,7 @@ import gpu_utils as gu
 import picotron_b200 as pb
 from oracle import picotron_oracle as po
 from oracle import tolerance
-from picotron_b200 import _capi, ops
+from picotron_b200 import _capi
 from picotron_b200.errors import TritonRMSNormUnavailable, TritonSwiGLUUnavailable
 from picotron_b200.modules import RMSNorm, RotaryEmbedding, SwiGLU
 

@@ -13,7 +13,6 @@ from torch.nn import functional as F
 
 import golden_io
 import gpu_utils as gu
-import picotron_b200 as pb
 from oracle import picotron_oracle as po
 from oracle import tolerance
 from picotron_b200 import _capi
