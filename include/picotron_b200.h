@@ -16,6 +16,11 @@
  *   - the device scratch array of pt_rmsnorm_bwd_noalloc (see there), shared by all its
  *     calls on a device.
  *
+ * Work is ordered on the given stream as for any launch. The RMSNorm kernels and the dweight
+ * reduce are launched as programmatic dependents of the stream's previous kernel: their CTAs
+ * may start while that kernel finishes and wait, before touching global memory, for it to
+ * complete, so the ordering seen by the caller is unchanged (also inside CUDA graphs).
+ *
  * Every function returns a pt_status. On failure nothing has been launched and
  * pt_last_error() describes the cause on the calling thread. All pointers must be
  * device (or managed) memory of the CUDA device that is current on the calling thread;
