@@ -534,7 +534,7 @@ class Stack:
         # each, except that layer 0 forms its own bucket (2 norms, 32 KB). The backward runs
         # from the last layer down, so each bucket's all-reduce overlaps the backward of the
         # layers below it; only layer 0's small one is left at the end of the step.
-        self.bucket_starts = sorted({0, 1} | set(range(0, layers, 8)) - {layers})
+        self.bucket_starts = sorted(s for s in {0, 1} | set(range(0, layers, 8)) if s < layers)
         # When a list, each step appends the (start, end) events around its final waits for
         # the all-reduces: the collective time the backward did not hide.
         self.wait_events: list | None = None
